@@ -1,0 +1,196 @@
+// b2g_host.cpp -- host-only part of libb200gemm.so: error reporting, device facts, the
+// cuBLAS comparison column, the host input generators and the tile-scheduler mapping.
+#include <cublas_v2.h>
+#include <cuda_runtime.h>
+#include <omp.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "b2g.h"
+#include "b2g_internal.h"
+#include "tile_sched.h"
+
+namespace b2g {
+
+namespace {
+thread_local std::string t_last_error;
+std::mutex g_mu;
+unsigned long long g_timeout_us = 0;  // 0 = not initialised yet
+DeviceInfo g_dev[64];
+}  // namespace
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+void clear_error() { t_last_error.clear(); }
+
+unsigned long long wait_timeout_ns() {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_timeout_us == 0) {
+        g_timeout_us = 4000000ull;
+        if (const char* e = std::getenv("B2G_WAIT_TIMEOUT_US")) {
+            const unsigned long long v = std::strtoull(e, nullptr, 10);
+            if (v > 0) g_timeout_us = v;
+        }
+    }
+    return g_timeout_us * 1000ull;
+}
+
+int current_device(DeviceInfo& out) {
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0)
+        return fail(B2G_ERR_NO_DEVICE, "no CUDA device: %s", cudaGetErrorString(e));
+    if (dev < 64) {
+        std::lock_guard<std::mutex> lock(g_mu);
+        if (g_dev[dev].device == dev) {
+            out = g_dev[dev];
+            return B2G_OK;
+        }
+    }
+    DeviceInfo di;
+    di.device = dev;
+    cudaDeviceGetAttribute(&di.major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&di.minor, cudaDevAttrComputeCapabilityMinor, dev);
+    cudaDeviceGetAttribute(&di.sm_count, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&di.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (di.major != 10 || di.minor != 0)
+        return fail(B2G_ERR_NO_DEVICE,
+                    "device %d is sm_%d%d; this library is built for sm_100a (B200) only", dev,
+                    di.major, di.minor);
+    if (dev < 64) {
+        std::lock_guard<std::mutex> lock(g_mu);
+        g_dev[dev] = di;
+    }
+    out = di;
+    return B2G_OK;
+}
+
+namespace {
+
+uint64_t mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// IEEE binary32 -> binary16, round to nearest even (what __float2half does on the host).
+uint16_t f32_to_f16(float f) {
+    uint32_t x;
+    std::memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u) return (uint16_t)(sign | 0x7C00u | (ax > 0x7F800000u ? 0x200u : 0u));
+    if (ax >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u);
+    if (ax >= 0x38800000u) {
+        uint32_t h = ((((ax >> 23) - 112u) << 10) | ((ax & 0x7FFFFFu) >> 13));
+        const uint32_t rem = ax & 0x1FFFu;
+        if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) ++h;
+        return (uint16_t)(sign | h);
+    }
+    const uint32_t e = ax >> 23;
+    if (e == 0) return (uint16_t)sign;
+    const uint32_t m = (ax & 0x7FFFFFu) | 0x800000u;
+    const int shift = 126 - (int)e;
+    if (shift >= 32) return (uint16_t)sign;
+    uint32_t h = m >> shift;
+    const uint32_t rem = m & ((1u << shift) - 1u), half = 1u << (shift - 1);
+    if (rem > half || (rem == half && (h & 1u))) ++h;
+    return (uint16_t)(sign | h);
+}
+
+struct CublasSlot {
+    int device = -1;
+    cublasHandle_t h = nullptr;
+};
+thread_local CublasSlot t_cublas[64];
+
+}  // namespace
+}  // namespace b2g
+
+using namespace b2g;
+
+B2G_EXPORT const char* b2g_last_error(void) { return t_last_error.c_str(); }
+
+B2G_EXPORT unsigned long long b2g_set_wait_timeout_us(unsigned long long us) {
+    const unsigned long long prev = wait_timeout_ns() / 1000ull;
+    if (us > 0) {
+        std::lock_guard<std::mutex> lock(g_mu);
+        g_timeout_us = us;
+    }
+    return prev;
+}
+
+B2G_EXPORT int b2g_version(void) { return 100; }  // 0.1.0
+
+B2G_EXPORT void b2g_tile_coord(int linear, int tiles_m, int tiles_n, int group, int* m_tile,
+                               int* n_tile) {
+    int m = 0, n = 0;
+    tile_coord(linear, tiles_m, tiles_n, group, m, n);
+    if (m_tile) *m_tile = m;
+    if (n_tile) *n_tile = n;
+}
+
+// The reference's init (src/gemm_bench.cu:760-765), bit for bit.
+B2G_EXPORT void b2g_fill_lcg_f16(uint16_t* A, long long nA, uint16_t* B, long long nB,
+                                 uint16_t* bias, long long nbias) {
+    uint32_t s = 12345u;
+    auto rnd = [&] {
+        s = s * 1664525u + 1013904223u;
+        return (float)((s >> 16) & 1023u) / 1023.f - 0.5f;
+    };
+    for (long long i = 0; i < nA; ++i) A[i] = f32_to_f16(rnd());
+    for (long long i = 0; i < nB; ++i) B[i] = f32_to_f16(rnd());
+    for (long long i = 0; i < nbias; ++i) bias[i] = f32_to_f16(rnd());
+}
+
+B2G_EXPORT void b2g_fill_uniform_f16(uint16_t* dst, long long n, long long first,
+                                     uint64_t seed, uint32_t tensor_id, double lo, double hi) {
+    const uint64_t key =
+        mix64(seed * 0x9E3779B97F4A7C15ull ^ ((uint64_t)tensor_id + 1ull) * 0xD1B54A32D192ED03ull);
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < n; ++i) {
+        const uint64_t h = mix64(key + (uint64_t)(first + i) * 0x9E3779B97F4A7C15ull);
+        const double u = (double)(h >> 40) * (1.0 / 16777216.0);
+        const double v = lo + (hi - lo) * u;
+        dst[i] = f32_to_f16((float)v);
+    }
+}
+
+// The reference's cuBLAS speed-of-light call (src/gemm_bench.cu:621-633): row-major
+// D(M x N) = A(M x K) * B(N x K)^T computed as column-major D^T = B^T * A^T.
+B2G_EXPORT int b2g_cublas_gemm(const void* A, const void* B, void* D, int M, int N, int K,
+                               void* stream) {
+    clear_error();
+    if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_ARG, "negative shape");
+    if (M == 0 || N == 0) return B2G_OK;
+    DeviceInfo di;
+    if (int rc = current_device(di)) return rc;
+    CublasSlot& slot = t_cublas[di.device & 63];
+    if (slot.device != di.device || !slot.h) {
+        cublasHandle_t h = nullptr;
+        if (cublasCreate(&h) != CUBLAS_STATUS_SUCCESS)
+            return fail(B2G_ERR_LIBRARY, "cublasCreate failed");
+        cublasSetMathMode(h, CUBLAS_TENSOR_OP_MATH);
+        slot.device = di.device;
+        slot.h = h;
+    }
+    cublasSetStream(slot.h, (cudaStream_t)stream);
+    const float alpha = 1.f, beta = 0.f;
+    cublasStatus_t st = cublasGemmEx(slot.h, CUBLAS_OP_T, CUBLAS_OP_N, N, M, K, &alpha, B,
+                                      CUDA_R_16F, K, A, CUDA_R_16F, K, &beta, D, CUDA_R_16F, N,
+                                      CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT_TENSOR_OP);
+    if (st != CUBLAS_STATUS_SUCCESS) return fail(B2G_ERR_LIBRARY, "cublasGemmEx: status %d", (int)st);
+    return B2G_OK;
+}

@@ -1,0 +1,29 @@
+// b2g_internal.h -- state shared by the device translation unit (b2g_kernels.cu) and the
+// host-only one (b2g_host.cpp): error reporting, the wait limit, per-device facts.
+#pragma once
+
+#include <cstdarg>
+#include <cstdint>
+
+#define B2G_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace b2g {
+
+// Records a formatted message as this thread's last error and returns `code`.
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+void clear_error();
+
+// Device-side wait limit in nanoseconds (b2g_set_wait_timeout_us / B2G_WAIT_TIMEOUT_US).
+unsigned long long wait_timeout_ns();
+
+struct DeviceInfo {
+    int device = -1;
+    int major = 0, minor = 0;
+    int sm_count = 0;
+    int smem_optin = 0;  // max dynamic shared memory per block (opt-in)
+};
+
+// Facts about the current device, cached. Returns B2G_OK or an error (with message).
+int current_device(DeviceInfo& out);
+
+}  // namespace b2g

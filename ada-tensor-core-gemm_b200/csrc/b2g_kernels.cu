@@ -1,0 +1,416 @@
+// b2g_kernels.cu -- the device translation unit of libb200gemm.so: every sm_100a kernel of
+// the library and the C-ABI entry points that launch them. (All device code lives in this
+// one translation unit so the per-device status word g_b2g_status is a single symbol.)
+//
+// Launch boundary: b2g_gemm replaces the reference's run_cfg + pick dispatch
+// (src/gemm_bench.cu:451-605): it validates the problem, builds the TMA tensor maps on the
+// host, picks the tile configuration and launches the persistent kernel asynchronously.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "b2g.h"
+#include "b2g_internal.h"
+#include "aux_sm100.cuh"
+#include "gemm_sm100.cuh"
+#include "probe_sm100.cuh"
+
+namespace b2g {
+namespace {
+
+// ---------------------------------------------------------------------------------------
+// TMA tensor maps
+// ---------------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// A 2-D FP16 tensor (outer x inner, inner contiguous, row pitch ld elements) read in boxes
+// of box_outer x box_inner with 128-byte swizzle (box_inner * 2 must be 128).
+int make_tmap(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld,
+              uint32_t box_inner, uint32_t box_outer, const char* what) {
+    auto enc = encode_fn();
+    if (!enc) return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {ld * 2};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(ptr), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled(%s: %llu x %llu, ld %llu) failed: %d",
+                    what, (unsigned long long)outer, (unsigned long long)inner,
+                    (unsigned long long)ld, (int)r);
+    return B2G_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// Per-device kernel set-up (opt-in shared memory), done once per kernel and device.
+// ---------------------------------------------------------------------------------------
+constexpr int kMaxDevices = 64;
+
+template <class K>
+int prepare_kernel(K kern, int device, size_t dyn_smem, bool (&done)[kMaxDevices],
+                   std::mutex& mu) {
+    std::lock_guard<std::mutex> lock(mu);
+    if (device >= 0 && device < kMaxDevices && done[device]) return B2G_OK;
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_smem);
+    if (e != cudaSuccess)
+        return fail(B2G_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem %zu): %s", dyn_smem,
+                    cudaGetErrorString(e));
+    if (device >= 0 && device < kMaxDevices) done[device] = true;
+    return B2G_OK;
+}
+
+struct TileDesc {
+    int bn;
+    size_t stage_bytes;
+};
+
+TileDesc tile_desc(int tile) {
+    switch (tile) {
+        case B2G_TILE_128x128: return {128, TileTraits<128>::kStageBytes};
+        case B2G_TILE_128x256: return {256, TileTraits<256>::kStageBytes};
+        default: return {0, 0};
+    }
+}
+
+size_t smem_for(int tile, int stages) {
+    return tile == B2G_TILE_128x128 ? gemm_smem_bytes<128>(stages) : gemm_smem_bytes<256>(stages);
+}
+
+int max_stages_for(int tile, int smem_optin) {
+    int s = kMaxStages;
+    while (s > 2 && smem_for(tile, s) > (size_t)smem_optin) --s;
+    return s;
+}
+
+template <int BN>
+int launch_gemm_1cta(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
+                     int grid, size_t smem, int device, cudaStream_t s) {
+    static bool done[kMaxDevices] = {};
+    static std::mutex mu;
+    DeviceInfo di;
+    if (int rc = current_device(di)) return rc;
+    const size_t max_dyn = (size_t)di.smem_optin;
+    if (int rc = prepare_kernel(gemm_sm100_1cta<BN>, device, max_dyn, done, mu)) return rc;
+    gemm_sm100_1cta<BN><<<grid, kThreads, smem, s>>>(tmA, tmB, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return fail(B2G_ERR_CUDA, "gemm_sm100_1cta<%d> launch (grid %d, smem %zu): %s", BN, grid,
+                    smem, cudaGetErrorString(e));
+    return B2G_OK;
+}
+
+int elementwise_grid(size_t n, int sm_count) {
+    const size_t blocks = (n + 255) / 256;
+    const size_t cap = (size_t)sm_count * 8;
+    return (int)std::max<size_t>(1, std::min(blocks, cap));
+}
+
+}  // namespace
+}  // namespace b2g
+
+using namespace b2g;
+
+// ---------------------------------------------------------------------------------------
+// GEMM
+// ---------------------------------------------------------------------------------------
+B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias, int M, int N,
+                        int K, long long lda, long long ldb, long long ldd, int b_layout,
+                        int acc, int epilogue, float alpha, int tile, int stages, int group,
+                        void* stream) {
+    clear_error();
+    if (M < 0 || N < 0 || K < 0)
+        return fail(B2G_ERR_ARG, "negative shape M=%d N=%d K=%d", M, N, K);
+    if (b_layout != B2G_B_NK && b_layout != B2G_B_KN)
+        return fail(B2G_ERR_ARG, "b_layout must be 0 (N x K) or 1 (K x N), got %d", b_layout);
+    if (acc != B2G_ACC_F32 && acc != B2G_ACC_F16)
+        return fail(B2G_ERR_ARG, "acc must be 0 (FP32) or 1 (FP16), got %d", acc);
+    if (epilogue != B2G_EPI_NONE && epilogue != B2G_EPI_BIAS_RELU)
+        return fail(B2G_ERR_ARG, "epilogue must be 0 (none) or 1 (bias+ReLU), got %d", epilogue);
+    if (tile != B2G_TILE_AUTO && tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 &&
+        tile != B2G_TILE_256x256_2SM)
+        return fail(B2G_ERR_ARG, "tile must be -1 (auto), 0, 1 or 2, got %d", tile);
+    if (stages != 0 && (stages < 2 || stages > kMaxStages))
+        return fail(B2G_ERR_ARG, "stages must be 0 (auto) or 2..%d, got %d", kMaxStages, stages);
+    if (group < 0) return fail(B2G_ERR_ARG, "group must be >= 0, got %d", group);
+    if (M == 0 || N == 0) return B2G_OK;
+    if (!D) return fail(B2G_ERR_ARG, "D is NULL");
+    if (ldd < N) return fail(B2G_ERR_ARG, "ldd (%lld) < N (%d)", ldd, N);
+    if (epilogue == B2G_EPI_NONE) bias = nullptr;
+
+    DeviceInfo di;
+    if (int rc = current_device(di)) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+
+    if (K == 0) {  // zero accumulator: only the epilogue remains
+        const size_t n = (size_t)M * N;
+        zero_k_fill_kernel<<<elementwise_grid(n, di.sm_count), 256, 0, s>>>(
+            (__half*)D, (const __half*)bias, M, N, ldd, epilogue);
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? B2G_OK
+                                : fail(B2G_ERR_CUDA, "K == 0 fill launch: %s", cudaGetErrorString(e));
+    }
+    if (!A || !B) return fail(B2G_ERR_ARG, "A or B is NULL");
+    const long long ldb_min = b_layout == B2G_B_NK ? K : N;
+    if (lda < K) return fail(B2G_ERR_ARG, "lda (%lld) < K (%d)", lda, K);
+    if (ldb < ldb_min) return fail(B2G_ERR_ARG, "ldb (%lld) < %s (%lld)", ldb,
+                                   b_layout == B2G_B_NK ? "K" : "N", ldb_min);
+    if (((uintptr_t)A & 15) || ((uintptr_t)B & 15))
+        return fail(B2G_ERR_ALIGN, "A and B must be 16-byte aligned (TMA)");
+    if ((lda % 8) || (ldb % 8))
+        return fail(B2G_ERR_ALIGN,
+                    "lda (%lld) and ldb (%lld) must be multiples of 8 elements: TMA row "
+                    "strides are multiples of 16 bytes (pad the leading dimension)",
+                    lda, ldb);
+    if (b_layout == B2G_B_KN)
+        return fail(B2G_ERR_UNSUPPORTED, "b_layout K x N is not built yet");
+
+    if (tile == B2G_TILE_AUTO) tile = N <= 128 ? B2G_TILE_128x128 : B2G_TILE_128x256;
+    if (tile == B2G_TILE_256x256_2SM)
+        return fail(B2G_ERR_UNSUPPORTED, "tile 2 (256x256 2-SM pair) is not built yet");
+    const TileDesc td = tile_desc(tile);
+    const int max_st = max_stages_for(tile, di.smem_optin);
+    if (stages == 0) stages = max_st;
+    const size_t smem = smem_for(tile, stages);
+    if (smem > (size_t)di.smem_optin)
+        return fail(B2G_ERR_SMEM, "smem over per-block opt-in limit: %zu > %d (tile %d, %d stages)",
+                    smem, di.smem_optin, tile, stages);
+
+    GemmParams p{};
+    p.M = M;
+    p.N = N;
+    p.K = K;
+    p.tiles_m = (M + kBM - 1) / kBM;
+    p.tiles_n = (N + td.bn - 1) / td.bn;
+    const long long nt = (long long)p.tiles_m * p.tiles_n;
+    if (nt > 0x7fffffffLL) return fail(B2G_ERR_ARG, "too many tiles (%lld)", nt);
+    p.num_tiles = (int)nt;
+    p.num_kb = (K + kBK - 1) / kBK;
+    p.group = group < 1 ? 1 : group;
+    p.stages = stages;
+    p.idesc = idesc_f16(kBM, td.bn, acc == B2G_ACC_F32, false);
+    p.acc_f16 = acc == B2G_ACC_F16;
+    p.epilogue = epilogue;
+    p.alpha = alpha;
+    p.bias = (const __half*)bias;
+    p.D = (__half*)D;
+    p.ldd = ldd;
+    p.d_vec = (((uintptr_t)D & 15) == 0) && (ldd % 8 == 0);
+    p.b_mn_major = 0;
+    p.timeout_ns = wait_timeout_ns();
+
+    CUtensorMap tmA, tmB;
+    if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK, kBM, "A"))
+        return rc;
+    if (int rc = make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, td.bn, "B"))
+        return rc;
+
+    const int grid = std::min(p.num_tiles, di.sm_count);
+    if (td.bn == 128) return launch_gemm_1cta<128>(tmA, tmB, p, grid, smem, di.device, s);
+    return launch_gemm_1cta<256>(tmA, tmB, p, grid, smem, di.device, s);
+}
+
+B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, int* smem_bytes,
+                               int* ctas_per_sm, int* tmem_cols, int* stages_used) {
+    clear_error();
+    if (tile == B2G_TILE_AUTO) tile = B2G_TILE_128x256;
+    if (tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256)
+        return fail(B2G_ERR_UNSUPPORTED, "tile %d is not built", tile);
+    DeviceInfo di;
+    if (int rc = current_device(di)) return rc;
+    if (stages == 0) stages = max_stages_for(tile, di.smem_optin);
+    if (stages < 2 || stages > kMaxStages)
+        return fail(B2G_ERR_ARG, "stages must be 2..%d", kMaxStages);
+    const size_t smem = smem_for(tile, stages);
+    cudaFuncAttributes fa{};
+    cudaError_t e = tile == B2G_TILE_128x128 ? cudaFuncGetAttributes(&fa, gemm_sm100_1cta<128>)
+                                             : cudaFuncGetAttributes(&fa, gemm_sm100_1cta<256>);
+    if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+    int occ = 0;
+    if (smem <= (size_t)di.smem_optin) {
+        if (tile == B2G_TILE_128x128) {
+            cudaFuncSetAttribute(gemm_sm100_1cta<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 di.smem_optin);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_sm100_1cta<128>, kThreads, smem);
+        } else {
+            cudaFuncSetAttribute(gemm_sm100_1cta<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 di.smem_optin);
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_sm100_1cta<256>, kThreads, smem);
+        }
+    }
+    if (threads) *threads = kThreads;
+    if (regs) *regs = fa.numRegs;
+    if (smem_bytes) *smem_bytes = (int)smem;
+    if (ctas_per_sm) *ctas_per_sm = occ;
+    if (tmem_cols) *tmem_cols = 2 * tile_desc(tile).bn;
+    if (stages_used) *stages_used = stages;
+    return smem <= (size_t)di.smem_optin
+               ? B2G_OK
+               : fail(B2G_ERR_SMEM, "smem over per-block opt-in limit: %zu > %d", smem, di.smem_optin);
+}
+
+// ---------------------------------------------------------------------------------------
+// Status word
+// ---------------------------------------------------------------------------------------
+B2G_EXPORT int b2g_sync_status(void* stream) {
+    clear_error();
+    cudaError_t e = cudaStreamSynchronize((cudaStream_t)stream);
+    if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "stream synchronize: %s", cudaGetErrorString(e));
+    unsigned int word = 0;
+    e = cudaMemcpyFromSymbol(&word, g_b2g_status, sizeof(word));
+    if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "read status word: %s", cudaGetErrorString(e));
+    if (word == 0) return B2G_OK;
+    const unsigned int zero = 0;
+    cudaMemcpyToSymbol(g_b2g_status, &zero, sizeof(zero));
+    return fail(B2G_ERR_TIMEOUT,
+                "device wait gave up (status 0x%x:%s%s%s%s%s%s); the kernel unwound and returned",
+                word, (word & kErrWaitProducer) ? " producer" : "", (word & kErrWaitMma) ? " mma" : "",
+                (word & kErrWaitEpilogue) ? " epilogue" : "",
+                (word & kErrWaitSelftest) ? " selftest" : "", (word & kErrWaitDrain) ? " drain" : "",
+                (word & kErrWaitProbe) ? " probe" : "");
+}
+
+B2G_EXPORT int b2g_selftest_wait_timeout(unsigned timeout_us, void* stream) {
+    clear_error();
+    if (timeout_us < 1 || timeout_us > 2000000)
+        return fail(B2G_ERR_ARG, "timeout_us must be 1..2000000, got %u", timeout_us);
+    DeviceInfo di;
+    if (int rc = current_device(di)) return rc;
+    selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(1000ull * timeout_us);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "selftest launch: %s", cudaGetErrorString(e));
+    return b2g_sync_status(stream);
+}
+
+// ---------------------------------------------------------------------------------------
+// Auxiliary kernels
+// ---------------------------------------------------------------------------------------
+B2G_EXPORT int b2g_max_rel_diff(const void* x, const void* y, size_t n, float* out_dev,
+                                void* stream) {
+    clear_error();
+    if (!out_dev || (n && (!x || !y))) return fail(B2G_ERR_ARG, "NULL pointer");
+    DeviceInfo di;
+    if (int rc = current_device(di)) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t e = cudaMemsetAsync(out_dev, 0, sizeof(float), s);
+    if (e == cudaSuccess && n) {
+        max_rel_diff_kernel<<<elementwise_grid(n, di.sm_count), 256, 0, s>>>(
+            (const __half*)x, (const __half*)y, n, out_dev);
+        e = cudaGetLastError();
+    }
+    return e == cudaSuccess ? B2G_OK : fail(B2G_ERR_CUDA, "max_rel_diff: %s", cudaGetErrorString(e));
+}
+
+B2G_EXPORT int b2g_bias_relu(void* D, const void* bias, int M, int N, long long ldd, float alpha,
+                             void* stream) {
+    clear_error();
+    if (M < 0 || N < 0 || ldd < N) return fail(B2G_ERR_ARG, "bad shape M=%d N=%d ldd=%lld", M, N, ldd);
+    if (M == 0 || N == 0) return B2G_OK;
+    if (!D) return fail(B2G_ERR_ARG, "D is NULL");
+    DeviceInfo di;
+    if (int rc = current_device(di)) return rc;
+    const size_t n = (size_t)M * N;
+    bias_relu_kernel<<<elementwise_grid(n, di.sm_count), 256, 0, (cudaStream_t)stream>>>(
+        (__half*)D, (const __half*)bias, M, N, ldd, alpha);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? B2G_OK : fail(B2G_ERR_CUDA, "bias_relu: %s", cudaGetErrorString(e));
+}
+
+B2G_EXPORT int b2g_probe_hbm(const void* src, void* dst, size_t bytes, int reps, void* stream,
+                             double* gbs) {
+    clear_error();
+    if (!src || !dst || !gbs || reps < 1 || bytes < 16 || (bytes & 15) ||
+        (((uintptr_t)src | (uintptr_t)dst) & 15))
+        return fail(B2G_ERR_ARG, "hbm probe needs 16-byte aligned buffers, bytes %% 16 == 0, reps >= 1");
+    DeviceInfo di;
+    if (int rc = current_device(di)) return rc;
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t n16 = bytes / 16;
+    const int grid = di.sm_count * 4;
+    for (int w = 0; w < 3; ++w)
+        hbm_copy_kernel<<<grid, 512, 0, s>>>((const uint4*)src, (uint4*)dst, n16);
+    cudaEvent_t t0, t1;
+    cudaEventCreate(&t0);
+    cudaEventCreate(&t1);
+    cudaEventRecord(t0, s);
+    for (int r = 0; r < reps; ++r)
+        hbm_copy_kernel<<<grid, 512, 0, s>>>((const uint4*)src, (uint4*)dst, n16);
+    cudaEventRecord(t1, s);
+    cudaError_t e = cudaEventSynchronize(t1);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, t0, t1);
+    cudaEventDestroy(t0);
+    cudaEventDestroy(t1);
+    if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "hbm probe: %s", cudaGetErrorString(e));
+    *gbs = 2.0 * (double)bytes * reps / (ms * 1e-3) / 1e9;  // each byte read once, written once
+    return B2G_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// tcgen05 issue-rate probe
+// ---------------------------------------------------------------------------------------
+B2G_EXPORT int b2g_probe_tcgen05(int kind, int cta_group, int n, int iters,
+                                 double* flop_per_clk_sm, long long* cycles_out) {
+    clear_error();
+    if (kind < 0 || kind > 3) return fail(B2G_ERR_ARG, "kind must be 0..3, got %d", kind);
+    if (cta_group != 1)
+        return fail(B2G_ERR_UNSUPPORTED, "cta_group %d probe is not built yet", cta_group);
+    if (n < 16 || n > 256 || n % 16) return fail(B2G_ERR_ARG, "n must be 16..256, step 16");
+    if (iters < 1 || iters > (1 << 24)) return fail(B2G_ERR_ARG, "iters must be 1..2^24");
+    DeviceInfo di;
+    if (int rc = current_device(di)) return rc;
+    const int blocks = di.sm_count;
+    long long* dcyc = nullptr;
+    cudaError_t e = cudaMalloc(&dcyc, sizeof(long long) * blocks);
+    if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "probe cudaMalloc: %s", cudaGetErrorString(e));
+    const uint32_t idesc = idesc_probe(kind, 128, n);
+    const unsigned long long tmo = wait_timeout_ns();
+    auto run = [&](auto kern) -> cudaError_t {
+        cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)kProbeSmem);
+        if (r != cudaSuccess) return r;
+        for (int w = 0; w < 3; ++w) kern<<<blocks, kProbeThreads, kProbeSmem>>>(idesc, iters, dcyc, tmo);
+        kern<<<blocks, kProbeThreads, kProbeSmem>>>(idesc, iters, dcyc, tmo);
+        return cudaDeviceSynchronize();
+    };
+    switch (kind) {
+        case kProbeF16F32: e = run(probe_tcgen05_kernel<kProbeF16F32>); break;
+        case kProbeF16F16: e = run(probe_tcgen05_kernel<kProbeF16F16>); break;
+        case kProbeI8: e = run(probe_tcgen05_kernel<kProbeI8>); break;
+        default: e = run(probe_tcgen05_kernel<kProbeE4M3>); break;
+    }
+    long long best = -1;
+    if (e == cudaSuccess) {
+        long long* h = new long long[blocks];
+        e = cudaMemcpy(h, dcyc, sizeof(long long) * blocks, cudaMemcpyDeviceToHost);
+        for (int b = 0; b < blocks && e == cudaSuccess; ++b)
+            if (h[b] > 0 && (best < 0 || h[b] < best)) best = h[b];  // least-perturbed SM
+        delete[] h;
+    }
+    cudaFree(dcyc);
+    if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "probe: %s", cudaGetErrorString(e));
+    if (int rc = b2g_sync_status(nullptr)) return rc;
+    if (best <= 0) return fail(B2G_ERR_TIMEOUT, "probe produced no timing");
+    const double flop = 2.0 * 128.0 * n * probe_mma_k(kind) * (double)iters;
+    if (flop_per_clk_sm) *flop_per_clk_sm = flop / (double)best;
+    if (cycles_out) *cycles_out = best;
+    return B2G_OK;
+}

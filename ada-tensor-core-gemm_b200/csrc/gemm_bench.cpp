@@ -1,0 +1,456 @@
+// gemm_bench.cpp -- command-line driver of the B200 GEMM, with the reference CLI's flags.
+//
+// Mirrors the reference's gemm_bench (src/gemm_bench.cu:698-868): same flags, same
+// defaults where they still mean something, same fail-fast behaviour (unknown flag ->
+// exit 2), the same whitespace-separated result table (column order is the contract that
+// scripts/sweep.ps1:33-51 parses; new columns are appended at the end), the same `SOAK,`
+// CSV lines, a cuBLAS comparison column, the device max-rel check (--check) and the FP64
+// host spot check (--cpu S). All GPU work goes through the library's C-ABI (b2g.h).
+//
+// Differences, all because the hardware path changed:
+//   --tile    selects B200 tiles: 0 = 128x128, 1 = 128x256 (default), 2 = 256x256 2-SM pair
+//   --layout  only 2 (swizzle) exists on sm_100a: TMA writes the 128-byte-swizzled layout
+//             tcgen05.mma reads; 0 / 1 print a SKIP row like an unsupported config
+//   --stages  shared-memory ring depth 2..8 (0 = deepest that fits); --sweep runs 2..8
+//   no K % 32 restriction (TMA zero-fills the K tail); A/B leading dimensions are padded
+//             to a multiple of 8 elements when K is not (16-byte TMA row strides)
+// New flags: --acc f32|f16, --fused, --b-layout nk|kn, --init ref|uniform, --seed S,
+//            --dist LO,HI, --frob ROWS, --json.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "b2g.h"
+
+#define CUDA_CHECK(x)                                                                   \
+    do {                                                                                \
+        cudaError_t e_ = (x);                                                           \
+        if (e_ != cudaSuccess) {                                                        \
+            fprintf(stderr, "CUDA error %s:%d: %s\n", __FILE__, __LINE__,               \
+                    cudaGetErrorString(e_));                                            \
+            exit(1);                                                                    \
+        }                                                                               \
+    } while (0)
+
+namespace {
+
+struct Args {
+    int M = 4096, N = 4096, K = 4096;
+    int tile = 1, stages = 0, layout = 2, group = 1;
+    int iters = 50, warmup = 20;
+    int cpu = 0;        // output elements verified by the FP64 host spot check
+    int frob = 0;       // rows of D checked by an FP64 relative Frobenius norm
+    double soak = 0;    // seconds of back-to-back launches (0 = fixed iters)
+    double window = 2.0;
+    bool check = false, ref = true, sweep = false, unfused = false, gsweep = false;
+    bool fused = false, json = false;
+    int acc = B2G_ACC_F32, b_layout = B2G_B_NK;
+    bool init_ref = true;
+    unsigned long long seed = 0;
+    double lo = -0.5, hi = 0.5;
+};
+
+float h2f(uint16_t h) {
+    uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 0x1Fu, m = h & 0x3FFu, x;
+    if (e == 0x1F) {
+        x = sign | 0x7F800000u | (m << 13);
+    } else if (e == 0) {
+        if (m == 0) {
+            x = sign;
+        } else {
+            int s = 0;
+            while (!(m & 0x400u)) { m <<= 1; ++s; }
+            x = sign | ((uint32_t)(113 - s) << 23) | ((m & 0x3FFu) << 13);
+        }
+    } else {
+        x = sign | ((e + 112u) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &x, 4);
+    return f;
+}
+
+double now_s() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+// FP64 spot check with the reference's semantics (src/gemm_bench.cu:666-696): `samples`
+// output elements at a fixed odd stride, FP64 dot products of the FP16 inputs, relative
+// error |got - ref| / max(1, |ref|), bias + ReLU applied when an epilogue ran.
+double spot_check(const std::vector<uint16_t>& A, long long lda, const std::vector<uint16_t>& B,
+                  long long ldb, int b_layout, const std::vector<uint16_t>& D, long long ldd,
+                  const std::vector<uint16_t>& bias, int M, int N, int K, int samples, bool epi,
+                  float alpha, int* wm, int* wn) {
+    double worst = 0.0;
+    *wm = *wn = -1;
+    const long long total = (long long)M * N;
+    const long long stride = (total / std::max(1, samples)) | 1;
+    long long idx = 0;
+    for (long long s = 0; s < samples && s < total; ++s, idx = (idx + stride) % total) {
+        const int m = (int)(idx / N), n = (int)(idx % N);
+        double acc = 0.0;
+        for (int k = 0; k < K; ++k) {
+            const uint16_t b = b_layout == B2G_B_NK ? B[(size_t)n * ldb + k] : B[(size_t)k * ldb + n];
+            acc += (double)h2f(A[(size_t)m * lda + k]) * (double)h2f(b);
+        }
+        if (epi) {
+            acc = acc * alpha + (double)h2f(bias[n]);
+            if (acc < 0) acc = 0;
+        }
+        const double got = (double)h2f(D[(size_t)m * ldd + n]);
+        const double rel = fabs(got - acc) / std::max(1.0, fabs(acc));
+        if (rel > worst) { worst = rel; *wm = m; *wn = n; }
+    }
+    return worst;
+}
+
+// Relative Frobenius error over `rows` rows spread evenly through D (FP64 reference).
+double frobenius_rows(const std::vector<uint16_t>& A, long long lda, const std::vector<uint16_t>& B,
+                      long long ldb, int b_layout, const std::vector<uint16_t>& D, long long ldd,
+                      const std::vector<uint16_t>& bias, int M, int N, int K, int rows, bool epi,
+                      float alpha) {
+    double num = 0, den = 0;
+    rows = std::min(rows, M);
+    std::vector<double> bcol((size_t)K);
+    std::vector<double> ref((size_t)N);
+    for (int r = 0; r < rows; ++r) {
+        const int m = (int)((long long)r * M / rows);
+        for (int n = 0; n < N; ++n) {
+            double acc = 0;
+            for (int k = 0; k < K; ++k) {
+                const uint16_t b = b_layout == B2G_B_NK ? B[(size_t)n * ldb + k] : B[(size_t)k * ldb + n];
+                acc += (double)h2f(A[(size_t)m * lda + k]) * (double)h2f(b);
+            }
+            if (epi) acc = std::max(0.0, acc * alpha + (double)h2f(bias[n]));
+            const double d = (double)h2f(D[(size_t)m * ldd + n]) - acc;
+            num += d * d;
+            den += acc * acc;
+        }
+    }
+    return den > 0 ? sqrt(num / den) : sqrt(num);
+}
+
+const char* tile_name(int t) {
+    return t == 0 ? "128x128x64" : t == 1 ? "128x256x64" : t == 2 ? "256x256x64" : "auto";
+}
+
+void usage(const char* argv0) {
+    printf("usage: %s [--m M --n N --k K] [--tile 0|1|2] [--stages 0|2..8]\n"
+           "       [--layout 2] [--group G] [--iters N] [--warmup N] [--check] [--cpu S]\n"
+           "       [--noref] [--sweep] [--gsweep] [--unfused] [--soak SEC] [--window SEC]\n"
+           "       [--acc f32|f16] [--fused] [--b-layout nk|kn] [--init ref|uniform]\n"
+           "       [--seed S] [--dist LO,HI] [--frob ROWS] [--json]\n"
+           "  --check    compare against cuBLAS on the device (max |x-y|/max(1,|y|))\n"
+           "  --cpu S    verify S output elements against an FP64 host dot product\n"
+           "  --frob R   FP64 relative Frobenius error over R rows spread through D\n"
+           "  tile 0 = 128x128x64  1 CTA, UMMA 128x128, TMEM 2x128 cols\n"
+           "       1 = 128x256x64  1 CTA, UMMA 128x256, TMEM 2x256 cols (default)\n"
+           "       2 = 256x256x64  2-CTA pair (cta_group::2), UMMA 256x256\n"
+           "  --stages   shared-memory ring depth (0 = deepest that fits)\n"
+           "  --group G  L2 rasterization: G M-tiles walked column-major (1 = row-major)\n"
+           "  --sweep    stages 2..8 at fixed tile/group;  --gsweep  group 1,2,4,8,16\n"
+           "  --acc      f32 (default) or f16 accumulation; --fused alpha*acc+bias+ReLU\n"
+           "  --init     ref = the reference's LCG (default), uniform = seeded U[LO,HI]\n",
+           argv0);
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    Args a;
+    for (int i = 1; i < argc; ++i) {
+        auto eq = [&](const char* s) { return strcmp(argv[i], s) == 0; };
+        auto sval = [&]() -> const char* { return (i + 1 < argc) ? argv[++i] : ""; };
+        auto val = [&]() -> int { return atoi(sval()); };
+        auto dval = [&]() -> double { return atof(sval()); };
+        if (eq("--m")) a.M = val();
+        else if (eq("--n")) a.N = val();
+        else if (eq("--k")) a.K = val();
+        else if (eq("--tile")) a.tile = val();
+        else if (eq("--stages")) a.stages = val();
+        else if (eq("--layout")) a.layout = val();
+        else if (eq("--iters")) a.iters = val();
+        else if (eq("--warmup")) a.warmup = val();
+        else if (eq("--group")) a.group = val();
+        else if (eq("--cpu")) a.cpu = val();
+        else if (eq("--frob")) a.frob = val();
+        else if (eq("--soak")) a.soak = dval();
+        else if (eq("--window")) a.window = dval();
+        else if (eq("--check")) a.check = true;
+        else if (eq("--noref")) a.ref = false;
+        else if (eq("--sweep")) a.sweep = true;
+        else if (eq("--gsweep")) a.gsweep = true;
+        else if (eq("--unfused")) a.unfused = true;
+        else if (eq("--fused")) a.fused = true;
+        else if (eq("--json")) a.json = true;
+        else if (eq("--acc")) {
+            std::string v = sval();
+            if (v == "f32") a.acc = B2G_ACC_F32;
+            else if (v == "f16") a.acc = B2G_ACC_F16;
+            else { fprintf(stderr, "--acc must be f32 or f16\n"); return 2; }
+        } else if (eq("--b-layout")) {
+            std::string v = sval();
+            if (v == "nk") a.b_layout = B2G_B_NK;
+            else if (v == "kn") a.b_layout = B2G_B_KN;
+            else { fprintf(stderr, "--b-layout must be nk or kn\n"); return 2; }
+        } else if (eq("--init")) {
+            std::string v = sval();
+            if (v == "ref") a.init_ref = true;
+            else if (v == "uniform") a.init_ref = false;
+            else { fprintf(stderr, "--init must be ref or uniform\n"); return 2; }
+        } else if (eq("--seed")) a.seed = strtoull(sval(), nullptr, 10);
+        else if (eq("--dist")) {
+            if (sscanf(sval(), "%lf,%lf", &a.lo, &a.hi) != 2) {
+                fprintf(stderr, "--dist needs LO,HI\n");
+                return 2;
+            }
+        } else if (eq("--help")) {
+            usage(argv[0]);
+            return 0;
+        } else {
+            // silently ignoring an unrecognised flag once cost the reference a soak run
+            fprintf(stderr, "unknown option '%s' (try --help)\n", argv[i]);
+            return 2;
+        }
+    }
+    if (a.M < 0 || a.N < 0 || a.K < 0) { fprintf(stderr, "M, N, K must be >= 0\n"); return 1; }
+
+    int dev = 0;
+    CUDA_CHECK(cudaGetDevice(&dev));
+    cudaDeviceProp prop{};
+    CUDA_CHECK(cudaGetDeviceProperties(&prop, dev));
+
+    // leading dimensions: TMA wants 16-byte row strides for A and B
+    const long long lda = ((long long)a.K + 7) / 8 * 8;
+    const long long ldb = a.b_layout == B2G_B_NK ? lda : ((long long)a.N + 7) / 8 * 8;
+    const long long ldd = a.N;
+    const long long brows = a.b_layout == B2G_B_NK ? a.N : a.K;
+    const size_t nA = (size_t)a.M * lda, nB = (size_t)brows * ldb, nD = (size_t)a.M * ldd;
+    std::vector<uint16_t> hA(nA, 0), hB(nB, 0), hBias((size_t)std::max(a.N, 1), 0);
+    {
+        // logical (unpadded) data first, then spread into the padded rows
+        std::vector<uint16_t> tA((size_t)a.M * a.K), tB((size_t)a.N * a.K);
+        if (a.init_ref) {
+            b2g_fill_lcg_f16(tA.data(), (long long)tA.size(), tB.data(), (long long)tB.size(),
+                             hBias.data(), a.N);
+        } else {
+            b2g_fill_uniform_f16(tA.data(), (long long)tA.size(), 0, a.seed, 0, a.lo, a.hi);
+            b2g_fill_uniform_f16(tB.data(), (long long)tB.size(), 0, a.seed, 1, a.lo, a.hi);
+            b2g_fill_uniform_f16(hBias.data(), a.N, 0, a.seed, 2, a.lo, a.hi);
+        }
+        for (int m = 0; m < a.M; ++m)
+            memcpy(&hA[(size_t)m * lda], &tA[(size_t)m * a.K], (size_t)a.K * 2);
+        // tB is N x K; in KN mode store its transpose
+        for (int n = 0; n < a.N; ++n)
+            for (int k = 0; k < a.K; ++k) {
+                const uint16_t v = tB[(size_t)n * a.K + k];
+                if (a.b_layout == B2G_B_NK) hB[(size_t)n * ldb + k] = v;
+                else hB[(size_t)k * ldb + n] = v;
+            }
+    }
+    void *dA, *dB, *dD, *dRef, *dBias;
+    float* dErr;
+    CUDA_CHECK(cudaMalloc(&dA, std::max<size_t>(nA, 8) * 2));
+    CUDA_CHECK(cudaMalloc(&dB, std::max<size_t>(nB, 8) * 2));
+    CUDA_CHECK(cudaMalloc(&dD, std::max<size_t>(nD, 8) * 2));
+    CUDA_CHECK(cudaMalloc(&dRef, std::max<size_t>(nD, 8) * 2));
+    CUDA_CHECK(cudaMalloc(&dBias, hBias.size() * 2));
+    CUDA_CHECK(cudaMalloc(&dErr, sizeof(float)));
+    CUDA_CHECK(cudaMemcpy(dA, hA.data(), nA * 2, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy(dB, hB.data(), nB * 2, cudaMemcpyHostToDevice));
+    CUDA_CHECK(cudaMemcpy(dBias, hBias.data(), hBias.size() * 2, cudaMemcpyHostToDevice));
+    cudaStream_t stream = 0;
+
+    const double flop = 2.0 * a.M * a.N * a.K;
+    double ref_ms = 0, ref_tflops = 0;
+    const bool cublas_ok = a.b_layout == B2G_B_NK && lda == a.K;  // the reference call's layout
+    if ((a.ref || a.check) && cublas_ok && a.M && a.N && a.K) {
+        for (int i = 0; i < a.warmup; ++i)
+            if (b2g_cublas_gemm(dA, dB, dRef, a.M, a.N, a.K, stream)) {
+                fprintf(stderr, "cuBLAS: %s\n", b2g_last_error());
+                return 1;
+            }
+        cudaEvent_t t0, t1;
+        CUDA_CHECK(cudaEventCreate(&t0));
+        CUDA_CHECK(cudaEventCreate(&t1));
+        CUDA_CHECK(cudaEventRecord(t0, stream));
+        for (int i = 0; i < a.iters; ++i) b2g_cublas_gemm(dA, dB, dRef, a.M, a.N, a.K, stream);
+        CUDA_CHECK(cudaEventRecord(t1, stream));
+        CUDA_CHECK(cudaEventSynchronize(t1));
+        float tot = 0;
+        CUDA_CHECK(cudaEventElapsedTime(&tot, t0, t1));
+        ref_ms = tot / std::max(1, a.iters);
+        ref_tflops = flop / (ref_ms * 1e-3) / 1e12;
+        cudaEventDestroy(t0);
+        cudaEventDestroy(t1);
+    }
+
+    const bool epi = a.fused || a.unfused;
+    printf("# device        : %s  sm_%d%d  %d SMs\n", prop.name, prop.major, prop.minor,
+           prop.multiProcessorCount);
+    printf("# problem       : M=%d N=%d K=%d  fp16 in / %s acc / fp16 out  (A row-major, B %s)\n",
+           a.M, a.N, a.K, a.acc == B2G_ACC_F32 ? "fp32" : "fp16",
+           a.b_layout == B2G_B_NK ? "N x K (col-major K x N)" : "K x N row-major");
+    printf("# accumulate    : %s\n", a.acc == B2G_ACC_F32 ? "FP32 (tcgen05 kind::f16, F32 D in TMEM)"
+                                                          : "FP16 (tcgen05 kind::f16, F16 D in TMEM)");
+    printf("# epilogue      : %s\n", a.fused ? "FUSED alpha*acc + bias + ReLU"
+                                             : a.unfused ? "UNFUSED bias+ReLU kernel" : "plain store");
+    printf("# inputs        : %s\n", a.init_ref ? "reference LCG (seed 12345)" : "seeded uniform");
+    printf("# iters         : %d (warmup %d)\n", a.iters, a.warmup);
+    if (a.ref && ref_ms > 0) printf("# cuBLAS (SoL)  : %8.3f ms  %7.2f TFLOP/s\n", ref_ms, ref_tflops);
+    printf("\n");
+    printf("%-6s %-12s %-8s %6s %5s %5s %7s %6s %6s %10s %9s %8s %s\n", "tile", "CTA", "layout",
+           "stages", "grp", "thr", "reg/thr", "smem", "CTA/SM", "ms", "TFLOP/s", "%SoL", "maxrel");
+    printf("%s\n", std::string(118, '-').c_str());
+
+    struct Job { int tile, layout, stages, group; };
+    std::vector<Job> jobs;
+    if (a.sweep) {
+        for (int s = 2; s <= 8; ++s) jobs.push_back({a.tile, a.layout, s, a.group});
+    } else if (a.gsweep) {
+        for (int g : {1, 2, 4, 8, 16}) jobs.push_back({a.tile, a.layout, a.stages, g});
+    } else {
+        jobs.push_back({a.tile, a.layout, a.stages, a.group});
+    }
+
+    int rc_all = 0;
+    for (const Job& j : jobs) {
+        auto skip = [&](const char* why) {
+            printf("%-6d %-12s %-8s %6d %5d %5s %7s %6s %6s %10s %9s %8s  SKIP: %s\n", j.tile,
+                   tile_name(j.tile), "sw128", j.stages, j.group, "-", "-", "-", "-", "-", "-",
+                   "-", why);
+        };
+        if (j.layout != 2) {
+            skip("layout not applicable on sm_100a (TMA writes the 128B-swizzled UMMA layout)");
+            continue;
+        }
+        int thr = 0, regs = 0, smem = 0, occ = 0, tmem = 0, st_used = 0;
+        if (b2g_config_info(j.tile, j.stages, &thr, &regs, &smem, &occ, &tmem, &st_used)) {
+            skip(b2g_last_error());
+            continue;
+        }
+        CUDA_CHECK(cudaMemset(dD, 0, std::max<size_t>(nD, 8) * 2));
+        auto launch = [&]() -> int {
+            int rc = b2g_gemm(dA, dB, dD, a.fused ? dBias : nullptr, a.M, a.N, a.K, lda, ldb, ldd,
+                              a.b_layout, a.acc, a.fused ? B2G_EPI_BIAS_RELU : B2G_EPI_NONE, 1.0f,
+                              j.tile, j.stages, j.group, stream);
+            if (rc == B2G_OK && a.unfused)
+                rc = b2g_bias_relu(dD, dBias, a.M, a.N, ldd, 1.0f, stream);
+            return rc;
+        };
+        int rc = B2G_OK;
+        for (int i = 0; i < a.warmup && rc == B2G_OK; ++i) rc = launch();
+        if (rc == B2G_OK) rc = b2g_sync_status(stream);
+        if (rc != B2G_OK) {
+            skip(b2g_last_error());
+            rc_all = 1;
+            continue;
+        }
+        cudaEvent_t t0, t1;
+        CUDA_CHECK(cudaEventCreate(&t0));
+        CUDA_CHECK(cudaEventCreate(&t1));
+        double ms = 0, tflops = 0;
+        if (a.soak > 0) {
+            printf("# soak %.0f s, window %.1f s -- columns are parseable CSV after 'SOAK,'\n",
+                   a.soak, a.window);
+            printf("SOAK,elapsed_s,window_ms,iters,tflops,ms_per_iter\n");
+            fflush(stdout);
+            const double wall0 = now_s();
+            double best = 0, worst = 1e30, sum_flop = 0, sum_s = 0;
+            int nwin = 0;
+            while (now_s() - wall0 < a.soak) {
+                int n = 0;
+                CUDA_CHECK(cudaEventRecord(t0, stream));
+                const double ws = now_s();
+                do {
+                    launch();
+                    ++n;
+                    if ((n & 7) == 0) CUDA_CHECK(cudaStreamSynchronize(stream));
+                } while (now_s() - ws < a.window);
+                CUDA_CHECK(cudaEventRecord(t1, stream));
+                CUDA_CHECK(cudaEventSynchronize(t1));
+                float wms = 0;
+                CUDA_CHECK(cudaEventElapsedTime(&wms, t0, t1));
+                const double tf = flop * n / (wms * 1e-3) / 1e12;
+                printf("SOAK,%.2f,%.2f,%d,%.3f,%.4f\n", now_s() - wall0, wms, n, tf, wms / n);
+                fflush(stdout);
+                best = std::max(best, tf);
+                worst = std::min(worst, tf);
+                sum_flop += flop * n;
+                sum_s += wms * 1e-3;
+                ++nwin;
+            }
+            const double avg = sum_flop / sum_s / 1e12;
+            printf("# soak summary: windows=%d  avg=%.2f  max=%.2f  min=%.2f TFLOP/s  spread=%.1f%%\n",
+                   nwin, avg, best, worst, 100.0 * (best - worst) / best);
+            ms = sum_s * 1e3 / (sum_flop / flop);
+            tflops = avg;
+        } else {
+            CUDA_CHECK(cudaEventRecord(t0, stream));
+            for (int i = 0; i < a.iters; ++i) launch();
+            CUDA_CHECK(cudaEventRecord(t1, stream));
+            CUDA_CHECK(cudaEventSynchronize(t1));
+            float tot = 0;
+            CUDA_CHECK(cudaEventElapsedTime(&tot, t0, t1));
+            ms = tot / std::max(1, a.iters);
+            tflops = flop / (ms * 1e-3) / 1e12;
+        }
+        cudaEventDestroy(t0);
+        cudaEventDestroy(t1);
+        rc = b2g_sync_status(stream);
+        if (rc != B2G_OK) {
+            skip(b2g_last_error());
+            rc_all = 1;
+            continue;
+        }
+
+        double maxrel = -1, cpurel = -1, frob = -1;
+        int wm = -1, wn = -1;
+        if (a.check && !epi && cublas_ok && ref_ms > 0) {
+            b2g_max_rel_diff(dD, dRef, nD, dErr, stream);
+            float e = 0;
+            CUDA_CHECK(cudaMemcpy(&e, dErr, sizeof e, cudaMemcpyDeviceToHost));
+            maxrel = e;
+        }
+        if (a.cpu > 0 || a.frob > 0) {
+            std::vector<uint16_t> hD(nD);
+            CUDA_CHECK(cudaMemcpy(hD.data(), dD, nD * 2, cudaMemcpyDeviceToHost));
+            if (a.cpu > 0)
+                cpurel = spot_check(hA, lda, hB, ldb, a.b_layout, hD, ldd, hBias, a.M, a.N, a.K,
+                                    a.cpu, epi, 1.0f, &wm, &wn);
+            if (a.frob > 0)
+                frob = frobenius_rows(hA, lda, hB, ldb, a.b_layout, hD, ldd, hBias, a.M, a.N, a.K,
+                                      a.frob, epi, 1.0f);
+        }
+        char errbuf[32], solbuf[16];
+        if (maxrel < 0) snprintf(errbuf, sizeof errbuf, "-");
+        else snprintf(errbuf, sizeof errbuf, "%.2e%s", maxrel, maxrel < 3e-2 ? " OK" : " FAIL");
+        if (a.ref && ref_tflops > 0) snprintf(solbuf, sizeof solbuf, "%.1f%%", 100.0 * tflops / ref_tflops);
+        else snprintf(solbuf, sizeof solbuf, "-");
+        printf("%-6d %-12s %-8s %6d %5d %5d %7d %6d %6d %10.3f %9.2f %8s %s", j.tile,
+               tile_name(j.tile), "sw128", st_used, j.group, thr, regs, smem, occ, ms, tflops,
+               solbuf, errbuf);
+        if (cpurel >= 0)
+            printf("  cpu=%.2e%s(worst m=%d n=%d)", cpurel, cpurel < 3e-2 ? " OK " : " FAIL ", wm, wn);
+        if (frob >= 0) printf("  frob=%.2e", frob);
+        printf("\n");
+        if (a.json)
+            printf("{\"M\": %d, \"N\": %d, \"K\": %d, \"tile\": %d, \"stages\": %d, \"group\": %d, "
+                   "\"acc\": \"%s\", \"ms\": %.5f, \"tflops\": %.3f, \"cublas_tflops\": %.3f, "
+                   "\"maxrel_vs_cublas\": %.3e, \"cpu_maxrel\": %.3e, \"frob_rel\": %.3e}\n",
+                   a.M, a.N, a.K, j.tile, st_used, j.group, a.acc == B2G_ACC_F32 ? "f32" : "f16", ms,
+                   tflops, ref_tflops, maxrel, cpurel, frob);
+        fflush(stdout);
+    }
+    cudaFree(dA); cudaFree(dB); cudaFree(dD); cudaFree(dRef); cudaFree(dBias); cudaFree(dErr);
+    return rc_all;
+}

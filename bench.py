@@ -1,0 +1,551 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 FP16 GEMM hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload headline|f16acc|sharded] [--tile T] [--stages S] [--group G]
+
+A step is one GEMM D = A * B over one batch of synthetic FP16 input (seeded uniform,
+BASELINE.json configs). Workloads:
+  headline  configs[1]: 4096^3, seed 1, U[-1,1], FP32 accumulate. Under torchrun every rank
+            multiplies its own 4096-row M-panel of a (4096*N) x 4096 x 4096 GEMM with B
+            replicated (no data-path collective): weak scaling.
+  f16acc    configs[2]: 4096^3, seed 2, U[-0.5,0.5], FP16 accumulate (same sharding).
+  sharded   configs[4]: 32768 x 32768 x 8192, seed 3, U[-1,1], FP32 accumulate; the M rows
+            are split over the ranks (strong scaling); --allgather adds a timed NCCL
+            all-gather of the D panels, reported separately.
+
+`value` is whole-job TFLOP/s with inputs resident in HBM, timed with CUDA events on the
+launching stream, max over ranks. Between timed iterations the inputs rotate over enough
+buffer sets that the working set exceeds the 126 MB L2. `e2e` is the same metric through
+the C-ABI with pinned host buffers: every step copies A and B host->device and D back.
+--impl reference times the reference's own implementation on the same workload: its CPU
+GEMM code (the FP64 dot products of cpu_spot_check, src/gemm_bench.cu:672-696, compiled
+from its source) on all host cores, plus its sm_89 kernel JIT-run on this B200 as an extra
+column.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import glob
+import json
+import math
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "ada-tensor-core-gemm_b200")
+sys.path.insert(0, PKG)
+
+METRIC = "TFLOP/s (4096³ FP16→FP32acc) and % of B200 dense FP16 peak; 1/2/4/8-GPU"
+L2_BYTES = 126 * 1024 * 1024
+
+WORKLOADS = {
+    "headline": dict(M=4096, N=4096, K=4096, seed=1, lo=-1.0, hi=1.0, acc="f32", split=False,
+                     name="configs[1]: 4096x4096x4096 FP16 in, FP32 acc, per GPU (M-panels)"),
+    "f16acc": dict(M=4096, N=4096, K=4096, seed=2, lo=-0.5, hi=0.5, acc="f16", split=False,
+                   name="configs[2]: 4096x4096x4096 FP16 in, FP16 acc, per GPU (M-panels)"),
+    "sharded": dict(M=32768, N=32768, K=8192, seed=3, lo=-1.0, hi=1.0, acc="f32", split=True,
+                    name="configs[4]: 32768x32768x8192 FP16 in, FP32 acc, M split over GPUs"),
+}
+
+NVML_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+                0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+                0x100: "display_clock_setting"}
+
+
+def parse():
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--workload", choices=tuple(WORKLOADS), default="headline")
+    p.add_argument("--tile", type=int, default=-1)
+    p.add_argument("--stages", type=int, default=0)
+    p.add_argument("--group", type=int, default=8)
+    p.add_argument("--e2e-steps", type=int, default=0, help="0 = min(steps, 20)")
+    p.add_argument("--cpu-seconds", type=float, default=10.0,
+                   help="target CPU time of the bounded cpu_baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--allgather", action="store_true")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------------------
+def panel(M, world, rank):
+    """Rows [r0, r1) of rank `rank` when M rows are split as evenly as possible."""
+    r0 = M * rank // world
+    r1 = M * (rank + 1) // world
+    return r0, r1
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            d = json.load(fh)
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def traffic_from_profiles(kernel_key: str):
+    """DRAM bytes per launch from a committed ncu summary line
+    `dram_bytes_per_launch[<kernel_key>]: <bytes>` under profiles/."""
+    pat = re.compile(r"dram_bytes_per_launch\[" + re.escape(kernel_key) + r"\]:\s*([0-9.eE+]+)")
+    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", "*.md"))):
+        with open(path) as fh:
+            m = pat.search(fh.read())
+        if m:
+            return float(m.group(1)), os.path.relpath(path, ROOT)
+    return None, None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML in a background thread."""
+
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
+        self.period = period_s
+        self.samples = []  # (t, sm_mhz, reasons_bits)
+        self.ok = False
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = None
+            try:
+                import torch
+
+                uuid = str(torch.cuda.get_device_properties(cuda_index).uuid)
+                if not uuid.startswith("GPU-"):
+                    uuid = "GPU-" + uuid
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid.encode())
+            except Exception:
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+                idx = int(vis.split(",")[cuda_index]) if vis else cuda_index
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # noqa: BLE001
+            self.err = str(e)
+
+    def _reasons(self):
+        nv = self.nv
+        for fn in ("nvmlDeviceGetCurrentClocksEventReasons",
+                   "nvmlDeviceGetCurrentClocksThrottleReasons"):
+            if hasattr(nv, fn):
+                return getattr(nv, fn)(self.h)
+        return 0
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append((time.perf_counter(),
+                                     self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM),
+                                     self._reasons()))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
+
+    def start(self):
+        if not self.ok:
+            return
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+
+    def mark(self, name):
+        setattr(self, name, time.perf_counter())
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self, t0, t1):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0,
+                    "note": "NVML unavailable: " + getattr(self, "err", "?")}
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not inside and self.samples:  # timed region shorter than the sampling period
+            inside = [min(self.samples, key=lambda s: abs(s[0] - t1))]
+        bits = 0
+        for s in inside:
+            bits |= s[2]
+        reasons = sorted(n for b, n in NVML_REASONS.items() if bits & b and b != 0x1)
+        return {"sm_mhz": statistics.median(s[1] for s in inside) if inside else None,
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(inside)}
+
+
+# ---------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------
+def run_ours(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import b2g
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+
+    wl = WORKLOADS[args.workload]
+    Mg, N, K = wl["M"] * (1 if wl["split"] else world), wl["N"], wl["K"]
+    r0, r1 = panel(Mg, world, rank)
+    rows = r1 - r0
+    acc = b2g.ACC_F32 if wl["acc"] == "f32" else b2g.ACC_F16
+    flop_rank = 2.0 * rows * N * K
+    flop_job = 2.0 * Mg * N * K
+
+    # pinned host inputs of this rank (its M-panel of A, all of B)
+    hA = torch.empty((rows, K), dtype=torch.float16, pin_memory=True)
+    hB = torch.empty((N, K), dtype=torch.float16, pin_memory=True)
+    hD = torch.empty((rows, N), dtype=torch.float16, pin_memory=True)
+    b2g.fill_uniform(rows * K, wl["seed"], 0, wl["lo"], wl["hi"], out=hA.data_ptr(),
+                     first=r0 * K)
+    b2g.fill_uniform(N * K, wl["seed"], 1, wl["lo"], wl["hi"], out=hB.data_ptr())
+
+    set_bytes = 2 * (rows * K + N * K + rows * N)
+    nbuf = max(1, min(4, math.ceil(2 * L2_BYTES / set_bytes)))
+    sets = []
+    for _ in range(nbuf):
+        dA = torch.empty((rows, K), dtype=torch.float16, device=dev)
+        dB = torch.empty((N, K), dtype=torch.float16, device=dev)
+        dA.copy_(hA)
+        dB.copy_(hB)
+        sets.append((dA, dB, torch.empty((rows, N), dtype=torch.float16, device=dev)))
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+
+    def launch(i, which="ours"):
+        dA, dB, dD = sets[i % nbuf]
+        if which == "ours":
+            b2g.gemm_raw(dA.data_ptr(), dB.data_ptr(), dD.data_ptr(), None, rows, N, K, K, K, N,
+                         b2g.B_NK, acc, b2g.EPI_NONE, 1.0, args.tile, args.stages, args.group,
+                         sptr)
+        else:
+            b2g.cublas_gemm(dA, dB, dD, sptr)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def timed(which, steps, warmup, sampler=None):
+        for i in range(warmup):
+            launch(i, which)
+        b2g.sync_status(sptr)
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if sampler:
+            sampler.mark("t0")
+        e0.record(stream)
+        for i in range(steps):
+            launch(i, which)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if sampler:
+            sampler.mark("t1")
+        barrier()
+        b2g.sync_status(sptr)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    # tcgen05 issue-rate probe (FLOP/clk/SM), for the %-of-peak column
+    probe_fpc, _ = b2g.probe_tcgen05(1 if acc == b2g.ACC_F16 else 0, 1, 256, 4096)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    ms = timed("ours", args.steps, args.warmup, sampler)
+    sampler.stop()
+    clocks = sampler.summary(sampler.t0, sampler.t1)
+
+    # correctness of the timed output against cuBLAS (device max-rel, reference metric)
+    dA, dB, dD = sets[(args.steps - 1) % nbuf]
+    dRef = torch.empty_like(dD)
+    b2g.cublas_gemm(dA, dB, dRef, sptr)
+    err = torch.zeros(1, dtype=torch.float32, device=dev)
+    b2g.max_rel_diff(dD, dRef, err, sptr)
+    maxrel = float(err.item())
+    del dRef
+    ms_cublas = timed("cublas", args.steps, args.warmup)
+
+    # e2e through the C-ABI with pinned host buffers: H2D of A and B, GEMM, D2H of D
+    e2e_steps = args.e2e_steps or min(args.steps, 20)
+    dA, dB, dD = sets[0]
+
+    def e2e_step():
+        dA.copy_(hA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        b2g.gemm_raw(dA.data_ptr(), dB.data_ptr(), dD.data_ptr(), None, rows, N, K, K, K, N,
+                     b2g.B_NK, acc, b2g.EPI_NONE, 1.0, args.tile, args.stages, args.group, sptr)
+        hD.copy_(dD, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    b2g.sync_status(sptr)
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    b2g.sync_status(sptr)
+    ms_e2e = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms_e2e], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+
+    allgather = None
+    if args.allgather and world > 1:
+        full = torch.empty((rows * world, N), dtype=torch.float16, device=dev)
+        src = sets[0][2]
+        for _ in range(2):
+            dist.all_gather_into_tensor(full, src)
+        torch.cuda.synchronize()
+        barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(stream)
+        reps = 5
+        for _ in range(reps):
+            dist.all_gather_into_tensor(full, src)
+        a1.record(stream)
+        torch.cuda.synchronize()
+        ag = a0.elapsed_time(a1) / reps
+        t = torch.tensor([ag], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ag = float(t.item())
+        recv = (world - 1) * rows * N * 2
+        allgather = {"ms": ag, "bytes_received_per_gpu": recv, "gbs_per_gpu": recv / (ag * 1e-3) / 1e9}
+        del full
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(hA.numpy().view(np.uint16), hB.numpy().view(np.uint16), N, K,
+                           args.cpu_seconds, wl)
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks, peak_src = measured_peaks()
+    per_launch_ms = ms / args.steps
+    achieved = flop_rank / (per_launch_ms * 1e-3) / 1e12
+    sustained = ms > 1000.0
+    peak = peaks["bf16_tflops_sustained" if sustained else "bf16_tflops"]
+    kernel_key = f"gemm_sm100_{args.workload}"
+    traffic, traffic_src = traffic_from_profiles(kernel_key)
+    sms = torch.cuda.get_device_properties(local).multi_processor_count
+    sm_mhz = clocks.get("sm_mhz") or peaks.get("clocks_under_load", {}).get("sm_mhz_median")
+    probe_peak = probe_fpc * sms * sm_mhz * 1e6 / 1e12 if sm_mhz else None
+    value = flop_job * args.steps / (ms * 1e-3) / 1e12
+    h2d = 2 * (rows * K + N * K)
+    d2h = 2 * rows * N
+    out = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "strong" if wl["split"] else "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic: seeded counter-based uniform FP16 (BASELINE.json seeds/ranges)",
+        "config": {
+            "workload": wl["name"], "M_total": Mg, "M_per_gpu": rows, "N": N, "K": K,
+            "acc": wl["acc"], "seed": wl["seed"], "dist": [wl["lo"], wl["hi"]],
+            "tile": args.tile, "stages": args.stages, "group": args.group,
+            "parallelism": f"M-row panels x{world}, B replicated, no data-path collective",
+            "l2": f"{nbuf} rotating input sets of {set_bytes / 2**20:.0f} MiB "
+                  f"({nbuf * set_bytes / 2**20:.0f} MiB > 126 MiB L2)",
+        },
+        "roofline": {
+            "bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+            "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+            "peak_source": f"{peak_src} cuBLAS bf16 "
+                           f"{'sustained' if sustained else 'burst'} (MEASURED_PEAKS.json)",
+            "traffic": traffic, "traffic_source": traffic_src,
+            "algorithmic_flop_per_launch": flop_rank,
+            "algorithmic_bytes_per_launch": 2 * (rows * K + N * K + rows * N),
+        },
+        "pct_probe_peak": round(100 * achieved / probe_peak, 2) if probe_peak else None,
+        "probe": {"flop_per_clk_sm": round(probe_fpc, 1), "sms": sms, "sm_mhz": sm_mhz,
+                  "peak_tflops": round(probe_peak, 1) if probe_peak else None},
+        "cublas_tflops": round(flop_job * args.steps / (ms_cublas * 1e-3) / 1e12, 3),
+        "maxrel_vs_cublas": maxrel,
+        "e2e": {"value": round(flop_job * e2e_steps / (ms_e2e * 1e-3) / 1e12, 3),
+                "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
+                "d2h_bytes_per_step": d2h * world, "steps": e2e_steps},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    if cpu:
+        out["cpu_baseline"] = cpu
+    if allgather:
+        out["allgather"] = allgather
+    print(json.dumps(out), flush=True)
+
+
+def cpu_baseline(A, B, N, K, seconds, wl):
+    """Blocked FP32 CPU GEMM (the oracle's, all OpenMP threads) on a bounded row sample."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    O.lib()
+    t = time.perf_counter()
+    O.gemm_f32_blocked(A, B, 0, 0, 16)
+    dt = max(time.perf_counter() - t, 1e-6)
+    rows = int(min(A.shape[0], max(16, 16 * seconds / dt)))
+    t = time.perf_counter()
+    _, threads = O.gemm_f32_blocked(A, B, 0, 0, rows)
+    dt = time.perf_counter() - t
+    return {"value": round(2.0 * rows * N * K / dt / 1e12, 5), "unit": "TFLOP/s",
+            "cores": threads, "kind": "port",
+            "sample": f"{rows} of {A.shape[0]} rows of the {wl['M']}x{N}x{K} GEMM, blocked "
+                      f"FP32 (oracle/oracle.c orc_gemm_f32_blocked), {dt:.1f} s"}
+
+
+# ---------------------------------------------------------------------------------------
+# reference arm
+# ---------------------------------------------------------------------------------------
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+
+    import oracle as O
+
+    wl = WORKLOADS[args.workload]
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    if not O.ref_available():
+        print(json.dumps({"impl": "reference",
+                          "unavailable": "oracle/_ref/libref.so was not built (needs the "
+                                         "reference checkout at build time)"}))
+        return
+    R = O.ref()
+    A = O.fill_uniform((M, K), wl["seed"], 0, wl["lo"], wl["hi"])
+    B = O.fill_uniform((N, K), wl["seed"], 1, wl["lo"], wl["hi"])
+    D = np.zeros((M, N), np.uint16)
+    try:
+        threads = len(os.sched_getaffinity(0))
+    except AttributeError:
+        threads = os.cpu_count() or 1
+    # calibrate: one row per thread
+    t = R.ref_cpu_rows(A, B, D, M, N, K, 0, threads, threads)
+    rate = 2.0 * threads * N * K / max(t, 1e-6)  # FLOP/s
+    budget = 90.0
+    t_step = budget / max(1, args.steps + args.warmup)
+    rows = int(max(threads, min(M, rate * t_step / (2.0 * N * K))))
+    for i in range(args.warmup):
+        R.ref_cpu_rows(A, B, D, M, N, K, (i * rows) % max(1, M - rows + 1), rows, threads)
+    tot = 0.0
+    for i in range(args.steps):
+        tot += R.ref_cpu_rows(A, B, D, M, N, K, (i * rows) % max(1, M - rows + 1), rows, threads)
+    value = 2.0 * rows * N * K * args.steps / tot / 1e12
+    sample = (f"{rows} of {M} output rows per step (every element of those rows, FP64 dot "
+              f"products), {threads} host threads")
+    out = {
+        "metric": METRIC, "value": round(value, 6), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(tot / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong" if wl["split"] else "weak", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic: seeded counter-based uniform FP16 (BASELINE.json seeds/ranges)",
+        "config": {"workload": wl["name"], "M": M, "N": N, "K": K, "acc": wl["acc"],
+                   "seed": wl["seed"], "dist": [wl["lo"], wl["hi"]]},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "reference",
+                         "sample": sample + "; cpu_spot_check from src/gemm_bench.cu "
+                                            "compiled from the reference's source"},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    try:
+        out["ref_sm89_on_b200"] = ref_kernel_on_gpu(R, A, B, M, N, K, wl, args)
+    except Exception as e:  # noqa: BLE001
+        out["ref_sm89_on_b200"] = {"unavailable": str(e)[:200]}
+    print(json.dumps(out), flush=True)
+
+
+def ref_kernel_on_gpu(R, A, B, M, N, K, wl, args):
+    """The reference's own sm_89 kernel (README best config: tile 3, 3 stages, swizzle,
+    group 2, MMA_K8; or its FP16-accumulate build) JIT-run on this B200."""
+    import numpy as np
+    import torch
+
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    variant = 2 if wl["acc"] == "f16" else 3
+    dA = torch.from_numpy(A.view(np.float16)).cuda()
+    dB = torch.from_numpy(B.view(np.float16)).cuda()
+    nbuf = 3
+    Ds = [torch.empty((M, N), dtype=torch.float16, device="cuda") for _ in range(nbuf)]
+    As = [dA] + [dA.clone() for _ in range(nbuf - 1)]
+    Bs = [dB] + [dB.clone() for _ in range(nbuf - 1)]
+    s = torch.cuda.current_stream()
+
+    def launch(i):
+        rc = R.ref_gemm_launch(variant, As[i % nbuf].data_ptr(), Bs[i % nbuf].data_ptr(),
+                               Ds[i % nbuf].data_ptr(), None, M, N, K, 1.0, 2, 3, 3, 2,
+                               s.cuda_stream)
+        if rc != 0:
+            raise RuntimeError(f"reference kernel launch failed: cudaError {rc}")
+
+    for i in range(max(3, args.warmup)):
+        launch(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(args.steps):
+        launch(i)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    return {"tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 3), "ms_per_step": ms,
+            "kernel": "gemm_kernel<128,128,32,2,2,3,SWZ> MMA_K8" if variant == 3
+            else "gemm_kernel<128,128,32,2,2,3,SWZ> ACC_F16",
+            "build": "compute_89 PTX from src/gemm_bench.cu, JIT by the driver"}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

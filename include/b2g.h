@@ -1,0 +1,176 @@
+/*
+ * b2g.h -- C-ABI of the B200 (sm_100a) FP16 tensor-core GEMM.
+ *
+ * D = A * B with FP16 inputs, FP32 or FP16 accumulation, FP16 output, optionally fused
+ * alpha*acc + bias + ReLU. Kernels are hand-written for sm_100a: TMA tile loads into an
+ * mbarrier-guarded shared-memory ring, tcgen05.mma with accumulators in tensor memory,
+ * and a persistent, warp-specialised tile scheduler.
+ *
+ * The reference (a single-file sm_89 benchmark) has no library ABI; its boundary is the
+ * kernel launch inside its CLI. Each entry point below names the reference code it
+ * replaces (paths relative to the reference project root).
+ *
+ * Conventions
+ *   - Plain pointers and sizes only. FP16 data is IEEE binary16 (uint16_t bit patterns).
+ *   - Device pointers are caller-owned; no entry point keeps them after it returns.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Layouts (reference src/gemm_bench.cu:8-15):
+ *       A: M x K row-major, leading dimension lda >= K
+ *       B: b_layout B2G_B_NK: N x K row-major (ldb >= K), the reference's "TN" layout
+ *          b_layout B2G_B_KN: K x N row-major (ldb >= N)
+ *       D: M x N row-major, ldd >= N
+ *   - Launch entry points are asynchronous and never call exit(). They return a b2g_status;
+ *     b2g_last_error() gives the message of the last failure on the calling thread.
+ *     A device-side failure (a bounded wait that ran out) is reported by b2g_sync_status().
+ */
+#ifndef B2G_H
+#define B2G_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum b2g_status {
+    B2G_OK = 0,
+    B2G_ERR_ARG = 1,         /* bad shape or flag value                                   */
+    B2G_ERR_ALIGN = 2,       /* pointer / leading dimension breaks the 16-byte TMA rule   */
+    B2G_ERR_UNSUPPORTED = 3, /* configuration not built (reference: pick() -> nullptr)    */
+    B2G_ERR_SMEM = 4,        /* over the shared-memory opt-in limit (reference: SKIP row) */
+    B2G_ERR_CUDA = 5,        /* a CUDA runtime / driver call failed                       */
+    B2G_ERR_TIMEOUT = 6,     /* a device-side wait hit its limit; the kernel returned     */
+    B2G_ERR_NO_DEVICE = 7,   /* no sm_100 device is current                               */
+    B2G_ERR_LIBRARY = 8      /* cuBLAS (comparison column only) failed                    */
+};
+
+enum { B2G_B_NK = 0, B2G_B_KN = 1 };              /* B operand layout               */
+enum { B2G_ACC_F32 = 0, B2G_ACC_F16 = 1 };        /* accumulator type               */
+enum { B2G_EPI_NONE = 0, B2G_EPI_BIAS_RELU = 1 }; /* epilogue                       */
+
+/* Tile configurations (the `tile` argument). Replaces the reference's TileCfg<0..4>
+ * (src/gemm_bench.cu:413-425), which are Ada warp tilings with no meaning on tcgen05.
+ *   B2G_TILE_128x128   : one CTA, UMMA 128x128x16, TMEM 2 x 128 columns
+ *   B2G_TILE_128x256   : one CTA, UMMA 128x256x16, TMEM 2 x 256 columns
+ *   B2G_TILE_256x256_2SM : a 2-CTA cluster (cta_group::2), UMMA 256x256x16, each CTA loads
+ *                        its own 128 rows of A and 128 rows of B (no multicast)
+ *   B2G_TILE_AUTO      : chosen from the shape                                           */
+enum {
+    B2G_TILE_128x128 = 0,
+    B2G_TILE_128x256 = 1,
+    B2G_TILE_256x256_2SM = 2,
+    B2G_TILE_AUTO = -1
+};
+
+/* ---------------------------------------------------------------------------------------
+ * GEMM. Replaces gemm_kernel<BM,BN,BK,WM,WN,STAGES,LAYOUT>(A, B, D, bias, M, N, K, alpha,
+ * group) (src/gemm_bench.cu:213-217) as launched by run_cfg (src/gemm_bench.cu:480-488)
+ * and selected by pick(tile, layout, stages) (src/gemm_bench.cu:596-605). The reference's
+ * compile-time switches FUSE_EPILOGUE and ACC_F16 (src/gemm_bench.cu:31-47) are the
+ * runtime arguments `epilogue` and `acc` here.
+ *
+ *   bias     : N FP16 values, read only when epilogue == B2G_EPI_BIAS_RELU (may be NULL)
+ *   alpha    : epilogue scale (reference passes 1.0f, src/gemm_bench.cu:482)
+ *   tile     : B2G_TILE_* ; stages: shared-memory ring depth, 0 = deepest that fits
+ *   group    : L2 rasterization, `group` M-tiles walked column-major (1 = row-major),
+ *              same mapping as src/gemm_bench.cu:237-250
+ * Requirements: A, B 16-byte aligned; lda, ldb multiples of 8 elements (TMA strides are
+ * multiples of 16 bytes). D and ldd have no alignment rule (unaligned D takes a scalar
+ * store path). M, N, K >= 0; K == 0 writes the epilogue of a zero accumulator.
+ * Unlike the reference (K % 32 == 0, src/gemm_bench.cu:746) any K is accepted: the
+ * ragged K tail is zero-filled by TMA.
+ * ------------------------------------------------------------------------------------- */
+int b2g_gemm(const void* A, const void* B, void* D, const void* bias, int M, int N, int K,
+             long long lda, long long ldb, long long ldd, int b_layout, int acc, int epilogue,
+             float alpha, int tile, int stages, int group, void* stream);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* b2g_last_error(void);
+
+/* Synchronises `stream`, then reads and clears this device's status word. Returns
+ * B2G_ERR_TIMEOUT if any kernel of this library gave up a bounded wait since the last
+ * call (the message names the role and barrier), B2G_ERR_CUDA on a CUDA error. */
+int b2g_sync_status(void* stream);
+
+/* Static properties of a configuration, for the report table columns the reference prints
+ * from run_cfg (src/gemm_bench.cu:458-472): threads per CTA, registers per thread, dynamic
+ * shared memory bytes, resident CTAs per SM, TMEM columns, and the stage count used when
+ * `stages` is 0. Any output pointer may be NULL. */
+int b2g_config_info(int tile, int stages, int* threads, int* regs, int* smem_bytes,
+                    int* ctas_per_sm, int* tmem_cols, int* stages_used);
+
+/* cuBLAS comparison column: exactly the reference's call (src/gemm_bench.cu:625-633):
+ * cublasGemmEx(OP_T, OP_N, N, M, K, alpha, B, 16F, K, A, 16F, K, beta=0, D, 16F, N,
+ * COMPUTE_32F, DEFAULT_TENSOR_OP) on `stream`, with tensor-op math mode
+ * (src/gemm_bench.cu:777-778). Uses one cached handle per thread and device. */
+int b2g_cublas_gemm(const void* A, const void* B, void* D, int M, int N, int K, void* stream);
+
+/* Device-side max |x - y| / max(1, |y|) over n FP16 values into *out_dev (FP32, device
+ * memory). Replaces max_rel_diff (src/gemm_bench.cu:648-664). */
+int b2g_max_rel_diff(const void* x, const void* y, size_t n, float* out_dev, void* stream);
+
+/* Unfused epilogue: D = relu(alpha * D + bias[n]) in place (bias may be NULL). Replaces
+ * bias_relu_kernel (src/gemm_bench.cu:401-408), the reference's --unfused comparison. */
+int b2g_bias_relu(void* D, const void* bias, int M, int N, long long ldd, float alpha,
+                  void* stream);
+
+/* tcgen05 issue-rate probe. Replaces mma_probe / probe_one / probe
+ * (src/device_query.cu:48-163, 199-224), which time register-resident mma.sync.
+ *   kind     : 0 kind::f16 F16 in, F32 accumulate   1 kind::f16 F16 in, F16 accumulate
+ *              2 kind::i8 S8 in, S32 accumulate      3 kind::f8f6f4 E4M3 in, F32 accumulate
+ *   cta_group: 1 or 2 (2 = the MMA of a 2-CTA pair, M = 256)
+ *   n        : UMMA N (8..256, multiple of 16 for cta_group 1 M=128)
+ *   iters    : back-to-back MMAs per CTA (operands resident in shared memory,
+ *              accumulator in TMEM, no memory traffic in the loop)
+ * One CTA (or pair) per SM; clock64-timed on the device like the reference.
+ * Outputs the best (fewest-cycle) SM's dense FLOP per clock per SM and its cycles. */
+int b2g_probe_tcgen05(int kind, int cta_group, int n, int iters, double* flop_per_clk_sm,
+                      long long* cycles);
+
+/* HBM stream probe: `reps` copies of `bytes` from src to dst (both device, caller-owned,
+ * 16-byte aligned), timed with CUDA events on `stream`. Replaces bw_kernel /
+ * probe_bandwidth (src/device_query.cu:165-197). Outputs read+write GB/s. */
+int b2g_probe_hbm(const void* src, void* dst, size_t bytes, int reps, void* stream,
+                  double* gbs);
+
+/* Host input generators (the same values on every machine).
+ * b2g_fill_lcg_f16 reproduces the reference's deterministic init bit for bit
+ * (src/gemm_bench.cu:760-765): A, then B (N x K order), then bias.
+ * b2g_fill_uniform_f16 is the seeded counter-based generator of the synthetic inputs;
+ * dst[j] gets the value of global element index i = first + j (so a row panel of a
+ * larger matrix can be generated on its own):
+ *   key = mix(seed * 0x9E3779B97F4A7C15 ^ (tensor_id + 1) * 0xD1B54A32D192ED03)
+ *   u   = (mix(key + i * 0x9E3779B97F4A7C15) >> 40) * 2^-24,  v = lo + (hi - lo) * u
+ * (mix = the splitmix64 finaliser), rounded to FP16 (RNE). Multi-threaded. */
+void b2g_fill_lcg_f16(uint16_t* A, long long nA, uint16_t* B, long long nB, uint16_t* bias,
+                      long long nbias);
+void b2g_fill_uniform_f16(uint16_t* dst, long long n, long long first, uint64_t seed,
+                          uint32_t tensor_id, double lo, double hi);
+
+/* Tile scheduler mapping used by every persistent GEMM kernel: linear tile id ->
+ * (m_tile, n_tile). Same rasterization as src/gemm_bench.cu:237-250. */
+void b2g_tile_coord(int linear, int tiles_m, int tiles_n, int group, int* m_tile,
+                    int* n_tile);
+
+/* Failure-detection self-test: launches one CTA that waits on an mbarrier nothing
+ * arrives at, with a wait limit of `timeout_us` microseconds (1..2,000,000). The wait
+ * gives up, records B2G_ERR_TIMEOUT in the status word and the kernel returns; the call
+ * then returns what b2g_sync_status() returns (B2G_ERR_TIMEOUT when working). The CUDA
+ * context stays usable. No counterpart in the reference (it has fail-fast exit() only,
+ * src/gemm_bench.cu:59-76). */
+int b2g_selftest_wait_timeout(unsigned timeout_us, void* stream);
+
+/* Device-side wait limit used by every kernel of this library, in microseconds
+ * (default 4,000,000; the environment variable B2G_WAIT_TIMEOUT_US overrides it).
+ * Returns the previous value. */
+unsigned long long b2g_set_wait_timeout_us(unsigned long long us);
+
+/* Library version (major*10000 + minor*100 + patch). */
+int b2g_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2G_H */

@@ -1,0 +1,367 @@
+/*
+ * oracle.c -- CPU restatement of the reference GEMM path. TEST INFRASTRUCTURE ONLY.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg may load this
+ * library, and only as the checker (or the timed CPU baseline). The product path
+ * (ada-tensor-core-gemm_b200/) never links or calls it.
+ *
+ * What is restated, and from where (paths relative to the reference project root):
+ *   orc_fill_lcg        src/gemm_bench.cu:760-765   deterministic LCG init of A, B, bias
+ *   orc_spot_check      src/gemm_bench.cu:666-696   FP64 sampled dot-product check
+ *   orc_max_rel_diff    src/gemm_bench.cu:648-664   max |x-y|/max(1,|y|)
+ *   orc_tile_coord      src/gemm_bench.cu:237-250   grouped CTA rasterization
+ *   orc_epilogue        src/gemm_bench.cu:379-395   alpha*acc + bias, ReLU, FP16 RN store
+ *   orc_bias_relu       src/gemm_bench.cu:402-408   unfused epilogue kernel
+ * plus the oracle's own full-GEMM references (FP64, FP32 triple loop, blocked FP32 with
+ * OpenMP for the CPU baseline), the seeded counter-based uniform generator that the
+ * product uses for synthetic inputs, and IEEE binary16 conversions.
+ *
+ * Parity pins: the FP64 spot check and fp16 conversion are checked against the reference's
+ * own cpu_spot_check / host __float2half compiled from its source (oracle/ref_shim.cu);
+ * the LCG + spot check chain is checked on the GPU against the reference's published
+ * FP32-accumulate error (4.53e-04 at 4096^3, --cpu 512, docs/RESULTS.md:396).
+ *
+ * Layout conventions (same as the reference, src/gemm_bench.cu:8-10):
+ *   A: M x K row-major, leading dimension lda (elements)
+ *   B: b_layout 0 = "NK": N x K row-major (the reference's TN layout), ldb >= K
+ *      b_layout 1 = "KN": K x N row-major, ldb >= N
+ *   D: M x N row-major, ldd >= N
+ * All FP16 data is passed as uint16_t bit patterns.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+/* ------------------------------------------------------------------------------------ */
+/* IEEE binary16 <-> binary32, round to nearest even (what the reference gets from       */
+/* cuda_fp16.h's host __float2half / __half2float).                                     */
+/* ------------------------------------------------------------------------------------ */
+uint16_t orc_f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u) /* inf / nan */
+        return (uint16_t)(sign | 0x7C00u | (ax > 0x7F800000u ? 0x0200u : 0u));
+    if (ax >= 0x477FF000u) /* >= 65520 rounds to inf */
+        return (uint16_t)(sign | 0x7C00u);
+    if (ax >= 0x38800000u) { /* normal binary16 range, >= 2^-14 */
+        uint32_t e = (ax >> 23) - 127 + 15;
+        uint32_t mant = ax & 0x7FFFFFu;
+        uint32_t h = (e << 10) | (mant >> 13);
+        uint32_t rem = mant & 0x1FFFu;
+        if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+        return (uint16_t)(sign | h);
+    }
+    /* subnormal or zero: result = round(value / 2^-24) */
+    {
+        uint32_t e = ax >> 23;
+        if (e == 0) return (uint16_t)sign; /* f32 subnormals are far below 2^-25 */
+        uint32_t m = (ax & 0x7FFFFFu) | 0x800000u;
+        int shift = 126 - (int)e; /* value = m * 2^(e-150); in 2^-24 units: m >> (126-e) */
+        if (shift >= 32) return (uint16_t)sign;
+        uint32_t h = m >> shift;
+        uint32_t rem = m & ((1u << shift) - 1u);
+        uint32_t half = 1u << (shift - 1);
+        if (rem > half || (rem == half && (h & 1u))) h++;
+        return (uint16_t)(sign | h);
+    }
+}
+
+float orc_f16_to_f32(uint16_t h) {
+    uint32_t sign = ((uint32_t)h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 0x1Fu;
+    uint32_t m = h & 0x3FFu;
+    uint32_t x;
+    if (e == 0x1F) {
+        x = sign | 0x7F800000u | (m << 13);
+    } else if (e == 0) {
+        if (m == 0) {
+            x = sign;
+        } else { /* subnormal: normalise */
+            int s = 0;
+            while (!(m & 0x400u)) { m <<= 1; s++; }
+            m &= 0x3FFu;
+            x = sign | ((uint32_t)(127 - 15 + 1 - s) << 23) | (m << 13);
+        }
+    } else {
+        x = sign | ((e - 15 + 127) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &x, 4);
+    return f;
+}
+
+void orc_f32_to_f16_array(const float* src, uint16_t* dst, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) dst[i] = orc_f32_to_f16(src[i]);
+}
+
+void orc_f16_to_f32_array(const uint16_t* src, float* dst, int64_t n) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) dst[i] = orc_f16_to_f32(src[i]);
+}
+
+/* ------------------------------------------------------------------------------------ */
+/* Input generators                                                                     */
+/* ------------------------------------------------------------------------------------ */
+
+/* src/gemm_bench.cu:760-765: s = 12345; s = s*1664525 + 1013904223;
+ * value = ((s >> 16) & 1023) / 1023.f - 0.5f, A first, then B (N x K order), then bias. */
+void orc_fill_lcg(uint16_t* A, int64_t nA, uint16_t* B, int64_t nB, uint16_t* bias, int64_t nbias) {
+    uint32_t s = 12345u;
+#define ORC_RND() (s = s * 1664525u + 1013904223u, (float)((s >> 16) & 1023u) / 1023.f - 0.5f)
+    for (int64_t i = 0; i < nA; ++i) A[i] = orc_f32_to_f16(ORC_RND());
+    for (int64_t i = 0; i < nB; ++i) B[i] = orc_f32_to_f16(ORC_RND());
+    for (int64_t i = 0; i < nbias; ++i) bias[i] = orc_f32_to_f16(ORC_RND());
+#undef ORC_RND
+}
+
+/* Counter-based uniform generator used for the seeded synthetic inputs (the product
+ * implements the same formula in b2g_fill_uniform_f16; the tests check bit identity):
+ *   key = mix(seed * 0x9E3779B97F4A7C15 ^ (tensor_id + 1) * 0xD1B54A32D192ED03)
+ *   h   = mix(key + index * 0x9E3779B97F4A7C15)      (mix = splitmix64 finaliser)
+ *   index = first + position in dst (row panels of a larger matrix)
+ *   u   = (h >> 40) * 2^-24 in [0, 1)
+ *   v   = lo + (hi - lo) * u   (in double), rounded to float, then to FP16 (RNE). */
+static uint64_t orc_mix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+void orc_fill_uniform(uint16_t* dst, int64_t n, int64_t first, uint64_t seed, uint32_t tensor_id,
+                      double lo, double hi) {
+    const uint64_t key =
+        orc_mix64(seed * 0x9E3779B97F4A7C15ull ^ ((uint64_t)tensor_id + 1ull) * 0xD1B54A32D192ED03ull);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        uint64_t h = orc_mix64(key + (uint64_t)(first + i) * 0x9E3779B97F4A7C15ull);
+        double u = (double)(h >> 40) * (1.0 / 16777216.0);
+        double v = lo + (hi - lo) * u;
+        dst[i] = orc_f32_to_f16((float)v);
+    }
+}
+
+/* ------------------------------------------------------------------------------------ */
+/* Reference GEMMs                                                                      */
+/* ------------------------------------------------------------------------------------ */
+static inline float orc_b_at(const uint16_t* B, int b_layout, int64_t ldb, int64_t k, int64_t n) {
+    return orc_f16_to_f32(b_layout == 0 ? B[n * ldb + k] : B[k * ldb + n]);
+}
+
+/* Full FP64 GEMM: D64[m*N+n] = sum_k A[m,k]*B(k,n), exact FP16 products, FP64 sums in
+ * ascending k (the accumulation order of src/gemm_bench.cu:683-686). Rows [m0, m1). */
+void orc_gemm_f64(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb, int b_layout,
+                  int M, int N, int K, int m0, int m1, double* D64) {
+    (void)M;
+    /* B as FP64, N x K contiguous so every dot product streams both operands */
+    double* Bt = (double*)malloc(sizeof(double) * (size_t)N * (size_t)(K > 0 ? K : 1));
+#pragma omp parallel for schedule(static)
+    for (int64_t n = 0; n < N; ++n)
+        for (int64_t k = 0; k < K; ++k) Bt[n * K + k] = (double)orc_b_at(B, b_layout, ldb, k, n);
+#pragma omp parallel
+    {
+        double* arow = (double*)malloc(sizeof(double) * (size_t)(K > 0 ? K : 1));
+#pragma omp for schedule(dynamic, 1)
+        for (int64_t m = m0; m < m1; ++m) {
+            for (int64_t k = 0; k < K; ++k) arow[k] = (double)orc_f16_to_f32(A[m * lda + k]);
+            for (int64_t n = 0; n < N; ++n) {
+                const double* b = Bt + n * K;
+                double acc = 0.0;
+                for (int64_t k = 0; k < K; ++k) acc += arow[k] * b[k];
+                D64[(m - m0) * (int64_t)N + n] = acc;
+            }
+        }
+        free(arow);
+    }
+    free(Bt);
+}
+
+/* Plain FP32 triple loop (element-wise reference at 512^3).
+ * FP32 products and FP32 sums in ascending k. */
+void orc_gemm_f32_naive(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb,
+                        int b_layout, int M, int N, int K, float* D32) {
+#pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m)
+        for (int64_t n = 0; n < N; ++n) {
+            float acc = 0.f;
+            for (int64_t k = 0; k < K; ++k)
+                acc += orc_f16_to_f32(A[m * lda + k]) * orc_b_at(B, b_layout, ldb, k, n);
+            D32[m * (int64_t)N + n] = acc;
+        }
+}
+
+/* Blocked FP32 GEMM over all OpenMP threads: the CPU baseline the bench times.
+ * FP16 panels are widened to FP32, B is repacked K x N so the inner loop is a unit-stride
+ * AXPY the compiler vectorises; blocks of 64 rows x 512 cols x 256 k stay in L2.
+ * Computes rows [m0, m1) into D32 (row m at D32[(m-m0)*N]). Returns the thread count. */
+int orc_gemm_f32_blocked(const uint16_t* A, int64_t lda, const uint16_t* B, int64_t ldb,
+                         int b_layout, int M, int N, int K, int m0, int m1, float* D32) {
+    (void)M;
+    enum { MB = 64, NB = 512, KB = 256 };
+    const int64_t rows = m1 - m0;
+    float* Bf = (float*)malloc(sizeof(float) * (size_t)K * (size_t)N + 64);
+    float* Af = (float*)malloc(sizeof(float) * (size_t)rows * (size_t)K + 64);
+    int nthreads = 1;
+#pragma omp parallel
+    {
+#ifdef _OPENMP
+#pragma omp single
+        nthreads = omp_get_num_threads();
+#endif
+#pragma omp for schedule(static)
+        for (int64_t k = 0; k < K; ++k)
+            for (int64_t n = 0; n < N; ++n) Bf[k * N + n] = orc_b_at(B, b_layout, ldb, k, n);
+#pragma omp for schedule(static)
+        for (int64_t m = 0; m < rows; ++m)
+            for (int64_t k = 0; k < K; ++k) Af[m * K + k] = orc_f16_to_f32(A[(m + m0) * lda + k]);
+#pragma omp for schedule(static)
+        for (int64_t m = 0; m < rows; ++m)
+            for (int64_t n = 0; n < N; ++n) D32[m * N + n] = 0.f;
+        const int64_t mblocks = (rows + MB - 1) / MB, nblocks = (N + NB - 1) / NB;
+#pragma omp for collapse(2) schedule(dynamic, 1)
+        for (int64_t mb = 0; mb < mblocks; ++mb)
+            for (int64_t nb = 0; nb < nblocks; ++nb) {
+                const int64_t i0 = mb * MB, i1 = (i0 + MB < rows) ? i0 + MB : rows;
+                const int64_t j0 = nb * NB, j1 = (j0 + NB < N) ? j0 + NB : N;
+                for (int64_t k0 = 0; k0 < K; k0 += KB) {
+                    const int64_t k1 = (k0 + KB < K) ? k0 + KB : K;
+                    for (int64_t i = i0; i < i1; ++i) {
+                        float* __restrict__ c = D32 + i * N;
+                        const float* __restrict__ a = Af + i * K;
+                        for (int64_t k = k0; k < k1; ++k) {
+                            const float av = a[k];
+                            const float* __restrict__ b = Bf + k * N;
+                            for (int64_t j = j0; j < j1; ++j) c[j] += av * b[j];
+                        }
+                    }
+                }
+            }
+    }
+    free(Bf);
+    free(Af);
+    return nthreads;
+}
+
+/* ------------------------------------------------------------------------------------ */
+/* Checks restated from the reference                                                   */
+/* ------------------------------------------------------------------------------------ */
+
+/* src/gemm_bench.cu:672-696. B is N x K (the reference's layout). Returns the worst
+ * |got - ref| / max(1, |ref|) over `samples` elements visited at a fixed odd stride. */
+double orc_spot_check(const uint16_t* A, const uint16_t* B, const uint16_t* D,
+                      const uint16_t* bias, int M, int N, int K, int samples, int fused,
+                      float alpha, int* worst_m, int* worst_n) {
+    double worst = 0.0;
+    *worst_m = *worst_n = -1;
+    const long long total = (long long)M * N;
+    const long long stride = (total / (samples > 1 ? samples : 1)) | 1;
+    long long idx = 0;
+    for (long long s = 0; s < samples && s < total; ++s, idx = (idx + stride) % total) {
+        int m = (int)(idx / N), n = (int)(idx % N);
+        double acc = 0.0;
+        for (int k = 0; k < K; ++k)
+            acc += (double)orc_f16_to_f32(A[(size_t)m * K + k]) *
+                   (double)orc_f16_to_f32(B[(size_t)n * K + k]);
+        if (fused) {
+            acc = acc * alpha + (double)orc_f16_to_f32(bias[n]);
+            if (acc < 0) acc = 0;
+        }
+        double got = (double)orc_f16_to_f32(D[(size_t)m * N + n]);
+        double rel = fabs(got - acc) / (fabs(acc) > 1.0 ? fabs(acc) : 1.0);
+        if (rel > worst) {
+            worst = rel;
+            *worst_m = m;
+            *worst_n = n;
+        }
+    }
+    return worst;
+}
+
+/* src/gemm_bench.cu:648-664: max over i of |x-y| / max(1, |y|), in FP32. */
+float orc_max_rel_diff(const uint16_t* x, const uint16_t* y, int64_t n) {
+    float worst = 0.f;
+#pragma omp parallel for reduction(max : worst) schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        float a = orc_f16_to_f32(x[i]), b = orc_f16_to_f32(y[i]);
+        float d = fabsf(a - b) / fmaxf(1.f, fabsf(b));
+        if (d > worst) worst = d;
+    }
+    return worst;
+}
+
+/* Relative Frobenius error || D - R ||_F / || R ||_F over an M x N block (D FP16 with
+ * leading dimension ldd, R FP64 dense). */
+double orc_frobenius_rel(const uint16_t* D, int64_t ldd, const double* R, int M, int N) {
+    double num = 0.0, den = 0.0;
+#pragma omp parallel for reduction(+ : num, den) schedule(static)
+    for (int64_t m = 0; m < M; ++m)
+        for (int64_t n = 0; n < N; ++n) {
+            double r = R[m * (int64_t)N + n];
+            double d = (double)orc_f16_to_f32(D[m * ldd + n]) - r;
+            num += d * d;
+            den += r * r;
+        }
+    return den > 0 ? sqrt(num / den) : sqrt(num);
+}
+
+/* src/gemm_bench.cu:237-250: linear tile id -> (m_tile, n_tile), `group` M-tiles walked
+ * column-major inside each group; group <= 1 is plain row-major. */
+void orc_tile_coord(int linear, int tiles_m, int tiles_n, int group, int* m_tile, int* n_tile) {
+    if (group <= 1) {
+        *m_tile = linear / tiles_n;
+        *n_tile = linear % tiles_n;
+        return;
+    }
+    const int g = linear / (group * tiles_n);
+    const int first = g * group;
+    const int rows = (group < tiles_m - first) ? group : tiles_m - first;
+    const int idx = linear - first * tiles_n;
+    *m_tile = first + idx % rows;
+    *n_tile = idx / rows;
+}
+
+/* src/gemm_bench.cu:379-395: v = alpha*acc + bias[n]; ReLU; store FP16 RN.
+ * fused == 0 is the plain store. acc is an FP32 accumulator value. */
+uint16_t orc_epilogue(float acc, int fused, float alpha, uint16_t bias_n, int has_bias) {
+    float v = acc;
+    if (fused) {
+        /* nvcc contracts the reference's `v *= alpha; v += bias` into one FMA (-fmad=true) */
+        v = has_bias ? fmaf(v, alpha, orc_f16_to_f32(bias_n)) : v * alpha;
+        v = v > 0.f ? v : 0.f;
+    }
+    return orc_f32_to_f16(v);
+}
+
+void orc_epilogue_array(const float* acc, int M, int N, int fused, float alpha,
+                        const uint16_t* bias, uint16_t* out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m)
+        for (int64_t n = 0; n < N; ++n)
+            out[m * N + n] = orc_epilogue(acc[m * N + n], fused, alpha, bias ? bias[n] : 0,
+                                          bias != 0);
+}
+
+/* src/gemm_bench.cu:402-408 (unfused epilogue): D = relu(alpha*D + bias[i % N]) in place. */
+void orc_bias_relu(uint16_t* D, const uint16_t* bias, int M, int N, float alpha) {
+    const int64_t n = (int64_t)M * N;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        float v = orc_f16_to_f32(D[i]) * alpha;
+        if (bias) v += orc_f16_to_f32(bias[i % N]);
+        D[i] = orc_f32_to_f16(v > 0.f ? v : 0.f);
+    }
+}
+
+int orc_num_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

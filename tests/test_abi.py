@@ -1,0 +1,104 @@
+"""CPU tests of the C-ABI library: it loads without a GPU, exports every symbol that
+include/b2g.h declares, validates arguments before touching the device, and its host
+logic (tile scheduler, input generators) agrees with the oracle."""
+import ctypes as C
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import b2g
+import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "b2g.h")
+CLI = os.path.join(b2g.LIB_DIR, "gemm_bench")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(b2g_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = b2g.lib()
+    syms = declared_symbols()
+    assert len(syms) >= 15
+    for s in syms:
+        assert hasattr(L, s), f"{s} declared in b2g.h but not exported"
+    assert set(syms) == set(b2g.EXPORTS)
+
+
+def test_version_and_last_error():
+    assert b2g.version() >= 100
+    assert isinstance(b2g.last_error(), str)
+
+
+def test_argument_validation_without_gpu():
+    L = b2g.lib()
+    # bad arguments are rejected before any CUDA call
+    assert L.b2g_gemm(None, None, None, None, -1, 4, 4, 4, 4, 4, 0, 0, 0, 1.0, -1, 0, 1,
+                      None) == b2g.ERR_ARG
+    assert "negative" in b2g.last_error()
+    assert L.b2g_gemm(None, None, None, None, 4, 4, 4, 8, 8, 4, 5, 0, 0, 1.0, -1, 0, 1,
+                      None) == b2g.ERR_ARG
+    assert L.b2g_gemm(None, None, None, None, 4, 4, 4, 8, 8, 4, 0, 2, 0, 1.0, -1, 0, 1,
+                      None) == b2g.ERR_ARG
+    assert L.b2g_gemm(None, None, None, None, 4, 4, 4, 8, 8, 4, 0, 0, 0, 1.0, 7, 0, 1,
+                      None) == b2g.ERR_ARG
+    assert L.b2g_gemm(None, None, None, None, 4, 4, 4, 8, 8, 4, 0, 0, 0, 1.0, -1, 9, 1,
+                      None) == b2g.ERR_ARG
+    # empty problems are a no-op
+    assert L.b2g_gemm(None, None, None, None, 0, 4, 4, 8, 8, 4, 0, 0, 0, 1.0, -1, 0, 1,
+                      None) == b2g.OK
+    # a valid call on a machine without a device fails cleanly
+    rc = L.b2g_gemm(16, 16, 16, None, 4, 4, 8, 8, 8, 4, 0, 0, 0, 1.0, -1, 0, 1, None)
+    assert rc in (b2g.ERR_NO_DEVICE, b2g.OK)
+    assert L.b2g_selftest_wait_timeout(0, None) == b2g.ERR_ARG
+    assert L.b2g_probe_tcgen05(7, 1, 256, 10, None, None) == b2g.ERR_ARG
+
+
+def test_tile_coord_matches_reference_rasterization():
+    for tm, tn, g in [(1, 1, 1), (7, 5, 1), (7, 5, 2), (7, 5, 3), (32, 16, 8), (33, 17, 16),
+                      (3, 100, 16), (256, 256, 8)]:
+        seen = set()
+        for t in range(tm * tn):
+            got = b2g.tile_coord(t, tm, tn, g)
+            assert got == O.tile_coord(t, tm, tn, g)
+            seen.add(got)
+        assert len(seen) == tm * tn
+
+
+def test_generators_match_oracle():
+    for seed, tid, lo, hi in [(0, 0, -1.0, 1.0), (1, 1, -1.0, 1.0), (2, 0, -0.5, 0.5),
+                              (12345, 2, -0.3, 0.7)]:
+        got = b2g.fill_uniform(100003, seed, tid, lo, hi)
+        assert np.array_equal(got, O.fill_uniform((100003,), seed, tid, lo, hi))
+    A, B, bias = b2g.fill_lcg(33, 17, 40)
+    A2, B2, bias2 = O.fill_lcg(33, 17, 40)
+    assert np.array_equal(A, A2) and np.array_equal(B, B2) and np.array_equal(bias, bias2)
+
+
+def test_wait_timeout_setting():
+    prev = b2g.set_wait_timeout_us(1234567)
+    assert b2g.set_wait_timeout_us(prev) == 1234567
+
+
+def test_cli_flags_without_gpu():
+    assert os.path.exists(CLI)
+    r = subprocess.run([CLI, "--help"], capture_output=True, text=True)
+    assert r.returncode == 0 and "--tile" in r.stdout and "--soak" in r.stdout
+    r = subprocess.run([CLI, "--definitely-not-a-flag"], capture_output=True, text=True)
+    assert r.returncode == 2 and "unknown option" in r.stderr
+    r = subprocess.run([CLI, "--acc", "f64"], capture_output=True, text=True)
+    assert r.returncode == 2
+
+
+def test_generator_panels_are_slices_of_the_full_matrix():
+    full = b2g.fill_uniform(64 * 48, 3, 0)
+    for first, n in [(0, 100), (48 * 10, 48 * 7), (64 * 48 - 5, 5)]:
+        assert np.array_equal(b2g.fill_uniform(n, 3, 0, first=first), full[first:first + n])
+        assert np.array_equal(O.fill_uniform((n,), 3, 0, first=first), full[first:first + n])

@@ -1,0 +1,212 @@
+"""GPU parity tests of the sm_100a GEMM, through the C-ABI, against the CPU oracle and the
+reference's own sm_89 kernel (compiled from its source, JIT-run on the B200).
+
+Tolerances (from the north star): relative Frobenius error vs FP64 <= 1e-3 for FP32
+accumulation and <= 5e-3 for FP16 accumulation; the reference's own OK threshold on
+max |x - y| / max(1, |y|) is 3e-2 (src/gemm_bench.cu:851, :861).
+"""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+import b2g
+import oracle as O
+from helpers import check_rows, inputs, run, sample_rows, to_dev, to_host
+
+pytestmark = pytest.mark.gpu
+
+FROB_F32 = 1e-3
+FROB_F16 = 5e-3
+REF_OK = 3e-2
+# FP32 accumulation, FP16 output: the output rounding alone is up to 2^-11 relative; allow
+# two half-ulps element-wise for accumulation-order differences
+ELEM_F32 = 2 * 2.0 ** -11
+
+
+def test_config1_512_elementwise_vs_fp32_triple_loop(cuda):
+    """512^3, seed 0, U[-1,1], FP32 acc, element-wise vs FP32 loop."""
+    A, B, _ = inputs(512, 512, 512, seed=0)
+    D = run(cuda, A, B)
+    R32 = O.gemm_f32_naive(A, B)
+    Df = O.f16_to_f32(D)
+    rel = np.abs(Df - R32) / np.maximum(1.0, np.abs(R32))
+    assert rel.max() <= ELEM_F32, rel.max()
+    assert O.frobenius_rel(D, O.gemm_f64(A, B)) <= FROB_F32
+
+
+@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256])
+@pytest.mark.parametrize("shape", [(1, 1, 8), (1, 1, 1), (7, 9, 13), (128, 128, 64),
+                                   (129, 257, 72), (300, 200, 100), (256, 512, 1000),
+                                   (1000, 33, 64), (64, 640, 4096)])
+def test_shapes_small(cuda, tile, shape):
+    M, N, K = shape
+    A, B, _ = inputs(M, N, K, seed=11)
+    lda = (K + 7) // 8 * 8
+    D = run(cuda, A, B, tile=tile, lda=lda, ldb=lda)
+    frob, maxrel = check_rows(A, B, D, list(range(M)))
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256])
+@pytest.mark.parametrize("stages", [2, 3, 4, 0])
+@pytest.mark.parametrize("group", [1, 2, 8])
+def test_tiles_stages_groups(cuda, tile, stages, group):
+    A, B, _ = inputs(1024, 768, 320, seed=3)
+    D = run(cuda, A, B, tile=tile, stages=stages, group=group)
+    frob, maxrel = check_rows(A, B, D, sample_rows(1024, 96))
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+def test_headline_4096_fp32acc(cuda):
+    """4096^3, seed 1, U[-1,1], FP32 accumulation."""
+    A, B, _ = inputs(4096, 4096, 4096, seed=1)
+    D = run(cuda, A, B)
+    frob, maxrel = check_rows(A, B, D, sample_rows(4096, 64))
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+    w, _, _ = O.spot_check(A, B, D, samples=512)
+    assert w < REF_OK and w <= ELEM_F32, w
+
+
+def test_f16acc_4096(cuda):
+    """4096^3, seed 2, U[-0.5,0.5], FP16 accumulation."""
+    A, B, _ = inputs(4096, 4096, 4096, seed=2, lo=-0.5, hi=0.5)
+    D = run(cuda, A, B, acc=b2g.ACC_F16)
+    frob, maxrel = check_rows(A, B, D, sample_rows(4096, 64))
+    print(f"f16acc 4096^3: frob {frob:.3e} maxrel {maxrel:.3e}")
+    assert frob <= FROB_F16, frob
+
+
+@pytest.mark.parametrize("shape", [(4095, 4095, 4095), (5000, 3000, 2000)])
+def test_ragged_baseline_shapes(cuda, shape):
+    """BASELINE config 4 ragged shapes; K not a multiple of 8 needs a padded lda/ldb."""
+    M, N, K = shape
+    A, B, _ = inputs(M, N, K, seed=4)
+    lda = (K + 7) // 8 * 8
+    D = run(cuda, A, B, lda=lda, ldb=lda)
+    frob, maxrel = check_rows(A, B, D, sample_rows(M, 48))
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+@pytest.mark.parametrize("shape", [(16384, 16384, 256), (256, 16384, 16384)])
+def test_skinny_baseline_shapes(cuda, shape):
+    M, N, K = shape
+    A, B, _ = inputs(M, N, K, seed=5)
+    D = run(cuda, A, B)
+    frob, maxrel = check_rows(A, B, D, sample_rows(M, 16))
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+@pytest.mark.parametrize("alpha", [1.0, 0.5])
+@pytest.mark.parametrize("with_bias", [True, False])
+def test_fused_epilogue(cuda, alpha, with_bias):
+    A, B, bias = inputs(384, 320, 192, seed=6)
+    bias = bias if with_bias else None
+    D = run(cuda, A, B, bias, epilogue=b2g.EPI_BIAS_RELU, alpha=alpha)
+    frob, maxrel = check_rows(A, B, D, list(range(384)), bias=bias, alpha=alpha, epilogue=True)
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+    assert (O.f16_to_f32(D) >= 0).all()
+
+
+def test_unaligned_output_ld(cuda):
+    A, B, _ = inputs(200, 300, 64, seed=7)
+    D = run(cuda, A, B, ldd=301)
+    frob, maxrel = check_rows(A, B, D, list(range(200)))
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32
+
+
+def test_k_zero_and_empty(cuda):
+    torch = cuda
+    A = torch.zeros((64, 0), dtype=torch.float16, device="cuda")
+    B = torch.zeros((48, 0), dtype=torch.float16, device="cuda")
+    D = torch.full((64, 48), 7.0, dtype=torch.float16, device="cuda")
+    b2g.gemm(A, B, D)
+    b2g.sync_status()
+    assert (D == 0).all()
+    bias = torch.linspace(-1, 1, 48, dtype=torch.float16, device="cuda")
+    b2g.gemm(A, B, D, bias, epilogue=b2g.EPI_BIAS_RELU)
+    b2g.sync_status()
+    assert torch.equal(D, torch.relu(bias)[None, :].expand(64, 48))
+    E = torch.full((0, 48), 1.0, dtype=torch.float16, device="cuda")
+    b2g.gemm(torch.zeros((0, 8), dtype=torch.float16, device="cuda"),
+             torch.zeros((48, 8), dtype=torch.float16, device="cuda"), E)
+    b2g.sync_status()
+
+
+def test_rejects_unaligned_inputs(cuda):
+    torch = cuda
+    A = torch.zeros((64, 100), dtype=torch.float16, device="cuda")
+    B = torch.zeros((64, 100), dtype=torch.float16, device="cuda")
+    D = torch.zeros((64, 64), dtype=torch.float16, device="cuda")
+    with pytest.raises(b2g.B2GError) as e:
+        b2g.gemm(A, B, D)  # lda = 100 is not a multiple of 8
+    assert e.value.code == b2g.ERR_ALIGN
+    buf = torch.zeros(64 * 104 + 8, dtype=torch.float16, device="cuda")
+    with pytest.raises(b2g.B2GError) as e:
+        b2g.gemm_raw(buf.data_ptr() + 2, B.data_ptr(), D.data_ptr(), None, 64, 64, 96, 104,
+                     100, 64)
+    assert e.value.code in (b2g.ERR_ALIGN,)
+    b2g.sync_status()
+
+
+def test_unfused_bias_relu_kernel(cuda):
+    torch = cuda
+    A, B, bias = inputs(130, 70, 1, seed=8)
+    D = O.f32_to_f16(O.f16_to_f32(A)[:, :1] * np.linspace(-3, 3, 70, dtype=np.float32)[None, :])
+    dD = to_dev(torch, D)
+    b2g.bias_relu(dD, to_dev(torch, bias), alpha=0.75)
+    b2g.sync_status()
+    assert np.array_equal(to_host(dD), O.bias_relu(D, bias, 0.75))
+
+
+def test_max_rel_diff_kernel(cuda):
+    torch = cuda
+    x = O.fill_uniform((1000, 37), 9, 0, -4, 4)
+    y = O.fill_uniform((1000, 37), 9, 1, -4, 4)
+    out = torch.zeros(1, dtype=torch.float32, device="cuda")
+    b2g.max_rel_diff(to_dev(torch, x), to_dev(torch, y), out)
+    b2g.sync_status()
+    assert out.item() == O.max_rel_diff(x, y)
+
+
+def test_cublas_column(cuda):
+    torch = cuda
+    A, B, _ = inputs(512, 384, 256, seed=10)
+    dD = torch.zeros((512, 384), dtype=torch.float16, device="cuda")
+    b2g.cublas_gemm(to_dev(torch, A), to_dev(torch, B), dD)
+    b2g.sync_status()
+    frob, maxrel = check_rows(A, B, to_host(dD), list(range(512)))
+    assert frob <= FROB_F32 and maxrel < REF_OK
+
+
+def test_selftest_wait_timeout_then_gemm_still_works(cuda):
+    """A bounded device wait that nothing satisfies returns an error; the context lives."""
+    assert b2g.selftest_wait_timeout(20000) == b2g.ERR_TIMEOUT
+    assert "selftest" in b2g.last_error()
+    b2g.sync_status()  # status word was cleared
+    A, B, _ = inputs(256, 256, 128, seed=12)
+    D = run(cuda, A, B)
+    frob, _ = check_rows(A, B, D, list(range(256)))
+    assert frob <= FROB_F32
+
+
+def test_probe_tcgen05(cuda):
+    rates = {}
+    for kind in (0, 1, 2, 3):
+        fl, cyc = b2g.probe_tcgen05(kind, 1, 256, 2048)
+        rates[kind] = fl
+        print(f"probe kind {kind} ({b2g.PROBE_KINDS[kind]}): {fl:.1f} FLOP/clk/SM, {cyc} cycles")
+        assert cyc > 0
+    # dense kind::f16 on one SM: 128x256x16 per MMA; nominal 8192 FLOP/clk/SM
+    assert 2000 < rates[0] < 9000
+    assert rates[2] > rates[0] * 1.5  # 8-bit kinds issue at least ~2x the 16-bit rate
+
+
+def test_probe_hbm(cuda):
+    torch = cuda
+    n = 1 << 30
+    src = torch.empty(n, dtype=torch.uint8, device="cuda")
+    dst = torch.empty(n, dtype=torch.uint8, device="cuda")
+    gbs = b2g.probe_hbm(src, dst, n, reps=10)
+    print(f"hbm copy {gbs:.1f} GB/s")
+    assert gbs > 2000
