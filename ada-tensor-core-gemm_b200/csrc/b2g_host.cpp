@@ -65,6 +65,7 @@ int current_device(DeviceInfo& out) {
     cudaDeviceGetAttribute(&di.minor, cudaDevAttrComputeCapabilityMinor, dev);
     cudaDeviceGetAttribute(&di.sm_count, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&di.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&di.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     if (di.major != 10 || di.minor != 0)
         return fail(B2G_ERR_NO_DEVICE,
                     "device %d is sm_%d%d; this library is built for sm_100a (B200) only", dev,

@@ -20,7 +20,8 @@ struct DeviceInfo {
     int device = -1;
     int major = 0, minor = 0;
     int sm_count = 0;
-    int smem_optin = 0;  // max dynamic shared memory per block (opt-in)
+    int smem_optin = 0;   // max dynamic shared memory per block (opt-in)
+    int smem_per_sm = 0;  // shared memory per SM
 };
 
 // Facts about the current device, cached. Returns B2G_OK or an error (with message).

@@ -16,6 +16,7 @@
 #include "b2g_internal.h"
 #include "aux_sm100.cuh"
 #include "gemm_sm100.cuh"
+#include "gemm_sm100_2cta.cuh"
 #include "probe_sm100.cuh"
 
 namespace b2g {
@@ -78,43 +79,109 @@ int prepare_kernel(K kern, int device, size_t dyn_smem, bool (&done)[kMaxDevices
     return B2G_OK;
 }
 
-struct TileDesc {
-    int bn;
-    size_t stage_bytes;
+// Geometry of the three GEMM kernels: output tile, CTAs per tile, TMA box rows per CTA.
+struct TileGeom {
+    int bm, bn;        // output tile of one CTA (1-CTA kernels) or of one CTA pair
+    int ctas;          // CTAs per tile
+    int box_a, box_b;  // rows of A / B that one CTA loads per k-block
 };
 
-TileDesc tile_desc(int tile) {
+TileGeom geom(int tile) {
     switch (tile) {
-        case B2G_TILE_128x128: return {128, TileTraits<128>::kStageBytes};
-        case B2G_TILE_128x256: return {256, TileTraits<256>::kStageBytes};
-        default: return {0, 0};
+        case B2G_TILE_128x128: return {128, 128, 1, 128, 128};
+        case B2G_TILE_128x256: return {128, 256, 1, 128, 256};
+        default: return {kPairBM, kPairBN, 2, 128, 128};
     }
 }
 
-size_t smem_for(int tile, int stages) {
-    return tile == B2G_TILE_128x128 ? gemm_smem_bytes<128>(stages) : gemm_smem_bytes<256>(stages);
+const void* kernel_ptr(int tile) {
+    switch (tile) {
+        case B2G_TILE_128x128: return (const void*)gemm_sm100_1cta<128>;
+        case B2G_TILE_128x256: return (const void*)gemm_sm100_1cta<256>;
+        default: return (const void*)gemm_sm100_2cta;
+    }
+}
+
+size_t smem_needed(int tile, int stages) {
+    switch (tile) {
+        case B2G_TILE_128x128: return gemm_smem_bytes<128>(stages);
+        case B2G_TILE_128x256: return gemm_smem_bytes<256>(stages);
+        default: return gemm2_smem_bytes(stages);
+    }
+}
+
+// Dynamic shared memory actually requested: at least just over half of the SM, so exactly
+// one GEMM CTA is resident per SM. Every GEMM CTA allocates 2 x BN TMEM columns; two
+// co-resident CTAs of 2-CTA clusters could otherwise each hold the TMEM the other's peer
+// waits for.
+size_t smem_request(int tile, int stages, const DeviceInfo& di) {
+    return std::max(smem_needed(tile, stages), (size_t)di.smem_per_sm / 2 + 1024);
 }
 
 int max_stages_for(int tile, int smem_optin) {
     int s = kMaxStages;
-    while (s > 2 && smem_for(tile, s) > (size_t)smem_optin) --s;
+    while (s > 2 && smem_needed(tile, s) > (size_t)smem_optin) --s;
     return s;
 }
 
-template <int BN>
-int launch_gemm_1cta(const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
-                     int grid, size_t smem, int device, cudaStream_t s) {
-    static bool done[kMaxDevices] = {};
+int ensure_kernel_attrs(int tile, const DeviceInfo& di) {
+    static bool done[3][kMaxDevices] = {};
     static std::mutex mu;
-    DeviceInfo di;
-    if (int rc = current_device(di)) return rc;
-    const size_t max_dyn = (size_t)di.smem_optin;
-    if (int rc = prepare_kernel(gemm_sm100_1cta<BN>, device, max_dyn, done, mu)) return rc;
-    gemm_sm100_1cta<BN><<<grid, kThreads, smem, s>>>(tmA, tmB, p);
+    std::lock_guard<std::mutex> lock(mu);
+    if (di.device < kMaxDevices && done[tile][di.device]) return B2G_OK;
+    cudaError_t e = cudaFuncSetAttribute(kernel_ptr(tile),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         di.smem_optin);
+    if (e != cudaSuccess)
+        return fail(B2G_ERR_CUDA, "cudaFuncSetAttribute(tile %d, max dynamic smem %d): %s", tile,
+                    di.smem_optin, cudaGetErrorString(e));
+    if (di.device < kMaxDevices) done[tile][di.device] = true;
+    return B2G_OK;
+}
+
+// Clusters of two that can be resident at once (GPCs with an odd SM count leave one idle).
+int max_pair_clusters(const DeviceInfo& di, size_t smem) {
+    static int cache[kMaxDevices] = {};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    if (di.device < kMaxDevices && cache[di.device] > 0) return cache[di.device];
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (di.sm_count / 2), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_sm100_2cta, &cfg) != cudaSuccess ||
+        n <= 0) {
+        cudaGetLastError();
+        n = di.sm_count / 2;
+    }
+    n = std::min(n, di.sm_count / 2);
+    if (di.device < kMaxDevices) cache[di.device] = n;
+    return n;
+}
+
+int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
+                const DeviceInfo& di, size_t smem, cudaStream_t s) {
+    if (int rc = ensure_kernel_attrs(tile, di)) return rc;
+    int grid = 0;
+    switch (tile) {
+        case B2G_TILE_128x128:
+            grid = std::min(p.num_tiles, di.sm_count);
+            gemm_sm100_1cta<128><<<grid, kThreads, smem, s>>>(tmA, tmB, p);
+            break;
+        case B2G_TILE_128x256:
+            grid = std::min(p.num_tiles, di.sm_count);
+            gemm_sm100_1cta<256><<<grid, kThreads, smem, s>>>(tmA, tmB, p);
+            break;
+        default:
+            grid = 2 * std::min(p.num_tiles, max_pair_clusters(di, smem));
+            gemm_sm100_2cta<<<grid, kThreads, smem, s>>>(tmA, tmB, p);
+            break;
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
-        return fail(B2G_ERR_CUDA, "gemm_sm100_1cta<%d> launch (grid %d, smem %zu): %s", BN, grid,
-                    smem, cudaGetErrorString(e));
+        return fail(B2G_ERR_CUDA, "GEMM launch (tile %d, grid %d, smem %zu): %s", tile, grid, smem,
+                    cudaGetErrorString(e));
     return B2G_OK;
 }
 
@@ -183,30 +250,28 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
     if (b_layout == B2G_B_KN)
         return fail(B2G_ERR_UNSUPPORTED, "b_layout K x N is not built yet");
 
-    if (tile == B2G_TILE_AUTO) tile = N <= 128 ? B2G_TILE_128x128 : B2G_TILE_128x256;
-    if (tile == B2G_TILE_256x256_2SM)
-        return fail(B2G_ERR_UNSUPPORTED, "tile 2 (256x256 2-SM pair) is not built yet");
-    const TileDesc td = tile_desc(tile);
+    if (tile == B2G_TILE_AUTO) tile = N <= 128 ? B2G_TILE_128x128 : B2G_TILE_256x256_2SM;
+    const TileGeom g = geom(tile);
     const int max_st = max_stages_for(tile, di.smem_optin);
     if (stages == 0) stages = max_st;
-    const size_t smem = smem_for(tile, stages);
-    if (smem > (size_t)di.smem_optin)
+    if (smem_needed(tile, stages) > (size_t)di.smem_optin)
         return fail(B2G_ERR_SMEM, "smem over per-block opt-in limit: %zu > %d (tile %d, %d stages)",
-                    smem, di.smem_optin, tile, stages);
+                    smem_needed(tile, stages), di.smem_optin, tile, stages);
+    const size_t smem = smem_request(tile, stages, di);
 
     GemmParams p{};
     p.M = M;
     p.N = N;
     p.K = K;
-    p.tiles_m = (M + kBM - 1) / kBM;
-    p.tiles_n = (N + td.bn - 1) / td.bn;
+    p.tiles_m = (M + g.bm - 1) / g.bm;
+    p.tiles_n = (N + g.bn - 1) / g.bn;
     const long long nt = (long long)p.tiles_m * p.tiles_n;
     if (nt > 0x7fffffffLL) return fail(B2G_ERR_ARG, "too many tiles (%lld)", nt);
     p.num_tiles = (int)nt;
     p.num_kb = (K + kBK - 1) / kBK;
     p.group = group < 1 ? 1 : group;
     p.stages = stages;
-    p.idesc = idesc_f16(kBM, td.bn, acc == B2G_ACC_F32, false);
+    p.idesc = idesc_f16(g.bm, g.bn, acc == B2G_ACC_F32, false);
     p.acc_f16 = acc == B2G_ACC_F16;
     p.epilogue = epilogue;
     p.alpha = alpha;
@@ -218,53 +283,46 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
     p.timeout_ns = wait_timeout_ns();
 
     CUtensorMap tmA, tmB;
-    if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK, kBM, "A"))
+    if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK, g.box_a, "A"))
         return rc;
-    if (int rc = make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, td.bn, "B"))
+    if (int rc = make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, g.box_b, "B"))
         return rc;
-
-    const int grid = std::min(p.num_tiles, di.sm_count);
-    if (td.bn == 128) return launch_gemm_1cta<128>(tmA, tmB, p, grid, smem, di.device, s);
-    return launch_gemm_1cta<256>(tmA, tmB, p, grid, smem, di.device, s);
+    return launch_gemm(tile, tmA, tmB, p, di, smem, s);
 }
 
 B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, int* smem_bytes,
                                int* ctas_per_sm, int* tmem_cols, int* stages_used) {
     clear_error();
-    if (tile == B2G_TILE_AUTO) tile = B2G_TILE_128x256;
-    if (tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256)
+    if (tile == B2G_TILE_AUTO) tile = B2G_TILE_256x256_2SM;
+    if (tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 && tile != B2G_TILE_256x256_2SM)
         return fail(B2G_ERR_UNSUPPORTED, "tile %d is not built", tile);
     DeviceInfo di;
     if (int rc = current_device(di)) return rc;
     if (stages == 0) stages = max_stages_for(tile, di.smem_optin);
     if (stages < 2 || stages > kMaxStages)
         return fail(B2G_ERR_ARG, "stages must be 2..%d", kMaxStages);
-    const size_t smem = smem_for(tile, stages);
+    const size_t need = smem_needed(tile, stages);
+    if (need > (size_t)di.smem_optin)
+        return fail(B2G_ERR_SMEM, "smem over per-block opt-in limit: %zu > %d", need, di.smem_optin);
+    if (int rc = ensure_kernel_attrs(tile, di)) return rc;
+    const size_t smem = smem_request(tile, stages, di);
     cudaFuncAttributes fa{};
-    cudaError_t e = tile == B2G_TILE_128x128 ? cudaFuncGetAttributes(&fa, gemm_sm100_1cta<128>)
-                                             : cudaFuncGetAttributes(&fa, gemm_sm100_1cta<256>);
-    if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
+    cudaError_t e = cudaFuncGetAttributes(&fa, kernel_ptr(tile));
+    if (e != cudaSuccess)
+        return fail(B2G_ERR_CUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
     int occ = 0;
-    if (smem <= (size_t)di.smem_optin) {
-        if (tile == B2G_TILE_128x128) {
-            cudaFuncSetAttribute(gemm_sm100_1cta<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 di.smem_optin);
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_sm100_1cta<128>, kThreads, smem);
-        } else {
-            cudaFuncSetAttribute(gemm_sm100_1cta<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 di.smem_optin);
-            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemm_sm100_1cta<256>, kThreads, smem);
-        }
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel_ptr(tile), kThreads, smem) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        occ = 0;
     }
     if (threads) *threads = kThreads;
     if (regs) *regs = fa.numRegs;
-    if (smem_bytes) *smem_bytes = (int)smem;
+    if (smem_bytes) *smem_bytes = (int)need;
     if (ctas_per_sm) *ctas_per_sm = occ;
-    if (tmem_cols) *tmem_cols = 2 * tile_desc(tile).bn;
+    if (tmem_cols) *tmem_cols = 2 * geom(tile).bn;
     if (stages_used) *stages_used = stages;
-    return smem <= (size_t)di.smem_optin
-               ? B2G_OK
-               : fail(B2G_ERR_SMEM, "smem over per-block opt-in limit: %zu > %d", smem, di.smem_optin);
+    return B2G_OK;
 }
 
 // ---------------------------------------------------------------------------------------

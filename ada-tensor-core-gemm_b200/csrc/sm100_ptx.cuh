@@ -265,6 +265,13 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
         : "memory");
 }
 
+// 2-CTA form (all tcgen05 ops of a kernel use one cta_group): arrive on this CTA's `bar`.
+__device__ __forceinline__ void mma_commit_2(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+        : "memory");
+}
+
 // 2-CTA form: arrive on the barrier at offset `bar` in every CTA of `cta_mask`.
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask) {
     asm volatile(
