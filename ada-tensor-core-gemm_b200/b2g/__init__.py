@@ -38,6 +38,7 @@ EXPORTS = (
     "b2g_max_rel_diff", "b2g_bias_relu", "b2g_probe_tcgen05", "b2g_probe_hbm",
     "b2g_fill_lcg_f16", "b2g_fill_uniform_f16", "b2g_tile_coord",
     "b2g_selftest_wait_timeout", "b2g_set_wait_timeout_us", "b2g_version",
+    "b2g_kernel_clock",
 )
 
 
@@ -96,6 +97,8 @@ def lib():
         L.b2g_set_wait_timeout_us.argtypes = [C.c_ulonglong]
         L.b2g_version.restype = i
         L.b2g_version.argtypes = []
+        L.b2g_kernel_clock.restype = i
+        L.b2g_kernel_clock.argtypes = [C.POINTER(d), C.POINTER(d)]
         _lib = L
     return _lib
 
@@ -254,3 +257,10 @@ def set_wait_timeout_us(us: int) -> int:
 
 def version() -> int:
     return int(lib().b2g_version())
+
+
+def kernel_clock():
+    """(SM MHz, CTA-0 lifetime in us) of the most recent completed GEMM launch."""
+    mhz, us = C.c_double(), C.c_double()
+    _check(lib().b2g_kernel_clock(C.byref(mhz), C.byref(us)))
+    return mhz.value, us.value

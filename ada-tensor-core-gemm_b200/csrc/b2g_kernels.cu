@@ -160,22 +160,50 @@ int max_pair_clusters(const DeviceInfo& di, size_t smem) {
     return n;
 }
 
-int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB, const GemmParams& p,
-                const DeviceInfo& di, size_t smem, cudaStream_t s) {
+// Column-slice factor for the tail tiles of the 2-CTA kernel: the `rest` tiles of the last
+// partial wave become rest * split units of 1/split the work; pick the split (1, 2 or 4)
+// that minimises the tail's duration ceil(rest * split / clusters) / split.
+int tail_split_for(int rest, int clusters) {
+    int best = 1;
+    double best_t = 1.0;
+    for (int split : {2, 4}) {
+        const double t = (double)((rest * split + clusters - 1) / clusters) / split;
+        if (t < best_t - 1e-9) {
+            best_t = t;
+            best = split;
+        }
+    }
+    return best;
+}
+
+// L2 rasterization: the band of `group` M-tiles walked column-major keeps its A rows
+// resident while B streams through, so pick the largest band whose A panel fills less than
+// about 45% of the 126 MB L2 (capped at the number of M-tiles).
+int auto_group(const TileGeom& g, int tiles_m, int K) {
+    const double panel = (double)g.bm * (double)K * 2.0;  // bytes of A per M-tile
+    int grp = (int)(0.45 * 126.0 * 1024 * 1024 / panel);
+    grp = std::max(1, std::min(grp, tiles_m));
+    return grp;
+}
+
+int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                const CUtensorMap& tmBt, const CUtensorMap& tmD, const GemmParams& p,
+                const DeviceInfo& di, size_t smem,
+                cudaStream_t s) {
     if (int rc = ensure_kernel_attrs(tile, di)) return rc;
     int grid = 0;
     switch (tile) {
         case B2G_TILE_128x128:
             grid = std::min(p.num_tiles, di.sm_count);
-            gemm_sm100_1cta<128><<<grid, kThreads, smem, s>>>(tmA, tmB, p);
+            gemm_sm100_1cta<128><<<grid, kThreads, smem, s>>>(tmA, tmB, tmD, p);
             break;
         case B2G_TILE_128x256:
             grid = std::min(p.num_tiles, di.sm_count);
-            gemm_sm100_1cta<256><<<grid, kThreads, smem, s>>>(tmA, tmB, p);
+            gemm_sm100_1cta<256><<<grid, kThreads, smem, s>>>(tmA, tmB, tmD, p);
             break;
         default:
-            grid = 2 * std::min(p.num_tiles, max_pair_clusters(di, smem));
-            gemm_sm100_2cta<<<grid, kThreads, smem, s>>>(tmA, tmB, p);
+            grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
+            gemm_sm100_2cta<<<grid, kThreads, smem, s>>>(tmA, tmB, tmBt, tmD, p);
             break;
     }
     cudaError_t e = cudaGetLastError();
@@ -269,7 +297,7 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
     if (nt > 0x7fffffffLL) return fail(B2G_ERR_ARG, "too many tiles (%lld)", nt);
     p.num_tiles = (int)nt;
     p.num_kb = (K + kBK - 1) / kBK;
-    p.group = group < 1 ? 1 : group;
+    p.group = group > 0 ? group : auto_group(g, p.tiles_m, K);
     p.stages = stages;
     p.idesc = idesc_f16(g.bm, g.bn, acc == B2G_ACC_F32, false);
     p.acc_f16 = acc == B2G_ACC_F16;
@@ -279,7 +307,24 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
     p.D = (__half*)D;
     p.ldd = ldd;
     p.d_vec = (((uintptr_t)D & 15) == 0) && (ldd % 8 == 0);
+    p.d_tma = p.d_vec;
     p.b_mn_major = 0;
+    p.dp_tiles = p.num_tiles;
+    p.tail_split = 1;
+    p.num_units = p.num_tiles;
+    p.idesc_tail = p.idesc;
+    if (g.ctas == 2) {
+        // cut the tiles of the last, partial wave into column slices (see pair_unit)
+        const int clusters = max_pair_clusters(di, smem);
+        const int rest = p.num_tiles % clusters;
+        const int split = rest ? tail_split_for(rest, clusters) : 1;
+        if (split > 1) {
+            p.dp_tiles = p.num_tiles - rest;
+            p.tail_split = split;
+            p.num_units = p.dp_tiles + rest * split;
+            p.idesc_tail = idesc_f16(g.bm, g.bn / split, acc == B2G_ACC_F32, false);
+        }
+    }
     p.timeout_ns = wait_timeout_ns();
 
     CUtensorMap tmA, tmB;
@@ -287,7 +332,16 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
         return rc;
     if (int rc = make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, g.box_b, "B"))
         return rc;
-    return launch_gemm(tile, tmA, tmB, p, di, smem, s);
+    CUtensorMap tmBt = tmB;  // B boxes of the tail slices (width / 2 rows per CTA)
+    if (p.tail_split > 1)
+        if (int rc = make_tmap(&tmBt, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK,
+                               (uint32_t)(g.box_b / p.tail_split), "B tail"))
+            return rc;
+    CUtensorMap tmD = tmA;  // D in 32-row x 64-column boxes (unused without d_tma)
+    if (p.d_tma)
+        if (int rc = make_tmap(&tmD, D, (uint64_t)N, (uint64_t)M, (uint64_t)ldd, 64, 32, "D"))
+            return rc;
+    return launch_gemm(tile, tmA, tmB, tmBt, tmD, p, di, smem, s);
 }
 
 B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, int* smem_bytes,
@@ -344,6 +398,30 @@ B2G_EXPORT int b2g_sync_status(void* stream) {
                 (word & kErrWaitEpilogue) ? " epilogue" : "",
                 (word & kErrWaitSelftest) ? " selftest" : "", (word & kErrWaitDrain) ? " drain" : "",
                 (word & kErrWaitProbe) ? " probe" : "");
+}
+
+#ifdef B2G_INSTRUMENT
+// Instrumented builds only: copy out (n <= 1024 CTAs x 8 slots) and clear the wait-time
+// counters of sm100_ptx.cuh.
+B2G_EXPORT int b2g_instr_read(unsigned long long* out, int n_ctas) {
+    const size_t bytes = sizeof(unsigned long long) * kInstrSlots * (size_t)n_ctas;
+    if (cudaMemcpyFromSymbol(out, g_b2g_instr, bytes) != cudaSuccess) return B2G_ERR_CUDA;
+    static unsigned long long zeros[1024][kInstrSlots];
+    return cudaMemcpyToSymbol(g_b2g_instr, zeros, sizeof(zeros)) == cudaSuccess ? B2G_OK
+                                                                                : B2G_ERR_CUDA;
+}
+#endif
+
+B2G_EXPORT int b2g_kernel_clock(double* sm_mhz, double* cta0_us) {
+    clear_error();
+    unsigned long long c[4] = {0, 0, 0, 0};
+    cudaError_t e = cudaMemcpyFromSymbol(c, g_b2g_clock, sizeof(c));
+    if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "read clock telemetry: %s", cudaGetErrorString(e));
+    if (c[1] <= c[0] || c[3] <= c[2]) return fail(B2G_ERR_ARG, "no completed GEMM launch recorded");
+    const double ns = (double)(c[1] - c[0]);
+    if (sm_mhz) *sm_mhz = (double)(c[3] - c[2]) / ns * 1e3;
+    if (cta0_us) *cta0_us = ns * 1e-3;
+    return B2G_OK;
 }
 
 B2G_EXPORT int b2g_selftest_wait_timeout(unsigned timeout_us, void* stream) {

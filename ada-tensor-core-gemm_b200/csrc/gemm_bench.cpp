@@ -44,7 +44,7 @@ namespace {
 
 struct Args {
     int M = 4096, N = 4096, K = 4096;
-    int tile = 1, stages = 0, layout = 2, group = 1;
+    int tile = -1, stages = 0, layout = 2, group = 0;  // -1 / 0 = chosen from the shape
     int iters = 50, warmup = 20;
     int cpu = 0;        // output elements verified by the FP64 host spot check
     int frob = 0;       // rows of D checked by an FP64 relative Frobenius norm
@@ -442,6 +442,8 @@ int main(int argc, char** argv) {
         if (cpurel >= 0)
             printf("  cpu=%.2e%s(worst m=%d n=%d)", cpurel, cpurel < 3e-2 ? " OK " : " FAIL ", wm, wn);
         if (frob >= 0) printf("  frob=%.2e", frob);
+        double kmhz = 0, kus = 0;
+        if (b2g_kernel_clock(&kmhz, &kus) == B2G_OK) printf("  sm_mhz=%.0f", kmhz);
         printf("\n");
         if (a.json)
             printf("{\"M\": %d, \"N\": %d, \"K\": %d, \"tile\": %d, \"stages\": %d, \"group\": %d, "

@@ -45,8 +45,14 @@ struct GemmParams {
     __half* D;
     long long ldd;
     int d_vec;       // 16-byte vector stores allowed (D 16-byte aligned and ldd % 8 == 0)
+    int d_tma;       // D written by TMA stores (same alignment conditions as d_vec)
     int b_mn_major;  // B is K x N (MN-major) in global memory
     unsigned long long timeout_ns;
+    // 2-CTA kernel work list: tiles [0, dp_tiles) run whole; each remaining tile (the last,
+    // partial wave) is cut into tail_split column slices of kPairBN / tail_split columns,
+    // so the tail wave keeps every SM busy. num_units = dp_tiles + rest * tail_split.
+    int dp_tiles, tail_split, num_units;
+    uint32_t idesc_tail;
 };
 
 constexpr int kBM = 128;      // rows of A per CTA (UMMA M for cta_group::1)
@@ -55,6 +61,11 @@ constexpr int kUmmaK = 16;    // K of one kind::f16 MMA
 constexpr int kMaxStages = 8;
 constexpr int kThreads = 192; // producer warp, MMA warp, 4 epilogue warps
 constexpr uint32_t kAStageBytes = kBM * kBK * 2;  // 16 KiB
+// Epilogue staging for TMA stores: every epilogue warp owns two 32-row x 64-column FP16
+// boxes (4 KiB each, 128-byte swizzle), used alternately so the conversion of one chunk
+// overlaps the bulk store of the previous one.
+constexpr uint32_t kEpiBoxBytes = 32 * 64 * 2;
+constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBoxBytes;  // 4 epilogue warps: 32 KiB
 
 template <int BN>
 struct TileTraits {
@@ -75,10 +86,11 @@ struct SmemCtl {
     int never;  // stays 0: lets teardown waits ignore `abort` and use only their time limit
 };
 
+// Dynamic shared memory: [align slack][stages x (A, B)][epilogue staging][SmemCtl]
 template <int BN>
 constexpr size_t gemm_smem_bytes(int stages) {
     return 1024 /* alignment slack */ + (size_t)stages * TileTraits<BN>::kStageBytes +
-           sizeof(SmemCtl);
+           kEpiBytes + sizeof(SmemCtl);
 }
 
 __device__ __forceinline__ float acc_value(uint32_t raw, int acc_f16) {
@@ -126,18 +138,153 @@ __device__ __forceinline__ void store_row_chunk32(const GemmParams& p, int row, 
     }
 }
 
+// The epilogue's per-element work uses only these scalars, read once from the kernel
+// parameters into registers (per-element reads of GemmParams fields through a reference
+// cost ~4x in the conversion loop).
+struct EpiScalars {
+    int M, N;
+    float alpha;
+    const __half* bias;
+    int d_tma;
+};
+
+__device__ __forceinline__ EpiScalars epi_scalars(const GemmParams& p) {
+    return EpiScalars{p.M, p.N, p.alpha, p.bias, p.d_tma};
+}
+
+// alpha * acc + bias + ReLU (EPI) and round to FP16, two columns per word; ACC16: the
+// accumulator is F16 in the low half of each 32-bit TMEM column.
+template <bool ACC16, bool EPI>
+__device__ __forceinline__ uint32_t epi_pack2(const EpiScalars& e, int col, uint32_t r0,
+                                              uint32_t r1) {
+    float v0, v1;
+    if constexpr (ACC16) {
+        v0 = __half2float(__ushort_as_half((unsigned short)(r0 & 0xFFFFu)));
+        v1 = __half2float(__ushort_as_half((unsigned short)(r1 & 0xFFFFu)));
+    } else {
+        v0 = __uint_as_float(r0);
+        v1 = __uint_as_float(r1);
+    }
+    if constexpr (EPI) {
+        if (e.bias != nullptr) {
+            const int n0 = col < e.N ? col : e.N - 1;
+            const int n1 = col + 1 < e.N ? col + 1 : e.N - 1;
+            v0 = fmaf(v0, e.alpha, __half2float(e.bias[n0]));
+            v1 = fmaf(v1, e.alpha, __half2float(e.bias[n1]));
+        } else {
+            v0 *= e.alpha;
+            v1 *= e.alpha;
+        }
+        v0 = v0 > 0.f ? v0 : 0.f;
+        v1 = v1 > 0.f ? v1 : 0.f;
+    }
+    __half2 t = __floats2half2_rn(v0, v1);
+    return *reinterpret_cast<uint32_t*>(&t);
+}
+
+// One 64-column chunk already in registers: convert, stage and store. With d_tma the chunk
+// goes into a swizzled 32 x 64 staging box and lane 0 issues one TMA store (the tensor map
+// clips the M / N edges); otherwise each thread stores its own row with st.global.
+template <bool ACC16, bool EPI>
+__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const EpiScalars& e,
+                                               const CUtensorMap* tmD, const uint32_t (&r)[64],
+                                               int row0, int col, uint32_t stage0, int lane,
+                                               uint32_t& seq) {
+    if (e.d_tma) {
+        const uint32_t box = stage0 + (seq & 1u) * kEpiBoxBytes;
+        B2G_TIC(t_box);
+        if (lane == 0) bulk_wait_read<1>();  // the store that last read `box` is done
+        __syncwarp();
+        B2G_TOC64(10, t_box);
+        B2G_TIC(t_cvt);
+        // row `lane` of the box = 128 bytes; 16-byte chunk j lives at (j ^ (row & 7)) * 16
+        const uint32_t rowaddr = box + (uint32_t)lane * 128u;
+        const uint32_t sw = (uint32_t)(lane & 7);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int b = j * 8;
+            const int cc = col + b;
+            st_shared_v4(rowaddr + (((uint32_t)j ^ sw) << 4),
+                         epi_pack2<ACC16, EPI>(e, cc, r[b], r[b + 1]),
+                         epi_pack2<ACC16, EPI>(e, cc + 2, r[b + 2], r[b + 3]),
+                         epi_pack2<ACC16, EPI>(e, cc + 4, r[b + 4], r[b + 5]),
+                         epi_pack2<ACC16, EPI>(e, cc + 6, r[b + 6], r[b + 7]));
+        }
+        B2G_TOC64(9, t_cvt);
+        B2G_TIC(t_st);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+            tma_store_2d(tmD, box, col, row0);
+            bulk_commit();
+        }
+        B2G_TOC64(11, t_st);
+        ++seq;
+    } else {
+        store_row_chunk32(p, row0 + lane, col, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
+        store_row_chunk32(p, row0 + lane, col + 32,
+                          *reinterpret_cast<const uint32_t(*)[32]>(&r[32]));
+    }
+}
+
+template <bool ACC16, bool EPI>
+__device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiScalars& e,
+                                                const CUtensorMap* tmD, uint32_t trow, int row0,
+                                                int n_first, int nchunks, uint32_t stage0,
+                                                int lane, uint32_t& seq) {
+    uint32_t r[64];
+#pragma unroll 1
+    for (int c = 0; c < nchunks; ++c) {
+        B2G_TIC(t_ld);
+        tmem_ld_32x32b_x64(trow + (uint32_t)c * 64u, r);
+        tmem_ld_wait();
+        B2G_TOC64(8, t_ld);
+        B2G_COUNT(12, threadIdx.x == 64 ? 1 : 0);
+        epilogue_chunk<ACC16, EPI>(p, e, tmD, r, row0, n_first + c * 64, stage0, lane, seq);
+    }
+}
+
+// Epilogue of one warp: its 32 rows [row0, row0 + 32) x columns [n_first, n_first + width)
+// (width <= 256) of the accumulator at TMEM address `trow` (lane quarter and buffer
+// applied), 64 columns at a time. `seq` counts this warp's issued TMA stores.
+__device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiScalars& e,
+                                              const CUtensorMap* tmD, uint32_t trow, int row0,
+                                              int n_first, int width, uint32_t stage0,
+                                              int lane, uint32_t& seq, bool acc16, bool epi) {
+    if (row0 >= e.M) return;  // all 32 rows outside D (uniform in the warp)
+    int nchunks = (width + 63) / 64;
+    const int in_n = (e.N - n_first + 63) / 64;  // chunks that start inside D
+    if (in_n < nchunks) nchunks = in_n;
+    if (nchunks <= 0) return;
+    if (acc16) {
+        if (epi)
+            epilogue_rows_t<true, true>(p, e, tmD, trow, row0, n_first, nchunks, stage0, lane, seq);
+        else
+            epilogue_rows_t<true, false>(p, e, tmD, trow, row0, n_first, nchunks, stage0, lane, seq);
+    } else {
+        if (epi)
+            epilogue_rows_t<false, true>(p, e, tmD, trow, row0, n_first, nchunks, stage0, lane, seq);
+        else
+            epilogue_rows_t<false, false>(p, e, tmD, trow, row0, n_first, nchunks, stage0, lane, seq);
+    }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_sm100_1cta(const __grid_constant__ CUtensorMap tmA,
-                    const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
     using TT = TileTraits<BN>;
+    clock_mark(0);
     extern __shared__ uint8_t smem_dyn[];
     // stage buffers must be 1024-byte aligned (128-byte swizzle atoms, base offset 0)
     const uint32_t raw = smem_u32(smem_dyn);
     const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
     const uint32_t sA = raw + pad;
     const uint32_t sB = sA + (uint32_t)p.stages * kAStageBytes;
-    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * TT::kStageBytes);
+    const uint32_t sEpi = raw + pad + (uint32_t)p.stages * TT::kStageBytes;
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * TT::kStageBytes +
+                                              kEpiBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t full0 = smem_u32(&ctl->full[0]);
@@ -163,6 +310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        if (p.d_tma) prefetch_tmap(&tmD);
     }
     if (warp == 1) {
         tmem_alloc<1>(smem_u32(&ctl->tmem_base), TT::kTmemCols);
@@ -220,9 +368,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp == 1) {
-        if (lane == 0) {
+        {
             // ------------------------------- MMA issuer -------------------------------
+            // Whole warp runs the loop (warp-uniform operands), one elected lane issues;
+            // descriptors are advanced by adds (all operand addresses < 256 KiB).
             const WaitCtx w{p.timeout_ns, abort_flag, kErrWaitMma};
+            const uint64_t adesc0 = sdesc_sw128(sA, 16, 1024);
+            const uint64_t bdesc0 = sdesc_sw128(sB, 16, 1024);
+            constexpr uint32_t kAStep = kAStageBytes >> 4, kBStep = TT::kBStageBytes >> 4;
+            const uint32_t idesc = p.idesc;
             int stage = 0;
             uint32_t phase = 0;
             int it = 0;
@@ -230,45 +384,51 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++it) {
                 const int buf = it & 1;
                 const uint32_t use = (uint32_t)(it >> 1) & 1u;
-                if (!mbar_wait(tempty0 + 8 * buf, use ^ 1u, w)) {
+                if (!mbar_wait_warp(tempty0 + 8 * buf, use ^ 1u, w)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait(full0 + 8 * stage, phase, w)) {
+                    if (!mbar_wait_warp(full0 + 8 * stage, phase, w)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    const uint32_t a0 = sA + stage * kAStageBytes;
-                    const uint32_t b0 = sB + stage * TT::kBStageBytes;
-#pragma unroll
-                    for (int k = 0; k < kBK / kUmmaK; ++k) {
-                        const uint64_t ad = sdesc_sw128(a0 + 32u * k, 16, 1024);
-                        const uint64_t bd = sdesc_sw128(b0 + 32u * k, 16, 1024);
-                        mma_f16_ss<1>(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
+                    const uint64_t ad = adesc0 + (uint64_t)((uint32_t)stage * kAStep);
+                    const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kBStep);
+                    if (elect_one()) {
+                        mma_f16_ss<1>(d_tmem, ad, bd, idesc, kb > 0 ? 1u : 0u);
+                        mma_f16_ss<1>(d_tmem, ad + 2, bd + 2, idesc, 1u);
+                        mma_f16_ss<1>(d_tmem, ad + 4, bd + 4, idesc, 1u);
+                        mma_f16_ss<1>(d_tmem, ad + 6, bd + 6, idesc, 1u);
+                        mma_commit(empty0 + 8 * stage);  // frees the stage once these retire
                     }
-                    mma_commit(empty0 + 8 * stage);  // frees the stage once these MMAs retire
+                    __syncwarp();
                     if (++stage == p.stages) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
-                mma_commit(tfull0 + 8 * buf);  // accumulator `buf` is final
+                if (elect_one()) mma_commit(tfull0 + 8 * buf);  // accumulator `buf` is final
+                __syncwarp();
             }
             // drain: nothing may still read shared memory or write TMEM at teardown
             const WaitCtx wd{p.timeout_ns, no_abort, kErrWaitDrain};
-            mma_commit(drain);
-            mbar_wait(drain, 0, wd);
+            if (elect_one()) mma_commit(drain);
+            __syncwarp();
+            mbar_wait_warp(drain, 0, wd);
         }
         __syncwarp();
     } else {
         // -------------------------------- epilogue --------------------------------
         const WaitCtx w{p.timeout_ns, abort_flag, kErrWaitEpilogue};
         const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const uint32_t stage0 = sEpi + (uint32_t)(warp - 2) * 2u * kEpiBoxBytes;
+        const EpiScalars es = epi_scalars(p);
+        const bool acc16 = p.acc_f16 != 0, epi = p.epilogue != 0;
+        uint32_t seq = 0;
         int it = 0;
         for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
             const int buf = it & 1;
@@ -278,19 +438,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             int tm, tn;
             tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
-            const int row = tm * kBM + q * 32 + lane;
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-#pragma unroll 1
-            for (int c = 0; c < BN; c += 32) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tbase + (uint32_t)c, r);
-                tmem_ld_wait();
-                store_row_chunk32(p, row, tn * BN + c, r);
-            }
+            epilogue_rows(p, es, &tmD, tbase, tm * kBM + q * 32, tn * BN, BN, stage0, lane, seq,
+                          acc16, epi);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
         }
+        if (lane == 0) bulk_wait<0>();  // this warp's TMA stores have completed
+        __syncwarp();
     }
 
     __syncthreads();
@@ -299,6 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc<1>(tmem_base, TT::kTmemCols);
     }
+    clock_mark(1);
 }
 
 }  // namespace b2g

@@ -8,11 +8,16 @@
 // in its own TMEM, double-buffered (2 x 256 columns). No TMA multicast is used: each CTA
 // loads its halves itself (this code also runs on multi-GPU jobs).
 //
+// Work list: whole 256 x 256 tiles first, then the tiles of the last, partial wave cut into
+// `tail_split` (2 or 4) column slices of 128 or 64 columns (UMMA 256 x 128 / 256 x 64, B
+// read through a second tensor map with a 64- or 32-row box), so the tail wave keeps every
+// SM pair busy instead of leaving most of them idle. No workspace or reduction is needed.
+//
 // Roles (192 threads per CTA):
 //   warp 0, one thread, both CTAs: TMA producer. Waits for its stage's `empty` barrier,
-//     then loads its A half (128 x 64) and B half (128 x 64). Both CTAs' loads complete
+//     then loads its A half (128 x 64) and B half (width/2 x 64). Both CTAs' loads complete
 //     on the LEADER's `full` barrier, which the leader's producer armed with the pair's
-//     total byte count (2 x 32 KiB).
+//     total byte count.
 //   warp 1, one thread, leader only: MMA issuer. Waits for `full` (both halves landed),
 //     issues 4 x tcgen05.mma.cta_group::2, then a multicast tcgen05.commit that arrives on
 //     the `empty` barrier of the same stage in both CTAs. After the last k-block, a
@@ -33,19 +38,39 @@ constexpr uint32_t kPairStageBytes = 2 * kHalfBytes;  // per CTA: A half + B hal
 constexpr uint32_t kPairTmemCols = 2 * kPairBN;    // double-buffered accumulator
 
 constexpr size_t gemm2_smem_bytes(int stages) {
-    return 1024 + (size_t)stages * kPairStageBytes + sizeof(SmemCtl);
+    return 1024 + (size_t)stages * kPairStageBytes + kEpiBytes + sizeof(SmemCtl);
+}
+
+// Work unit u -> output tile (tm, tn), first output column and width of the unit.
+__device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& tm, int& tn,
+                                          int& n_first, int& width, bool& tail) {
+    int t = u, sub = 0;
+    tail = u >= p.dp_tiles;
+    if (tail) {
+        const int v = u - p.dp_tiles;
+        t = p.dp_tiles + v / p.tail_split;
+        sub = v - (t - p.dp_tiles) * p.tail_split;
+    }
+    tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
+    width = tail ? kPairBN / p.tail_split : kPairBN;
+    n_first = tn * kPairBN + sub * width;
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_sm100_2cta(const __grid_constant__ CUtensorMap tmA,
-                    const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmBt,
+                    const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
+    clock_mark(0);
+    B2G_TIC(t_life);
     extern __shared__ uint8_t smem_dyn[];
     const uint32_t raw = smem_u32(smem_dyn);
     const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
     const uint32_t sA = raw + pad;
     const uint32_t sB = sA + (uint32_t)p.stages * kHalfBytes;
-    SmemCtl* ctl =
-        reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * kPairStageBytes);
+    const uint32_t sEpi = sA + (uint32_t)p.stages * kPairStageBytes;
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad +
+                                              (size_t)p.stages * kPairStageBytes + kEpiBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();
@@ -74,6 +99,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        prefetch_tmap(&tmBt);
+        if (p.d_tma) prefetch_tmap(&tmD);
     }
     if (warp == 1) {
         tmem_alloc<2>(smem_u32(&ctl->tmem_base), kPairTmemCols);
@@ -96,20 +123,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters) {
-                int tm, tn;
-                tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
+            for (int u = cluster_id; u < p.num_units && ok; u += num_clusters) {
+                int tm, tn, n_first, width;
+                bool tail;
+                pair_unit(p, u, tm, tn, n_first, width, tail);
                 const int m0 = tm * kPairBM + (int)rank * 128;
-                const int n0 = tn * kPairBN + (int)rank * 128;
+                const int n0 = n_first + (int)rank * (width >> 1);
+                const CUtensorMap* mapB = tail ? &tmBt : &tmB;
+                // pair total: 2 x (A half 16 KiB + B half width/2 rows x 128 B)
+                const uint32_t bytes = 2u * (kHalfBytes + (uint32_t)(width >> 1) * 128u);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
+                    B2G_TIC(t_empty);
                     if (!mbar_wait<true>(empty0 + 8 * stage, phase ^ 1u, w)) {
                         ok = false;
                         break;
                     }
-                    if (leader) mbar_arrive_expect_tx(full0 + 8 * stage, 2 * kPairStageBytes);
+                    B2G_TOC(0, t_empty);
+                    if (leader) mbar_arrive_expect_tx(full0 + 8 * stage, bytes);
                     const uint32_t fb = full0_leader + 8 * stage;
                     tma_load_2d_pair(sA + stage * kHalfBytes, &tmA, fb, kb * kBK, m0);
-                    tma_load_2d_pair(sB + stage * kHalfBytes, &tmB, fb, kb * kBK, n0);
+                    tma_load_2d_pair(sB + stage * kHalfBytes, mapB, fb, kb * kBK, n0);
                     if (++stage == p.stages) {
                         stage = 0;
                         phase ^= 1u;
@@ -125,77 +158,99 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp == 1) {
-        if (lane == 0 && leader) {
+        if (leader) {
             // ------------------------------- MMA issuer -------------------------------
+            // The whole warp runs the loop (operands stay warp-uniform); one elected lane
+            // issues. Shared-memory descriptors are built once and advanced by adding the
+            // stage offset (and 32 bytes per K step) to the start-address field: every
+            // operand address is below 256 KiB, so the 14-bit field never carries.
             const WaitCtx w{p.timeout_ns, abort_flag, kErrWaitMma};
+            const uint64_t adesc0 = sdesc_sw128(sA, 16, 1024);
+            const uint64_t bdesc0 = sdesc_sw128(sB, 16, 1024);
+            constexpr uint32_t kStageStep = kHalfBytes >> 4;  // descriptor units per stage
             int stage = 0;
             uint32_t phase = 0;
             int it = 0;
             bool ok = true;
-            for (int t = cluster_id; t < p.num_tiles && ok; t += num_clusters, ++it) {
+            for (int u = cluster_id; u < p.num_units && ok; u += num_clusters, ++it) {
+                const uint32_t idesc = u >= p.dp_tiles ? p.idesc_tail : p.idesc;
                 const int buf = it & 1;
                 const uint32_t use = (uint32_t)(it >> 1) & 1u;
-                if (!mbar_wait<true>(tempty0 + 8 * buf, use ^ 1u, w)) {
+                B2G_TIC(t_te);
+                if (!mbar_wait_warp<true>(tempty0 + 8 * buf, use ^ 1u, w)) {
                     ok = false;
                     break;
                 }
+                B2G_TOC(2, t_te);
+                B2G_COUNT(7, 1);
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kPairBN);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
-                    if (!mbar_wait<true>(full0 + 8 * stage, phase, w)) {
+                    B2G_TIC(t_full);
+                    if (!mbar_wait_warp(full0 + 8 * stage, phase, w)) {
                         ok = false;
                         break;
                     }
-                    tc_fence_after();
-                    const uint32_t a0 = sA + stage * kHalfBytes;
-                    const uint32_t b0 = sB + stage * kHalfBytes;
-#pragma unroll
-                    for (int k = 0; k < kBK / kUmmaK; ++k) {
-                        const uint64_t ad = sdesc_sw128(a0 + 32u * k, 16, 1024);
-                        const uint64_t bd = sdesc_sw128(b0 + 32u * k, 16, 1024);
-                        mma_f16_ss<2>(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
+                    B2G_TOC(1, t_full);
+                    B2G_COUNT(6, 1);
+                    const uint64_t ad = adesc0 + (uint64_t)((uint32_t)stage * kStageStep);
+                    const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kStageStep);
+                    if (elect_one()) {
+                        mma_f16_ss<2>(d_tmem, ad, bd, idesc, kb > 0 ? 1u : 0u);
+                        mma_f16_ss<2>(d_tmem, ad + 2, bd + 2, idesc, 1u);
+                        mma_f16_ss<2>(d_tmem, ad + 4, bd + 4, idesc, 1u);
+                        mma_f16_ss<2>(d_tmem, ad + 6, bd + 6, idesc, 1u);
+                        mma_commit_pair(empty0 + 8 * stage, 0x3);  // frees the stage in both CTAs
                     }
-                    mma_commit_pair(empty0 + 8 * stage, 0x3);  // frees the stage in both CTAs
+                    __syncwarp();
                     if (++stage == p.stages) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
-                mma_commit_pair(tfull0 + 8 * buf, 0x3);  // accumulator final in both CTAs
+                if (elect_one()) mma_commit_pair(tfull0 + 8 * buf, 0x3);  // final in both CTAs
+                __syncwarp();
             }
             const WaitCtx wd{p.timeout_ns, no_abort, kErrWaitDrain};
-            mma_commit_2(drain);
-            mbar_wait<true>(drain, 0, wd);
+            if (elect_one()) mma_commit_2(drain);
+            __syncwarp();
+            mbar_wait_warp<true>(drain, 0, wd);
         }
         __syncwarp();
     } else {
         // -------------------------------- epilogue --------------------------------
         const WaitCtx w{p.timeout_ns, abort_flag, kErrWaitEpilogue};
         const int q = warp & 3;
+        const uint32_t stage0 = sEpi + (uint32_t)(warp - 2) * 2u * kEpiBoxBytes;
+        const EpiScalars es = epi_scalars(p);
+        const bool acc16 = p.acc_f16 != 0, epi = p.epilogue != 0;
+        uint32_t seq = 0;
         int it = 0;
-        for (int t = cluster_id; t < p.num_tiles; t += num_clusters, ++it) {
+        for (int u = cluster_id; u < p.num_units; u += num_clusters, ++it) {
             const int buf = it & 1;
             const uint32_t use = (uint32_t)(it >> 1) & 1u;
+            B2G_TIC(t_tf);
             const bool ok = mbar_wait<true>(tfull0 + 8 * buf, use, w);
             if (!__all_sync(0xffffffffu, ok)) break;
+            if (warp == 2 && lane == 0) B2G_TOC(3, t_tf);
             tc_fence_after();
-            int tm, tn;
-            tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
-            const int row = tm * kPairBM + (int)rank * 128 + q * 32 + lane;
+            int tm, tn, n_first, width;
+            bool tail;
+            pair_unit(p, u, tm, tn, n_first, width, tail);
+            const int row0 = tm * kPairBM + (int)rank * 128 + q * 32;
             const uint32_t tbase =
                 tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kPairBN);
-#pragma unroll 1
-            for (int c = 0; c < kPairBN; c += 32) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tbase + (uint32_t)c, r);
-                tmem_ld_wait();
-                store_row_chunk32(p, row, tn * kPairBN + c, r);
-            }
+            B2G_TIC(t_epi);
+            epilogue_rows(p, es, &tmD, tbase, row0, n_first, width, stage0, lane, seq, acc16,
+                          epi);
+            if (warp == 2 && lane == 0) B2G_TOC(4, t_epi);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_remote(tempty0_leader + 8 * buf);
         }
+        if (lane == 0) bulk_wait<0>();  // this warp's TMA stores have completed
+        __syncwarp();
     }
 
     // teardown: no CTA may leave while its peer can still signal its barriers or while
@@ -208,6 +263,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after();
         tmem_dealloc<2>(tmem_base, kPairTmemCols);
     }
+    if (threadIdx.x == 0) B2G_TOC(5, t_life);
+    clock_mark(1);
 }
 
 }  // namespace b2g

@@ -122,6 +122,40 @@ __device__ __forceinline__ void raise_status(uint32_t bits) {
     atomicOr(&g_b2g_status, bits);
 }
 
+// Clock telemetry of the last GEMM launch, written by CTA 0 of the grid:
+// [0] globaltimer at start (ns), [1] at exit, [2] clock64 at start, [3] at exit.
+// (clock64 delta / globaltimer delta = the SM clock the kernel actually ran at.)
+__device__ unsigned long long g_b2g_clock[4];
+
+__device__ __forceinline__ void clock_mark(int at_exit) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        g_b2g_clock[at_exit] = globaltimer_ns();
+        g_b2g_clock[2 + at_exit] = (unsigned long long)clock64();
+    }
+}
+
+// Optional wait-time instrumentation (build with -DB2G_INSTRUMENT; off in the library):
+// per CTA, clock64 cycles each role spent inside its barrier waits, plus the CTA's
+// lifetime. Slots: 0 producer/empty, 1 MMA/full, 2 MMA/tmem_empty, 3 epilogue/tmem_full
+// (warp 2), 4 epilogue work (warp 2), 5 CTA lifetime, 6 k-blocks issued, 7 units;
+// epilogue chunk phases of thread 64 (warp 2, lane 0): 8 TMEM load + wait, 9 convert +
+// shared stores, 10 wait for the staging box, 11 fence + store issue, 12 chunks.
+#ifdef B2G_INSTRUMENT
+constexpr int kInstrSlots = 16;
+__device__ unsigned long long g_b2g_instr[1024][kInstrSlots];
+#define B2G_TIC(v) const long long v = clock64()
+#define B2G_TOC(slot, v) \
+    atomicAdd(&g_b2g_instr[blockIdx.x][slot], (unsigned long long)(clock64() - (v)))
+#define B2G_COUNT(slot, n) atomicAdd(&g_b2g_instr[blockIdx.x][slot], (unsigned long long)(n))
+#define B2G_TOC64(slot, v) \
+    if (threadIdx.x == 64) B2G_TOC(slot, v)
+#else
+#define B2G_TOC64(slot, v)
+#define B2G_TIC(v)
+#define B2G_TOC(slot, v)
+#define B2G_COUNT(slot, n)
+#endif
+
 // Waits until the phase with parity `parity` of `bar` has completed. Returns false if the
 // CTA is aborting or the time limit ran out (then it sets the status bit and the abort
 // flag so the other roles unwind too). CLUSTER selects cluster-scope acquire.
@@ -142,6 +176,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
             }
         }
     }
+}
+
+// One lane of the (converged) warp gets true. Role loops run on whole warps and issue their
+// single-thread instructions (tcgen05.mma / commit, TMA) from the elected lane, so their
+// operands stay warp-uniform (uniform datapath) instead of being rebuilt per issue.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(pred));
+    return pred != 0;
+}
+
+// Bounded wait by a whole warp: every lane polls, the warp agrees on the outcome.
+template <bool CLUSTER = false>
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, const WaitCtx& w) {
+    const bool ok = mbar_wait<CLUSTER>(bar, parity, w);
+    return __all_sync(0xffffffffu, ok);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -170,6 +222,37 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1)
         : "memory");
+}
+
+// 2D tile store from this CTA's shared memory (bulk async-group completion). The tensor map
+// clips rows / columns outside the tensor; callers never start a store at a negative
+// coordinate.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, uint32_t src, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(tm)),
+        "r"(src), "r"(c0), "r"(c1)
+        : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// at most N of this thread's bulk groups may still be reading their shared memory source
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// at most N of this thread's bulk groups may still be in flight at all
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+                 "r"(d)
+                 : "memory");
 }
 
 // ---------------------------------------------------------------------------------------
@@ -295,6 +378,12 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
           "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
           "=r"(r[31])
         : "r"(taddr));
+}
+
+// 64 consecutive columns: two 32-column loads into one 64-register array.
+__device__ __forceinline__ void tmem_ld_32x32b_x64(uint32_t taddr, uint32_t (&r)[64]) {
+    tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+    tmem_ld_32x32b_x32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
 }
 
 __device__ __forceinline__ void tmem_ld_wait() {

@@ -68,7 +68,7 @@ def parse():
     p.add_argument("--workload", choices=tuple(WORKLOADS), default="headline")
     p.add_argument("--tile", type=int, default=-1)
     p.add_argument("--stages", type=int, default=0)
-    p.add_argument("--group", type=int, default=8)
+    p.add_argument("--group", type=int, default=0, help="0 = chosen from the L2 size")
     p.add_argument("--e2e-steps", type=int, default=0, help="0 = min(steps, 20)")
     p.add_argument("--cpu-seconds", type=float, default=10.0,
                    help="target CPU time of the bounded cpu_baseline sample")
@@ -279,6 +279,9 @@ def run_ours(args):
     ms = timed("ours", args.steps, args.warmup, sampler)
     sampler.stop()
     clocks = sampler.summary(sampler.t0, sampler.t1)
+    # the SM clock the last timed launch actually ran at (clock64 / globaltimer in CTA 0)
+    kmhz, _ = b2g.kernel_clock()
+    clocks["kernel_sm_mhz"] = round(kmhz, 1)
 
     # correctness of the timed output against cuBLAS (device max-rel, reference metric)
     dA, dB, dD = sets[(args.steps - 1) % nbuf]
@@ -362,7 +365,8 @@ def run_ours(args):
     kernel_key = f"gemm_sm100_{args.workload}"
     traffic, traffic_src = traffic_from_profiles(kernel_key)
     sms = torch.cuda.get_device_properties(local).multi_processor_count
-    sm_mhz = clocks.get("sm_mhz") or peaks.get("clocks_under_load", {}).get("sm_mhz_median")
+    sm_mhz = (clocks.get("kernel_sm_mhz") or clocks.get("sm_mhz")
+              or peaks.get("clocks_under_load", {}).get("sm_mhz_median"))
     probe_peak = probe_fpc * sms * sm_mhz * 1e6 / 1e12 if sm_mhz else None
     value = flop_job * args.steps / (ms * 1e-3) / 1e12
     h2d = 2 * (rows * K + N * K)

@@ -74,7 +74,8 @@ enum {
  *   alpha    : epilogue scale (reference passes 1.0f, src/gemm_bench.cu:482)
  *   tile     : B2G_TILE_* ; stages: shared-memory ring depth, 0 = deepest that fits
  *   group    : L2 rasterization, `group` M-tiles walked column-major (1 = row-major),
- *              same mapping as src/gemm_bench.cu:237-250
+ *              same mapping as src/gemm_bench.cu:237-250; 0 = the largest band whose A
+ *              rows fill under ~45% of the L2
  * Requirements: A, B 16-byte aligned; lda, ldb multiples of 8 elements (TMA strides are
  * multiples of 16 bytes). D and ldd have no alignment rule (unaligned D takes a scalar
  * store path). M, N, K >= 0; K == 0 writes the epilogue of a zero accumulator.
@@ -92,6 +93,13 @@ const char* b2g_last_error(void);
  * B2G_ERR_TIMEOUT if any kernel of this library gave up a bounded wait since the last
  * call (the message names the role and barrier), B2G_ERR_CUDA on a CUDA error. */
 int b2g_sync_status(void* stream);
+
+/* Clock telemetry of the most recent GEMM launch on the current device (call after the
+ * launch completed, e.g. after b2g_sync_status): CTA 0 records globaltimer and clock64 at
+ * entry and exit, so *sm_mhz = clock cycles / nanoseconds is the SM clock the kernel ran
+ * at and *cta0_us the lifetime of CTA 0. No counterpart in the reference, which reads
+ * clocks from nvidia-smi in its scripts (scripts/soak.ps1:38-62). */
+int b2g_kernel_clock(double* sm_mhz, double* cta0_us);
 
 /* Static properties of a configuration, for the report table columns the reference prints
  * from run_cfg (src/gemm_bench.cu:458-472): threads per CTA, registers per thread, dynamic

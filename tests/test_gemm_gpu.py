@@ -58,6 +58,26 @@ def test_tiles_stages_groups(cuda, tile, stages, group):
     assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
 
 
+@pytest.mark.parametrize("shape", [(1024, 1024, 512), (300, 520, 200), (4096, 4096, 256),
+                                   (2304, 4352, 128), (512, 300, 64)])
+def test_pair_tail_slices(cuda, shape):
+    """2-CTA kernel shapes whose last partial wave is cut into 128- or 64-column slices
+    (including slices that lie wholly beyond N)."""
+    M, N, K = shape
+    A, B, _ = inputs(M, N, K, seed=13)
+    D = run(cuda, A, B, tile=b2g.TILE_256x256_2SM)
+    frob, maxrel = check_rows(A, B, D, sample_rows(M, 128))
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+def test_kernel_clock_telemetry(cuda):
+    A, B, _ = inputs(1024, 1024, 1024, seed=14)
+    run(cuda, A, B)
+    mhz, us = b2g.kernel_clock()
+    print(f"kernel clock {mhz:.0f} MHz over {us:.1f} us")
+    assert 500 < mhz < 2500 and us > 0
+
+
 def test_headline_4096_fp32acc(cuda):
     """4096^3, seed 1, U[-1,1], FP32 accumulation."""
     A, B, _ = inputs(4096, 4096, 4096, seed=1)
