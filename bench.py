@@ -80,12 +80,6 @@ def parse():
 # ---------------------------------------------------------------------------------------
 # helpers
 # ---------------------------------------------------------------------------------------
-def panel(M, world, rank):
-    """Rows [r0, r1) of rank `rank` when M rows are split as evenly as possible."""
-    r0 = M * rank // world
-    r1 = M * (rank + 1) // world
-    return r0, r1
-
 
 def measured_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -195,6 +189,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     import b2g
+    from b2g.shard import max_over_ranks, panel
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -264,12 +259,7 @@ def run_ours(args):
             sampler.mark("t1")
         barrier()
         b2g.sync_status(sptr)
-        ms = e0.elapsed_time(e1)
-        if world > 1:
-            t = torch.tensor([ms], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return max_over_ranks(e0.elapsed_time(e1), dev)
 
     # tcgen05 issue-rate probe (FLOP/clk/SM), for the %-of-peak column
     probe_fpc, _ = b2g.probe_tcgen05(1 if acc == b2g.ACC_F16 else 0, 1, 256, 4096)
@@ -317,11 +307,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier()
     b2g.sync_status(sptr)
-    ms_e2e = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms_e2e], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_e2e = float(t.item())
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1), dev)
 
     allgather = None
     if args.allgather and world > 1:
@@ -338,10 +324,7 @@ def run_ours(args):
             dist.all_gather_into_tensor(full, src)
         a1.record(stream)
         torch.cuda.synchronize()
-        ag = a0.elapsed_time(a1) / reps
-        t = torch.tensor([ag], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ag = float(t.item())
+        ag = max_over_ranks(a0.elapsed_time(a1) / reps, dev)
         recv = (world - 1) * rows * N * 2
         allgather = {"ms": ag, "bytes_received_per_gpu": recv, "gbs_per_gpu": recv / (ag * 1e-3) / 1e9}
         del full
