@@ -10,6 +10,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "b2g.h"
@@ -186,27 +187,54 @@ int auto_group(const TileGeom& g, int tiles_m, int K) {
     return grp;
 }
 
+// Programmatic dependent launch (default on; B2G_PDL=0 turns it off): the GEMM's prologue
+// overlaps the previous kernel in the stream, and its griddepcontrol.wait orders all of its
+// global-memory accesses after that kernel. Every GEMM grid is fully co-resident
+// (persistent, <= one CTA per SM), so a dependent grid can never hold SMs this one needs.
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("B2G_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+template <class Kern, class... Args>
+cudaError_t launch_ex(Kern kern, int grid, size_t smem, cudaStream_t s, const Args&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
                 const CUtensorMap& tmBt, const CUtensorMap& tmD, const GemmParams& p,
-                const DeviceInfo& di, size_t smem,
-                cudaStream_t s) {
+                const DeviceInfo& di, size_t smem, cudaStream_t s) {
     if (int rc = ensure_kernel_attrs(tile, di)) return rc;
     int grid = 0;
+    cudaError_t e = cudaSuccess;
     switch (tile) {
         case B2G_TILE_128x128:
             grid = std::min(p.num_tiles, di.sm_count);
-            gemm_sm100_1cta<128><<<grid, kThreads, smem, s>>>(tmA, tmB, tmD, p);
+            e = launch_ex(gemm_sm100_1cta<128>, grid, smem, s, tmA, tmB, tmD, p);
             break;
         case B2G_TILE_128x256:
             grid = std::min(p.num_tiles, di.sm_count);
-            gemm_sm100_1cta<256><<<grid, kThreads, smem, s>>>(tmA, tmB, tmD, p);
+            e = launch_ex(gemm_sm100_1cta<256>, grid, smem, s, tmA, tmB, tmD, p);
             break;
         default:
             grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
-            gemm_sm100_2cta<<<grid, kThreads, smem, s>>>(tmA, tmB, tmBt, tmD, p);
+            e = launch_ex(gemm_sm100_2cta, grid, smem, s, tmA, tmB, tmBt, tmD, p);
             break;
     }
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "GEMM launch (tile %d, grid %d, smem %zu): %s", tile, grid, smem,
                     cudaGetErrorString(e));

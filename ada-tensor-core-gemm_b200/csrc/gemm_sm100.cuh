@@ -322,6 +322,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem_base = ctl->tmem_base;
     volatile int* abort_flag = &ctl->abort;
     volatile int* no_abort = &ctl->never;
+    // everything above overlapped the previous kernel; global memory only from here on
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp == 0) {
         if (lane == 0) {

@@ -115,6 +115,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     volatile int* no_abort = &ctl->never;
     const uint32_t full0_leader = mapa_shared(full0, 0);
     const uint32_t tempty0_leader = mapa_shared(tempty0, 0);
+    // everything above overlapped the previous kernel; global memory only from here on
+    grid_dep_wait();
+    grid_dep_launch();
 
     if (warp == 0) {
         if (lane == 0) {

@@ -178,6 +178,18 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
     }
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization
+// may start while the previous kernel in the stream is still running; `grid_dep_wait`
+// blocks until that kernel has completed and its memory is visible (every thread calls it
+// before its first global-memory access), and `grid_dep_launch` lets the next kernel start
+// its own prologue on SMs this grid frees.
+__device__ __forceinline__ void grid_dep_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dep_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // One lane of the (converged) warp gets true. Role loops run on whole warps and issue their
 // single-thread instructions (tcgen05.mma / commit, TMA) from the elected lane, so their
 // operands stay warp-uniform (uniform datapath) instead of being rebuilt per issue.
