@@ -38,7 +38,7 @@ EXPORTS = (
     "b2g_max_rel_diff", "b2g_bias_relu", "b2g_probe_tcgen05", "b2g_probe_hbm",
     "b2g_fill_lcg_f16", "b2g_fill_uniform_f16", "b2g_tile_coord",
     "b2g_selftest_wait_timeout", "b2g_set_wait_timeout_us", "b2g_version",
-    "b2g_kernel_clock",
+    "b2g_kernel_clock", "b2g_last_launch",
 )
 
 
@@ -99,6 +99,8 @@ def lib():
         L.b2g_version.argtypes = []
         L.b2g_kernel_clock.restype = i
         L.b2g_kernel_clock.argtypes = [C.POINTER(d), C.POINTER(d)]
+        L.b2g_last_launch.restype = i
+        L.b2g_last_launch.argtypes = [ip, ip, ip, ip, ip]
         _lib = L
     return _lib
 
@@ -176,6 +178,14 @@ def config_info(tile: int = TILE_AUTO, stages: int = 0) -> dict:
     vals = [C.c_int() for _ in range(6)]
     _check(lib().b2g_config_info(tile, stages, *[C.byref(v) for v in vals]))
     keys = ("threads", "regs", "smem", "ctas_per_sm", "tmem_cols", "stages")
+    return {k: v.value for k, v in zip(keys, vals)}
+
+
+def last_launch() -> dict:
+    """Grid, threads, tile, stages and work units of this thread's most recent GEMM launch."""
+    vals = [C.c_int() for _ in range(5)]
+    _check(lib().b2g_last_launch(*[C.byref(v) for v in vals]))
+    keys = ("grid", "threads", "tile", "stages", "units")
     return {k: v.value for k, v in zip(keys, vals)}
 
 

@@ -148,7 +148,7 @@ int max_pair_clusters(const DeviceInfo& di, size_t smem) {
     if (di.device < kMaxDevices && cache[di.device] > 0) return cache[di.device];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (di.sm_count / 2), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(kMaxThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_sm100_2cta, &cfg) != cudaSuccess ||
@@ -199,11 +199,30 @@ bool pdl_enabled() {
     return on;
 }
 
+// Epilogue warps of a launch: 8 when K <= 1024 (at most 16 k-blocks per tile: the next
+// tile's mainloop is too short to hide a 4-warp epilogue, and D's writes dominate), else 4.
+// B2G_EPI_WARPS=4 or 8 in the environment forces one (read once per process).
+int epi_warps_for(int num_kb) {
+    static const int forced = [] {
+        const char* e = std::getenv("B2G_EPI_WARPS");
+        return e ? std::atoi(e) : 0;
+    }();
+    if (forced == 4 || forced == 8) return forced;
+    return num_kb <= 16 ? 8 : 4;
+}
+
+// The most recent GEMM launch of this host thread (b2g_last_launch).
+struct LaunchRecord {
+    int grid, threads, tile, stages, units;
+};
+thread_local LaunchRecord g_last_launch = {};
+
 template <class Kern, class... Args>
-cudaError_t launch_ex(Kern kern, int grid, size_t smem, cudaStream_t s, const Args&... args) {
+cudaError_t launch_ex(Kern kern, int grid, int threads, size_t smem, cudaStream_t s,
+                      const Args&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -219,25 +238,27 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
                 const DeviceInfo& di, size_t smem, cudaStream_t s) {
     if (int rc = ensure_kernel_attrs(tile, di)) return rc;
     int grid = 0;
+    const int threads = gemm_threads(epi_warps_for(p.num_kb));
     cudaError_t e = cudaSuccess;
     switch (tile) {
         case B2G_TILE_128x128:
             grid = std::min(p.num_tiles, di.sm_count);
-            e = launch_ex(gemm_sm100_1cta<128>, grid, smem, s, tmA, tmB, tmD, p);
+            e = launch_ex(gemm_sm100_1cta<128>, grid, threads, smem, s, tmA, tmB, tmD, p);
             break;
         case B2G_TILE_128x256:
             grid = std::min(p.num_tiles, di.sm_count);
-            e = launch_ex(gemm_sm100_1cta<256>, grid, smem, s, tmA, tmB, tmD, p);
+            e = launch_ex(gemm_sm100_1cta<256>, grid, threads, smem, s, tmA, tmB, tmD, p);
             break;
         default:
             grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
-            e = launch_ex(gemm_sm100_2cta, grid, smem, s, tmA, tmB, tmBt, tmD, p);
+            e = launch_ex(gemm_sm100_2cta, grid, threads, smem, s, tmA, tmB, tmBt, tmD, p);
             break;
     }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "GEMM launch (tile %d, grid %d, smem %zu): %s", tile, grid, smem,
                     cudaGetErrorString(e));
+    g_last_launch = LaunchRecord{grid, threads, tile, p.stages, p.num_units};
     return B2G_OK;
 }
 
@@ -393,17 +414,29 @@ B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, in
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "cudaFuncGetAttributes: %s", cudaGetErrorString(e));
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel_ptr(tile), kThreads, smem) !=
-        cudaSuccess) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel_ptr(tile), kMaxThreads,
+                                                      smem) != cudaSuccess) {
         cudaGetLastError();
         occ = 0;
     }
-    if (threads) *threads = kThreads;
+    if (threads) *threads = kMaxThreads;
     if (regs) *regs = fa.numRegs;
     if (smem_bytes) *smem_bytes = (int)need;
     if (ctas_per_sm) *ctas_per_sm = occ;
     if (tmem_cols) *tmem_cols = 2 * geom(tile).bn;
     if (stages_used) *stages_used = stages;
+    return B2G_OK;
+}
+
+B2G_EXPORT int b2g_last_launch(int* grid, int* threads, int* tile, int* stages, int* units) {
+    clear_error();
+    const LaunchRecord r = g_last_launch;
+    if (r.grid == 0) return fail(B2G_ERR_ARG, "no GEMM kernel launched on this host thread yet");
+    if (grid) *grid = r.grid;
+    if (threads) *threads = r.threads;
+    if (tile) *tile = r.tile;
+    if (stages) *stages = r.stages;
+    if (units) *units = r.units;
     return B2G_OK;
 }
 

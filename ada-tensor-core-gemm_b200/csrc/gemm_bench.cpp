@@ -355,6 +355,7 @@ int main(int argc, char** argv) {
             rc_all = 1;
             continue;
         }
+        if (a.warmup > 0) b2g_last_launch(nullptr, &thr, nullptr, &st_used, nullptr);
         cudaEvent_t t0, t1;
         CUDA_CHECK(cudaEventCreate(&t0));
         CUDA_CHECK(cudaEventCreate(&t1));

@@ -12,8 +12,9 @@
 //                      reading both operands from shared memory, and tcgen05.commit's the
 //                      stage's `empty` barrier; after the last k-block it commits
 //                      `tmem_full[buf]`.
-//   warps 2-5          epilogue: wait for `tmem_full[buf]`, tcgen05.ld 32 columns at a time
-//                      (warp w reads TMEM lanes 32*(w%4)..+31 = tile rows), apply the
+//   warps 2..          epilogue (4 or 8 warps): wait for `tmem_full[buf]`, tcgen05.ld 64
+//                      columns at a time (warp w reads TMEM lanes 32*(w%4)..+31 = tile
+//                      rows; with 8 warps two share a quarter, alternate chunks), apply the
 //                      optional alpha*acc + bias + ReLU, round to FP16 (RN, as
 //                      __floats2half2_rn in the reference) and store; then arrive on
 //                      `tmem_empty[buf]` so the MMA warp can reuse that accumulator.
@@ -59,13 +60,20 @@ constexpr int kBM = 128;      // rows of A per CTA (UMMA M for cta_group::1)
 constexpr int kBK = 64;       // k-block: one 128-byte swizzle row of FP16
 constexpr int kUmmaK = 16;    // K of one kind::f16 MMA
 constexpr int kMaxStages = 8;
-constexpr int kThreads = 192; // producer warp, MMA warp, 4 epilogue warps
+// Epilogue warps: 4 or 8, chosen at launch (blockDim.x = 64 + 32 x epilogue warps). Warp w
+// may only read TMEM lanes 32*(w%4)..+31, so 4 warps cover the 128 accumulator rows once;
+// with 8, two warps share each lane quarter and take alternate 64-column chunks. That halves
+// the epilogue of a tile, which matters when K is small: the epilogue of tile i must finish
+// within the (short) mainloop of tile i + 1, and D's write traffic dominates.
+constexpr int kMaxEpiWarps = 8;
+constexpr int kMaxThreads = 64 + 32 * kMaxEpiWarps;
+__host__ __device__ constexpr int gemm_threads(int epi_warps) { return 64 + 32 * epi_warps; }
 constexpr uint32_t kAStageBytes = kBM * kBK * 2;  // 16 KiB
-// Epilogue staging for TMA stores: every epilogue warp owns two 32-row x 64-column FP16
-// boxes (4 KiB each, 128-byte swizzle), used alternately so the conversion of one chunk
-// overlaps the bulk store of the previous one.
+// Epilogue staging for TMA stores: eight 32-row x 64-column FP16 boxes (4 KiB each,
+// 128-byte swizzle). With 4 epilogue warps each owns two, used in turn so the conversion of
+// one chunk overlaps the bulk store of the previous one; with 8 warps each owns one.
 constexpr uint32_t kEpiBoxBytes = 32 * 64 * 2;
-constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBoxBytes;  // 4 epilogue warps: 32 KiB
+constexpr uint32_t kEpiBytes = 8 * kEpiBoxBytes;  // 32 KiB
 
 template <int BN>
 struct TileTraits {
@@ -146,10 +154,14 @@ struct EpiScalars {
     float alpha;
     const __half* bias;
     int d_tma;
+    uint64_t store_pol;  // L2 policy of the TMA stores of D: evict_first (D is not re-read)
+    int bufs;            // staging boxes of this warp (2 with 4 epilogue warps, 1 with 8)
+    int c_step;          // 64-column chunk stride of this warp (1 with 4 warps, 2 with 8)
 };
 
-__device__ __forceinline__ EpiScalars epi_scalars(const GemmParams& p) {
-    return EpiScalars{p.M, p.N, p.alpha, p.bias, p.d_tma};
+__device__ __forceinline__ EpiScalars epi_scalars(const GemmParams& p, int epi_warps) {
+    return EpiScalars{p.M, p.N, p.alpha, p.bias, p.d_tma, l2_policy_evict_first(),
+                      8 / epi_warps, epi_warps / 4};
 }
 
 // alpha * acc + bias + ReLU (EPI) and round to FP16, two columns per word; ACC16: the
@@ -191,9 +203,14 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const EpiSca
                                                int row0, int col, uint32_t stage0, int lane,
                                                uint32_t& seq) {
     if (e.d_tma) {
-        const uint32_t box = stage0 + (seq & 1u) * kEpiBoxBytes;
+        const uint32_t box = stage0 + (e.bufs == 2 ? (seq & 1u) : 0u) * kEpiBoxBytes;
         B2G_TIC(t_box);
-        if (lane == 0) bulk_wait_read<1>();  // the store that last read `box` is done
+        if (lane == 0) {  // the store that last read `box` is done
+            if (e.bufs == 2)
+                bulk_wait_read<1>();
+            else
+                bulk_wait_read<0>();
+        }
         __syncwarp();
         B2G_TOC64(10, t_box);
         B2G_TIC(t_cvt);
@@ -215,7 +232,7 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const EpiSca
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-            tma_store_2d(tmD, box, col, row0);
+            tma_store_2d_hint(tmD, box, col, row0, e.store_pol);
             bulk_commit();
         }
         B2G_TOC64(11, t_st);
@@ -230,11 +247,11 @@ __device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const EpiSca
 template <bool ACC16, bool EPI>
 __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiScalars& e,
                                                 const CUtensorMap* tmD, uint32_t trow, int row0,
-                                                int n_first, int nchunks, uint32_t stage0,
-                                                int lane, uint32_t& seq) {
+                                                int n_first, int nchunks, int c_first,
+                                                uint32_t stage0, int lane, uint32_t& seq) {
     uint32_t r[64];
 #pragma unroll 1
-    for (int c = 0; c < nchunks; ++c) {
+    for (int c = c_first; c < nchunks; c += e.c_step) {
         B2G_TIC(t_ld);
         tmem_ld_32x32b_x64(trow + (uint32_t)c * 64u, r);
         tmem_ld_wait();
@@ -246,31 +263,38 @@ __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiSc
 
 // Epilogue of one warp: its 32 rows [row0, row0 + 32) x columns [n_first, n_first + width)
 // (width <= 256) of the accumulator at TMEM address `trow` (lane quarter and buffer
-// applied), 64 columns at a time. `seq` counts this warp's issued TMA stores.
+// applied), 64 columns at a time: chunks c_first, c_first + e.c_step, ... (with 8 epilogue
+// warps the other warp of the lane quarter takes the rest). `seq` counts this warp's issued
+// TMA stores.
 __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiScalars& e,
                                               const CUtensorMap* tmD, uint32_t trow, int row0,
-                                              int n_first, int width, uint32_t stage0,
-                                              int lane, uint32_t& seq, bool acc16, bool epi) {
+                                              int n_first, int width, int c_first,
+                                              uint32_t stage0, int lane, uint32_t& seq,
+                                              bool acc16, bool epi) {
     if (row0 >= e.M) return;  // all 32 rows outside D (uniform in the warp)
     int nchunks = (width + 63) / 64;
     const int in_n = (e.N - n_first + 63) / 64;  // chunks that start inside D
     if (in_n < nchunks) nchunks = in_n;
-    if (nchunks <= 0) return;
+    if (nchunks <= c_first) return;
     if (acc16) {
         if (epi)
-            epilogue_rows_t<true, true>(p, e, tmD, trow, row0, n_first, nchunks, stage0, lane, seq);
+            epilogue_rows_t<true, true>(p, e, tmD, trow, row0, n_first, nchunks, c_first, stage0,
+                                        lane, seq);
         else
-            epilogue_rows_t<true, false>(p, e, tmD, trow, row0, n_first, nchunks, stage0, lane, seq);
+            epilogue_rows_t<true, false>(p, e, tmD, trow, row0, n_first, nchunks, c_first, stage0,
+                                         lane, seq);
     } else {
         if (epi)
-            epilogue_rows_t<false, true>(p, e, tmD, trow, row0, n_first, nchunks, stage0, lane, seq);
+            epilogue_rows_t<false, true>(p, e, tmD, trow, row0, n_first, nchunks, c_first, stage0,
+                                         lane, seq);
         else
-            epilogue_rows_t<false, false>(p, e, tmD, trow, row0, n_first, nchunks, stage0, lane, seq);
+            epilogue_rows_t<false, false>(p, e, tmD, trow, row0, n_first, nchunks, c_first,
+                                          stage0, lane, seq);
     }
 }
 
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_1cta(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
@@ -287,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                               kEpiBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
     const uint32_t full0 = smem_u32(&ctl->full[0]);
     const uint32_t empty0 = smem_u32(&ctl->empty[0]);
     const uint32_t tfull0 = smem_u32(&ctl->tmem_full[0]);
@@ -300,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull0 + 8 * b, 1);
-            mbar_init(tempty0 + 8 * b, 4);  // one arrive per epilogue warp
+            mbar_init(tempty0 + 8 * b, (uint32_t)epi_warps);  // one arrive per epilogue warp
         }
         mbar_init(drain, 1);
         ctl->abort = 0;
@@ -428,8 +453,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // -------------------------------- epilogue --------------------------------
         const WaitCtx w{p.timeout_ns, abort_flag, kErrWaitEpilogue};
         const int q = warp & 3;  // TMEM lane quarter this warp may access
-        const uint32_t stage0 = sEpi + (uint32_t)(warp - 2) * 2u * kEpiBoxBytes;
-        const EpiScalars es = epi_scalars(p);
+        const int c_first = (warp - 2) >> 2;  // first 64-column chunk of this warp
+        const EpiScalars es = epi_scalars(p, epi_warps);
+        const uint32_t stage0 = sEpi + (uint32_t)((warp - 2) * es.bufs) * kEpiBoxBytes;
         const bool acc16 = p.acc_f16 != 0, epi = p.epilogue != 0;
         uint32_t seq = 0;
         int it = 0;
@@ -442,8 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int tm, tn;
             tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-            epilogue_rows(p, es, &tmD, tbase, tm * kBM + q * 32, tn * BN, BN, stage0, lane, seq,
-                          acc16, epi);
+            epilogue_rows(p, es, &tmD, tbase, tm * kBM + q * 32, tn * BN, BN, c_first, stage0,
+                          lane, seq, acc16, epi);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(tempty0 + 8 * buf);

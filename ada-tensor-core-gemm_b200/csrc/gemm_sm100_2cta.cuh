@@ -13,7 +13,7 @@
 // read through a second tensor map with a 64- or 32-row box), so the tail wave keeps every
 // SM pair busy instead of leaving most of them idle. No workspace or reduction is needed.
 //
-// Roles (192 threads per CTA):
+// Roles (64 + 32 x 4 or 8 epilogue warps threads per CTA):
 //   warp 0, one thread, both CTAs: TMA producer. Waits for its stage's `empty` barrier,
 //     then loads its A half (128 x 64) and B half (width/2 x 64). Both CTAs' loads complete
 //     on the LEADER's `full` barrier, which the leader's producer armed with the pair's
@@ -22,8 +22,8 @@
 //     issues 4 x tcgen05.mma.cta_group::2, then a multicast tcgen05.commit that arrives on
 //     the `empty` barrier of the same stage in both CTAs. After the last k-block, a
 //     multicast commit on `tmem_full[buf]` of both CTAs.
-//   warps 2-5, both CTAs: epilogue of this CTA's 128 rows (same as the 1-CTA kernel),
-//     then one arrive per warp on the leader's `tmem_empty[buf]` (count 8).
+//   warps 2.., both CTAs: epilogue of this CTA's 128 rows (same as the 1-CTA kernel),
+//     then one arrive per warp on the leader's `tmem_empty[buf]` (count 2 x epilogue warps).
 // Barrier waits are cluster-scope acquires (their arrivals come from the peer SM).
 #pragma once
 
@@ -56,7 +56,7 @@ __device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& tm, i
     n_first = tn * kPairBN + sub * width;
 }
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_2cta(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmBt,
@@ -73,6 +73,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                               (size_t)p.stages * kPairStageBytes + kEpiBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
     const int cluster_id = blockIdx.x >> 1, num_clusters = gridDim.x >> 1;
@@ -89,7 +90,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull0 + 8 * b, 1);
-            mbar_init(tempty0 + 8 * b, 8);  // 4 epilogue warps x 2 CTAs (leader's copy)
+            mbar_init(tempty0 + 8 * b, 2u * epi_warps);  // epilogue warps x 2 CTAs (leader's copy)
         }
         mbar_init(drain, 1);
         ctl->abort = 0;
@@ -184,8 +185,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     ok = false;
                     break;
                 }
-                B2G_TOC(2, t_te);
-                B2G_COUNT(7, 1);
+                if (lane == 0) B2G_TOC(2, t_te);
+                if (lane == 0) B2G_COUNT(7, 1);
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kPairBN);
                 for (int kb = 0; kb < p.num_kb; ++kb) {
@@ -194,8 +195,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    B2G_TOC(1, t_full);
-                    B2G_COUNT(6, 1);
+                    if (lane == 0) B2G_TOC(1, t_full);
+                    if (lane == 0) B2G_COUNT(6, 1);
                     const uint64_t ad = adesc0 + (uint64_t)((uint32_t)stage * kStageStep);
                     const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kStageStep);
                     if (elect_one()) {
@@ -225,8 +226,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // -------------------------------- epilogue --------------------------------
         const WaitCtx w{p.timeout_ns, abort_flag, kErrWaitEpilogue};
         const int q = warp & 3;
-        const uint32_t stage0 = sEpi + (uint32_t)(warp - 2) * 2u * kEpiBoxBytes;
-        const EpiScalars es = epi_scalars(p);
+        const int c_first = (warp - 2) >> 2;
+        const EpiScalars es = epi_scalars(p, epi_warps);
+        const uint32_t stage0 = sEpi + (uint32_t)((warp - 2) * es.bufs) * kEpiBoxBytes;
         const bool acc16 = p.acc_f16 != 0, epi = p.epilogue != 0;
         uint32_t seq = 0;
         int it = 0;
@@ -245,8 +247,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const uint32_t tbase =
                 tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kPairBN);
             B2G_TIC(t_epi);
-            epilogue_rows(p, es, &tmD, tbase, row0, n_first, width, stage0, lane, seq, acc16,
-                          epi);
+            epilogue_rows(p, es, &tmD, tbase, row0, n_first, width, c_first, stage0, lane, seq,
+                          acc16, epi);
             if (warp == 2 && lane == 0) B2G_TOC(4, t_epi);
             tc_fence_before();
             __syncwarp();

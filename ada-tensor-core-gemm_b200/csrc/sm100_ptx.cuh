@@ -236,6 +236,47 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
         : "memory");
 }
 
+// L2 cache policies (createpolicy) for the `.L2::cache_hint` forms below.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const CUtensorMap* tm,
+                                                 uint32_t bar, int c0, int c1, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1), "l"(pol)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst, const CUtensorMap* tm,
+                                                      uint32_t bar, int c0, int c1,
+                                                      uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1), "l"(pol)
+        : "memory");
+}
+
+// 2D tile store with an L2 cache policy (e.g. evict_first for output that is not re-read).
+__device__ __forceinline__ void tma_store_2d_hint(const CUtensorMap* tm, uint32_t src, int c0,
+                                                  int c1, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group.L2::cache_hint"
+        " [%0, {%2, %3}], [%1], %4;" ::"l"(reinterpret_cast<uint64_t>(tm)),
+        "r"(src), "r"(c0), "r"(c1), "l"(pol)
+        : "memory");
+}
+
 // 2D tile store from this CTA's shared memory (bulk async-group completion). The tensor map
 // clips rows / columns outside the tensor; callers never start a store at a negative
 // coordinate.

@@ -102,11 +102,20 @@ int b2g_sync_status(void* stream);
 int b2g_kernel_clock(double* sm_mhz, double* cta0_us);
 
 /* Static properties of a configuration, for the report table columns the reference prints
- * from run_cfg (src/gemm_bench.cu:458-472): threads per CTA, registers per thread, dynamic
- * shared memory bytes, resident CTAs per SM, TMEM columns, and the stage count used when
- * `stages` is 0. Any output pointer may be NULL. */
+ * from run_cfg (src/gemm_bench.cu:458-472): threads per CTA (the maximum, 320: a launch uses
+ * 192 or 320, see b2g_last_launch), registers per thread, dynamic shared memory bytes,
+ * resident CTAs per SM, TMEM columns, and the stage count used when `stages` is 0. Any
+ * output pointer may be NULL. */
 int b2g_config_info(int tile, int stages, int* threads, int* regs, int* smem_bytes,
                     int* ctas_per_sm, int* tmem_cols, int* stages_used);
+
+/* The most recent GEMM kernel launch made by b2g_gemm on the calling host thread: grid
+ * size, threads per CTA (64 + 32 x epilogue warps: 8 epilogue warps when K <= 1024, else
+ * 4), the tile and stage count chosen, and the work units (tiles plus tail slices). The
+ * reference prints the same launch facts per configuration (src/gemm_bench.cu:458-472);
+ * here they depend on the shape, so they are read back after the call. Any output pointer
+ * may be NULL; B2G_ERR_ARG if this thread has not launched a GEMM yet. */
+int b2g_last_launch(int* grid, int* threads, int* tile, int* stages, int* units);
 
 /* cuBLAS comparison column: exactly the reference's call (src/gemm_bench.cu:625-633):
  * cublasGemmEx(OP_T, OP_N, N, M, K, alpha, B, 16F, K, A, 16F, K, beta=0, D, 16F, N,

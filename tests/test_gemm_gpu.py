@@ -70,6 +70,33 @@ def test_pair_tail_slices(cuda, shape):
     assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
 
 
+@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM])
+@pytest.mark.parametrize("K,warps", [(1024, 8), (1088, 4), (64, 8)])
+@pytest.mark.parametrize("mode", ["plain", "fused", "f16acc"])
+def test_epilogue_warps_by_k(cuda, tile, K, warps, mode):
+    """K <= 1024 launches 8 epilogue warps (two per TMEM lane quarter, alternate 64-column
+    chunks, one staging box each), longer K launches 4 (two boxes each); both give the same
+    result in every epilogue mode, including the 128-column tail slices of the 2-CTA kernel."""
+    M, N = 640, 704
+    A, B, bias = inputs(M, N, K, seed=21, lo=-0.5, hi=0.5)
+    kw = {}
+    if mode == "fused":
+        kw = dict(epilogue=b2g.EPI_BIAS_RELU, alpha=0.75)
+    elif mode == "f16acc":
+        kw = dict(acc=b2g.ACC_F16)
+    D = run(cuda, A, B, bias if mode == "fused" else None, tile=tile, **kw)
+    launch = b2g.last_launch()
+    assert launch["threads"] == 64 + 32 * warps, launch
+    assert launch["tile"] == tile
+    rows = sample_rows(M, 96)
+    frob, maxrel = check_rows(A, B, D, rows, bias=bias if mode == "fused" else None,
+                              alpha=kw.get("alpha", 1.0), epilogue=mode == "fused")
+    tol = FROB_F16 if mode == "f16acc" else FROB_F32
+    assert frob <= tol, (frob, maxrel)
+    if mode != "f16acc":
+        assert maxrel <= ELEM_F32, (frob, maxrel)
+
+
 def test_kernel_clock_telemetry(cuda):
     A, B, _ = inputs(1024, 1024, 1024, seed=14)
     run(cuda, A, B)
