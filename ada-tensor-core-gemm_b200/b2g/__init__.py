@@ -38,7 +38,7 @@ EXPORTS = (
     "b2g_max_rel_diff", "b2g_bias_relu", "b2g_probe_tcgen05", "b2g_probe_hbm",
     "b2g_fill_lcg_f16", "b2g_fill_uniform_f16", "b2g_tile_coord",
     "b2g_selftest_wait_timeout", "b2g_set_wait_timeout_us", "b2g_version",
-    "b2g_kernel_clock", "b2g_last_launch",
+    "b2g_kernel_clock", "b2g_last_launch", "b2g_gemm_splitk",
 )
 
 
@@ -68,6 +68,9 @@ def lib():
         vp, i, ll, f, d = C.c_void_p, C.c_int, C.c_longlong, C.c_float, C.c_double
         L.b2g_gemm.restype = i
         L.b2g_gemm.argtypes = [vp, vp, vp, vp, i, i, i, ll, ll, ll, i, i, i, f, i, i, i, vp]
+        L.b2g_gemm_splitk.restype = i
+        L.b2g_gemm_splitk.argtypes = [vp, vp, vp, vp, i, i, i, ll, ll, ll, i, i, i, f, i, i, i,
+                                      i, vp]
         L.b2g_last_error.restype = C.c_char_p
         L.b2g_last_error.argtypes = []
         L.b2g_sync_status.restype = i
@@ -100,7 +103,7 @@ def lib():
         L.b2g_kernel_clock.restype = i
         L.b2g_kernel_clock.argtypes = [C.POINTER(d), C.POINTER(d)]
         L.b2g_last_launch.restype = i
-        L.b2g_last_launch.argtypes = [ip, ip, ip, ip, ip]
+        L.b2g_last_launch.argtypes = [ip, ip, ip, ip, ip, ip]
         _lib = L
     return _lib
 
@@ -143,15 +146,23 @@ def _stream_ptr(stream) -> int | None:
 def gemm_raw(A: int, B: int, D: int, bias: int | None, M: int, N: int, K: int, lda: int,
              ldb: int, ldd: int, b_layout: int = B_NK, acc: int = ACC_F32,
              epilogue: int = EPI_NONE, alpha: float = 1.0, tile: int = TILE_AUTO,
-             stages: int = 0, group: int = 1, stream: int | None = None) -> None:
-    """Launch D = A * B on raw device pointers (asynchronous). Raises B2GError."""
-    _check(lib().b2g_gemm(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc, epilogue,
-                          alpha, tile, stages, group, stream))
+             stages: int = 0, group: int = 1, stream: int | None = None,
+             splits: int | None = None) -> None:
+    """Launch D = A * B on raw device pointers (asynchronous). Raises B2GError.
+
+    splits None: b2g_gemm (automatic split-K); an int: b2g_gemm_splitk with that factor
+    (0 automatic, 1 none, S >= 2 forced)."""
+    if splits is None:
+        _check(lib().b2g_gemm(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc, epilogue,
+                              alpha, tile, stages, group, stream))
+    else:
+        _check(lib().b2g_gemm_splitk(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc,
+                                     epilogue, alpha, tile, stages, group, splits, stream))
 
 
 def gemm(A, B, D, bias=None, *, b_layout: int = B_NK, acc: int = ACC_F32,
          epilogue: int = EPI_NONE, alpha: float = 1.0, tile: int = TILE_AUTO,
-         stages: int = 0, group: int = 1, stream=None) -> None:
+         stages: int = 0, group: int = 1, stream=None, splits: int | None = None) -> None:
     """D = A * B (+ optional alpha*acc + bias + ReLU) on CUDA FP16 tensors.
 
     A: M x K, B: N x K (b_layout B_NK, the reference's TN layout) or K x N (B_KN),
@@ -166,7 +177,7 @@ def gemm(A, B, D, bias=None, *, b_layout: int = B_NK, acc: int = ACC_F32,
         raise B2GError(ERR_ARG, f"D shape {tuple(D.shape)} != ({M}, {N})")
     gemm_raw(_ptr(A), _ptr(B), _ptr(D), _ptr(bias), M, N, K, A.stride(0), B.stride(0),
              D.stride(0), b_layout, acc, epilogue, alpha, tile, stages, group,
-             _stream_ptr(stream))
+             _stream_ptr(stream), splits)
 
 
 def sync_status(stream=None) -> None:
@@ -182,10 +193,11 @@ def config_info(tile: int = TILE_AUTO, stages: int = 0) -> dict:
 
 
 def last_launch() -> dict:
-    """Grid, threads, tile, stages and work units of this thread's most recent GEMM launch."""
-    vals = [C.c_int() for _ in range(5)]
+    """Grid, threads, tile, stages, work units and split-K factor of this thread's most recent
+    GEMM launch."""
+    vals = [C.c_int() for _ in range(6)]
     _check(lib().b2g_last_launch(*[C.byref(v) for v in vals]))
-    keys = ("grid", "threads", "tile", "stages", "units")
+    keys = ("grid", "threads", "tile", "stages", "units", "splits")
     return {k: v.value for k, v in zip(keys, vals)}
 
 

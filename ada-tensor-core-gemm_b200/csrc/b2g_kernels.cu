@@ -11,7 +11,9 @@
 
 #include <algorithm>
 #include <cstdlib>
+#include <map>
 #include <mutex>
+#include <utility>
 
 #include "b2g.h"
 #include "b2g_internal.h"
@@ -162,16 +164,19 @@ int max_pair_clusters(const DeviceInfo& di, size_t smem) {
 }
 
 // Column-slice factor for the tail tiles of the 2-CTA kernel: the `rest` tiles of the last
-// partial wave become rest * split units of 1/split the work; pick the split (1, 2 or 4)
-// that minimises the tail's duration ceil(rest * split / clusters) / split.
+// partial wave become rest * split units of 1/split the columns; pick the split (1, 2 or 4)
+// that minimises the tail's duration ceil(rest * split / clusters) * cost(split). A slice
+// costs more than 1/split of a tile because every slice reloads the tile's whole A panel
+// (per k-block 16 KiB of A + 128 B x width/2 of B per CTA): measured on B200, a 128-column
+// slice takes ~0.55 and a 64-column slice ~0.4 of a whole tile's time.
 int tail_split_for(int rest, int clusters) {
     int best = 1;
     double best_t = 1.0;
-    for (int split : {2, 4}) {
-        const double t = (double)((rest * split + clusters - 1) / clusters) / split;
+    for (const auto& sc : {std::pair<int, double>{2, 0.55}, std::pair<int, double>{4, 0.40}}) {
+        const double t = (double)((rest * sc.first + clusters - 1) / clusters) * sc.second;
         if (t < best_t - 1e-9) {
             best_t = t;
-            best = split;
+            best = sc.first;
         }
     }
     return best;
@@ -202,18 +207,18 @@ bool pdl_enabled() {
 // Epilogue warps of a launch: 8 when K <= 1024 (at most 16 k-blocks per tile: the next
 // tile's mainloop is too short to hide a 4-warp epilogue, and D's writes dominate), else 4.
 // B2G_EPI_WARPS=4 or 8 in the environment forces one (read once per process).
-int epi_warps_for(int num_kb) {
+int epi_warps_for(int num_kb, int splits) {
     static const int forced = [] {
         const char* e = std::getenv("B2G_EPI_WARPS");
         return e ? std::atoi(e) : 0;
     }();
     if (forced == 4 || forced == 8) return forced;
-    return num_kb <= 16 ? 8 : 4;
+    return (num_kb <= 16 || splits > 1) ? 8 : 4;  // split-K: the reduction wants 8 as well
 }
 
 // The most recent GEMM launch of this host thread (b2g_last_launch).
 struct LaunchRecord {
-    int grid, threads, tile, stages, units;
+    int grid, threads, tile, stages, units, splits;
 };
 thread_local LaunchRecord g_last_launch = {};
 
@@ -238,15 +243,15 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
                 const DeviceInfo& di, size_t smem, cudaStream_t s) {
     if (int rc = ensure_kernel_attrs(tile, di)) return rc;
     int grid = 0;
-    const int threads = gemm_threads(epi_warps_for(p.num_kb));
+    const int threads = gemm_threads(epi_warps_for(p.num_kb, p.splits));
     cudaError_t e = cudaSuccess;
     switch (tile) {
         case B2G_TILE_128x128:
-            grid = std::min(p.num_tiles, di.sm_count);
+            grid = std::min(p.num_units, di.sm_count);
             e = launch_ex(gemm_sm100_1cta<128>, grid, threads, smem, s, tmA, tmB, tmD, p);
             break;
         case B2G_TILE_128x256:
-            grid = std::min(p.num_tiles, di.sm_count);
+            grid = std::min(p.num_units, di.sm_count);
             e = launch_ex(gemm_sm100_1cta<256>, grid, threads, smem, s, tmA, tmB, tmD, p);
             break;
         default:
@@ -258,7 +263,96 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "GEMM launch (tile %d, grid %d, smem %zu): %s", tile, grid, smem,
                     cudaGetErrorString(e));
-    g_last_launch = LaunchRecord{grid, threads, tile, p.stages, p.num_units};
+    g_last_launch = LaunchRecord{grid, threads, tile, p.stages, p.num_units, p.splits};
+    return B2G_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// Split-K
+// ---------------------------------------------------------------------------------------
+// Automatic split factor. Only 1-CTA tiles are split, and only when the tiles fill less
+// than half of the SMs: the S in 1..4 (one wave) minimising a cycle estimate of one unit,
+//   ceil(num_kb / S) k-blocks x ~450 cycles + (S > 1) x ~10500 cycles,
+// the second term being the split overhead measured on B200 for a 128 x 128 tile (partial
+// store ~1.7K, arrival ~3K, the last split's reduction ~5.5K cycles, nearly independent of
+// S <= 4). For 2-CTA pair tiles the overhead is ~3x larger and splitting measured slower on
+// every shape tried, so pairs are never split automatically.
+int splitk_auto(int tiles, int concurrent, int num_kb, int ctas) {
+    if (ctas != 1 || 2 * tiles > concurrent) return 1;
+    int best = 1;
+    double best_t = num_kb * 450.0;
+    for (int s = 2; s <= 4 && tiles * s <= concurrent; ++s) {
+        const double t = ((num_kb + s - 1) / s) * 450.0 + 10500.0;
+        if (t < best_t) {
+            best_t = t;
+            best = s;
+        }
+    }
+    return best;
+}
+
+// Scratch of one split-K launch: FP32 partials, arrival counters and the launch's epoch.
+struct SplitScratch {
+    float* part;
+    unsigned long long* count;
+    unsigned int epoch;
+};
+
+// Library-owned split-K workspace, one per (device, stream) so GEMMs on different streams
+// never share partials or counters; launches on one stream are ordered by the stream.
+// It grows on demand (synchronising the stream first, since in-flight launches may still use
+// the old buffers); growing is refused while the stream is being captured into a graph.
+// Counters need no clearing between launches (epoch tags); a new counter buffer is zeroed.
+struct StreamWorkspace {
+    float* part = nullptr;
+    size_t part_bytes = 0;
+    unsigned long long* count = nullptr;
+    size_t count_entries = 0;
+    unsigned int epoch = 0;
+};
+
+int managed_scratch(const DeviceInfo& di, cudaStream_t s, size_t part_bytes, size_t count_entries,
+                    SplitScratch* out) {
+    static std::mutex mu;
+    static std::map<std::pair<int, cudaStream_t>, StreamWorkspace> spaces;
+    std::lock_guard<std::mutex> lock(mu);
+    StreamWorkspace& w = spaces[{di.device, s}];
+    if (part_bytes > w.part_bytes || count_entries > w.count_entries) {
+        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+        if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+            cudaGetLastError();
+            return fail(B2G_ERR_UNSUPPORTED,
+                        "split-K workspace must grow (to %zu + %zu bytes) while the stream is being "
+                        "captured: run one call of this shape on the stream before capturing",
+                        part_bytes, count_entries * sizeof(unsigned long long));
+        }
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess)
+            return fail(B2G_ERR_CUDA, "split-K workspace: stream synchronize: %s",
+                        cudaGetErrorString(e));
+        if (part_bytes > w.part_bytes) {
+            const size_t bytes = std::max(part_bytes, w.part_bytes * 2);
+            if (w.part) cudaFree(w.part);
+            w.part = nullptr;
+            w.part_bytes = 0;
+            if ((e = cudaMalloc(&w.part, bytes)) != cudaSuccess)
+                return fail(B2G_ERR_CUDA, "split-K workspace: cudaMalloc(%zu): %s", bytes,
+                            cudaGetErrorString(e));
+            w.part_bytes = bytes;
+        }
+        if (count_entries > w.count_entries) {
+            const size_t n = std::max(count_entries, w.count_entries * 2);
+            if (w.count) cudaFree(w.count);
+            w.count = nullptr;
+            w.count_entries = 0;
+            if ((e = cudaMalloc(&w.count, n * sizeof(unsigned long long))) != cudaSuccess ||
+                (e = cudaMemset(w.count, 0, n * sizeof(unsigned long long))) != cudaSuccess)
+                return fail(B2G_ERR_CUDA, "split-K counters (%zu): %s", n, cudaGetErrorString(e));
+            w.count_entries = n;
+        }
+    }
+    if (++w.epoch == 0) w.epoch = 1;
+    *out = SplitScratch{w.part, w.count, w.epoch};
     return B2G_OK;
 }
 
@@ -276,11 +370,14 @@ using namespace b2g;
 // ---------------------------------------------------------------------------------------
 // GEMM
 // ---------------------------------------------------------------------------------------
-B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias, int M, int N,
-                        int K, long long lda, long long ldb, long long ldd, int b_layout,
-                        int acc, int epilogue, float alpha, int tile, int stages, int group,
-                        void* stream) {
-    clear_error();
+namespace b2g {
+namespace {
+
+// Everything of b2g_gemm / b2g_gemm_splitk after argument decoding. `splits`: 0 = automatic,
+// 1 = no split-K, >= 2 = that many K splits (FP32 accumulation only).
+int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, int N, int K,
+              long long lda, long long ldb, long long ldd, int b_layout, int acc, int epilogue,
+              float alpha, int tile, int stages, int group, int splits, cudaStream_t s) {
     if (M < 0 || N < 0 || K < 0)
         return fail(B2G_ERR_ARG, "negative shape M=%d N=%d K=%d", M, N, K);
     if (b_layout != B2G_B_NK && b_layout != B2G_B_KN)
@@ -295,6 +392,11 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
     if (stages != 0 && (stages < 2 || stages > kMaxStages))
         return fail(B2G_ERR_ARG, "stages must be 0 (auto) or 2..%d, got %d", kMaxStages, stages);
     if (group < 0) return fail(B2G_ERR_ARG, "group must be >= 0, got %d", group);
+    if (splits < 0) return fail(B2G_ERR_ARG, "splits must be >= 0, got %d", splits);
+    if (splits > 1 && acc != B2G_ACC_F32)
+        return fail(B2G_ERR_UNSUPPORTED,
+                    "split-K sums FP32 partials: it needs FP32 accumulation (acc 0), got acc %d",
+                    acc);
     if (M == 0 || N == 0) return B2G_OK;
     if (!D) return fail(B2G_ERR_ARG, "D is NULL");
     if (ldd < N) return fail(B2G_ERR_ARG, "ldd (%lld) < N (%d)", ldd, N);
@@ -302,7 +404,6 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
 
     DeviceInfo di;
     if (int rc = current_device(di)) return rc;
-    cudaStream_t s = (cudaStream_t)stream;
 
     if (K == 0) {  // zero accumulator: only the epilogue remains
         const size_t n = (size_t)M * N;
@@ -327,7 +428,10 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
     if (b_layout == B2G_B_KN)
         return fail(B2G_ERR_UNSUPPORTED, "b_layout K x N is not built yet");
 
-    if (tile == B2G_TILE_AUTO) tile = N <= 128 ? B2G_TILE_128x128 : B2G_TILE_256x256_2SM;
+    // one CTA per 128 x 128 tile when either side is small (no half-empty 256-row pair
+    // tiles for skinny M, fewer idle columns for narrow N), else 2-CTA 256 x 256 pairs
+    if (tile == B2G_TILE_AUTO)
+        tile = (N <= 128 || M <= 128) ? B2G_TILE_128x128 : B2G_TILE_256x256_2SM;
     const TileGeom g = geom(tile);
     const int max_st = max_stages_for(tile, di.smem_optin);
     if (stages == 0) stages = max_st;
@@ -346,6 +450,11 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
     if (nt > 0x7fffffffLL) return fail(B2G_ERR_ARG, "too many tiles (%lld)", nt);
     p.num_tiles = (int)nt;
     p.num_kb = (K + kBK - 1) / kBK;
+    // A box rows: all of M in one 1-CTA tile -> load only round_up(M, 8) rows per k-block
+    const uint32_t a_rows = (g.ctas == 1 && p.tiles_m == 1)
+                                ? std::min<uint32_t>(g.box_a, (uint32_t)((M + 7) / 8 * 8))
+                                : g.box_a;
+    p.stage_tx = (a_rows + g.box_b) * kBK * 2;
     p.group = group > 0 ? group : auto_group(g, p.tiles_m, K);
     p.stages = stages;
     p.idesc = idesc_f16(g.bm, g.bn, acc == B2G_ACC_F32, false);
@@ -355,14 +464,32 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
     p.bias = (const __half*)bias;
     p.D = (__half*)D;
     p.ldd = ldd;
-    p.d_vec = (((uintptr_t)D & 15) == 0) && (ldd % 8 == 0);
-    p.d_tma = p.d_vec;
+    p.d_tma = (((uintptr_t)D & 15) == 0) && (ldd % 8 == 0);
     p.b_mn_major = 0;
     p.dp_tiles = p.num_tiles;
     p.tail_split = 1;
     p.num_units = p.num_tiles;
     p.idesc_tail = p.idesc;
-    if (g.ctas == 2) {
+    // split-K: tiles that fill under half of the SMs (pairs) get their K range split
+    const int concurrent = g.ctas == 2 ? max_pair_clusters(di, smem) : di.sm_count;
+    if (splits == 0)
+        splits = acc == B2G_ACC_F32 ? splitk_auto(p.num_tiles, concurrent, p.num_kb, g.ctas) : 1;
+    if (splits > p.num_kb)
+        return fail(B2G_ERR_ARG, "splits (%d) > k-blocks of 64 (%d)", splits, p.num_kb);
+    if ((long long)p.num_tiles * splits > 0x7fffffffLL)
+        return fail(B2G_ERR_ARG, "too many work units (%d tiles x %d splits)", p.num_tiles, splits);
+    p.splits = splits;
+    p.num_units = p.num_tiles * splits;
+    if (splits > 1) {
+        const size_t part = (size_t)p.num_tiles * splits * g.ctas * 128 * g.bn * sizeof(float);
+        const size_t counters = (size_t)p.num_tiles * g.ctas * kMaxEpiWarps;
+        SplitScratch sc{};
+        if (int rc = managed_scratch(di, s, part, counters, &sc)) return rc;
+        p.ws_part = sc.part;
+        p.ws_count = sc.count;
+        p.epoch = sc.epoch;
+    }
+    if (g.ctas == 2 && splits == 1) {
         // cut the tiles of the last, partial wave into column slices (see pair_unit)
         const int clusters = max_pair_clusters(di, smem);
         const int rest = p.num_tiles % clusters;
@@ -377,7 +504,7 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
     p.timeout_ns = wait_timeout_ns();
 
     CUtensorMap tmA, tmB;
-    if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK, g.box_a, "A"))
+    if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK, a_rows, "A"))
         return rc;
     if (int rc = make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, g.box_b, "B"))
         return rc;
@@ -391,6 +518,27 @@ B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias,
         if (int rc = make_tmap(&tmD, D, (uint64_t)N, (uint64_t)M, (uint64_t)ldd, 64, 32, "D"))
             return rc;
     return launch_gemm(tile, tmA, tmB, tmBt, tmD, p, di, smem, s);
+}
+
+}  // namespace
+}  // namespace b2g
+
+B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias, int M, int N,
+                        int K, long long lda, long long ldb, long long ldd, int b_layout,
+                        int acc, int epilogue, float alpha, int tile, int stages, int group,
+                        void* stream) {
+    clear_error();
+    return gemm_impl(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc, epilogue, alpha, tile,
+                     stages, group, 0, (cudaStream_t)stream);
+}
+
+B2G_EXPORT int b2g_gemm_splitk(const void* A, const void* B, void* D, const void* bias, int M,
+                               int N, int K, long long lda, long long ldb, long long ldd,
+                               int b_layout, int acc, int epilogue, float alpha, int tile,
+                               int stages, int group, int splits, void* stream) {
+    clear_error();
+    return gemm_impl(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc, epilogue, alpha, tile,
+                     stages, group, splits, (cudaStream_t)stream);
 }
 
 B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, int* smem_bytes,
@@ -428,7 +576,8 @@ B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, in
     return B2G_OK;
 }
 
-B2G_EXPORT int b2g_last_launch(int* grid, int* threads, int* tile, int* stages, int* units) {
+B2G_EXPORT int b2g_last_launch(int* grid, int* threads, int* tile, int* stages, int* units,
+                               int* splits) {
     clear_error();
     const LaunchRecord r = g_last_launch;
     if (r.grid == 0) return fail(B2G_ERR_ARG, "no GEMM kernel launched on this host thread yet");
@@ -437,6 +586,7 @@ B2G_EXPORT int b2g_last_launch(int* grid, int* threads, int* tile, int* stages, 
     if (tile) *tile = r.tile;
     if (stages) *stages = r.stages;
     if (units) *units = r.units;
+    if (splits) *splits = r.splits;
     return B2G_OK;
 }
 
@@ -454,11 +604,13 @@ B2G_EXPORT int b2g_sync_status(void* stream) {
     const unsigned int zero = 0;
     cudaMemcpyToSymbol(g_b2g_status, &zero, sizeof(zero));
     return fail(B2G_ERR_TIMEOUT,
-                "device wait gave up (status 0x%x:%s%s%s%s%s%s); the kernel unwound and returned",
+                "device wait gave up (status 0x%x:%s%s%s%s%s%s%s); the kernel unwound and "
+                "returned",
                 word, (word & kErrWaitProducer) ? " producer" : "", (word & kErrWaitMma) ? " mma" : "",
                 (word & kErrWaitEpilogue) ? " epilogue" : "",
                 (word & kErrWaitSelftest) ? " selftest" : "", (word & kErrWaitDrain) ? " drain" : "",
-                (word & kErrWaitProbe) ? " probe" : "");
+                (word & kErrWaitProbe) ? " probe" : "",
+                (word & kErrSplitCounter) ? " split-K counter" : "");
 }
 
 #ifdef B2G_INSTRUMENT

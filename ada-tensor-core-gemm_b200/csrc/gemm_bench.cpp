@@ -46,6 +46,7 @@ struct Args {
     int M = 4096, N = 4096, K = 4096;
     int tile = -1, stages = 0, layout = 2, group = 0;  // -1 / 0 = chosen from the shape
     int iters = 50, warmup = 20;
+    int splits = -1;    // split-K factor: -1 = b2g_gemm (automatic), else b2g_gemm_splitk
     int cpu = 0;        // output elements verified by the FP64 host spot check
     int frob = 0;       // rows of D checked by an FP64 relative Frobenius norm
     double soak = 0;    // seconds of back-to-back launches (0 = fixed iters)
@@ -152,9 +153,11 @@ void usage(const char* argv0) {
            "  --check    compare against cuBLAS on the device (max |x-y|/max(1,|y|))\n"
            "  --cpu S    verify S output elements against an FP64 host dot product\n"
            "  --frob R   FP64 relative Frobenius error over R rows spread through D\n"
-           "  tile 0 = 128x128x64  1 CTA, UMMA 128x128, TMEM 2x128 cols\n"
-           "       1 = 128x256x64  1 CTA, UMMA 128x256, TMEM 2x256 cols (default)\n"
+           "  tile -1 = chosen from the shape (default)\n"
+           "       0 = 128x128x64  1 CTA, UMMA 128x128, TMEM 2x128 cols\n"
+           "       1 = 128x256x64  1 CTA, UMMA 128x256, TMEM 2x256 cols\n"
            "       2 = 256x256x64  2-CTA pair (cta_group::2), UMMA 256x256\n"
+           "  --splits S split-K factor (0 automatic, 1 none, S >= 2 forced; default: automatic)\n"
            "  --stages   shared-memory ring depth (0 = deepest that fits)\n"
            "  --group G  L2 rasterization: G M-tiles walked column-major (1 = row-major)\n"
            "  --sweep    stages 2..8 at fixed tile/group;  --gsweep  group 1,2,4,8,16\n"
@@ -181,6 +184,7 @@ int main(int argc, char** argv) {
         else if (eq("--iters")) a.iters = val();
         else if (eq("--warmup")) a.warmup = val();
         else if (eq("--group")) a.group = val();
+        else if (eq("--splits")) a.splits = val();
         else if (eq("--cpu")) a.cpu = val();
         else if (eq("--frob")) a.frob = val();
         else if (eq("--soak")) a.soak = dval();
@@ -340,9 +344,14 @@ int main(int argc, char** argv) {
         }
         CUDA_CHECK(cudaMemset(dD, 0, std::max<size_t>(nD, 8) * 2));
         auto launch = [&]() -> int {
-            int rc = b2g_gemm(dA, dB, dD, a.fused ? dBias : nullptr, a.M, a.N, a.K, lda, ldb, ldd,
-                              a.b_layout, a.acc, a.fused ? B2G_EPI_BIAS_RELU : B2G_EPI_NONE, 1.0f,
-                              j.tile, j.stages, j.group, stream);
+            const int epi = a.fused ? B2G_EPI_BIAS_RELU : B2G_EPI_NONE;
+            int rc = a.splits < 0
+                         ? b2g_gemm(dA, dB, dD, a.fused ? dBias : nullptr, a.M, a.N, a.K, lda, ldb,
+                                    ldd, a.b_layout, a.acc, epi, 1.0f, j.tile, j.stages, j.group,
+                                    stream)
+                         : b2g_gemm_splitk(dA, dB, dD, a.fused ? dBias : nullptr, a.M, a.N, a.K,
+                                           lda, ldb, ldd, a.b_layout, a.acc, epi, 1.0f, j.tile,
+                                           j.stages, j.group, a.splits, stream);
             if (rc == B2G_OK && a.unfused)
                 rc = b2g_bias_relu(dD, dBias, a.M, a.N, ldd, 1.0f, stream);
             return rc;
@@ -355,7 +364,8 @@ int main(int argc, char** argv) {
             rc_all = 1;
             continue;
         }
-        if (a.warmup > 0) b2g_last_launch(nullptr, &thr, nullptr, &st_used, nullptr);
+        int used_splits = 1;
+        if (a.warmup > 0) b2g_last_launch(nullptr, &thr, nullptr, &st_used, nullptr, &used_splits);
         cudaEvent_t t0, t1;
         CUDA_CHECK(cudaEventCreate(&t0));
         CUDA_CHECK(cudaEventCreate(&t1));
@@ -445,13 +455,14 @@ int main(int argc, char** argv) {
         if (frob >= 0) printf("  frob=%.2e", frob);
         double kmhz = 0, kus = 0;
         if (b2g_kernel_clock(&kmhz, &kus) == B2G_OK) printf("  sm_mhz=%.0f", kmhz);
-        printf("\n");
+        printf("  splits=%d\n", used_splits);
         if (a.json)
             printf("{\"M\": %d, \"N\": %d, \"K\": %d, \"tile\": %d, \"stages\": %d, \"group\": %d, "
                    "\"acc\": \"%s\", \"ms\": %.5f, \"tflops\": %.3f, \"cublas_tflops\": %.3f, "
-                   "\"maxrel_vs_cublas\": %.3e, \"cpu_maxrel\": %.3e, \"frob_rel\": %.3e}\n",
+                   "\"maxrel_vs_cublas\": %.3e, \"cpu_maxrel\": %.3e, \"frob_rel\": %.3e, "
+                   "\"splits\": %d, \"sm_mhz\": %.0f}\n",
                    a.M, a.N, a.K, j.tile, st_used, j.group, a.acc == B2G_ACC_F32 ? "f32" : "f16", ms,
-                   tflops, ref_tflops, maxrel, cpurel, frob);
+                   tflops, ref_tflops, maxrel, cpurel, frob, used_splits, kmhz);
         fflush(stdout);
     }
     cudaFree(dA); cudaFree(dB); cudaFree(dD); cudaFree(dRef); cudaFree(dBias); cudaFree(dErr);

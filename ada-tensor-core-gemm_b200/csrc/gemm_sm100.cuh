@@ -45,8 +45,8 @@ struct GemmParams {
     const __half* bias;
     __half* D;
     long long ldd;
-    int d_vec;       // 16-byte vector stores allowed (D 16-byte aligned and ldd % 8 == 0)
-    int d_tma;       // D written by TMA stores (same alignment conditions as d_vec)
+    int d_tma;       // D written by TMA stores (D 16-byte aligned and ldd % 8 == 0), else by
+                     // coalesced plain stores from the same staging box
     int b_mn_major;  // B is K x N (MN-major) in global memory
     unsigned long long timeout_ns;
     // 2-CTA kernel work list: tiles [0, dp_tiles) run whole; each remaining tile (the last,
@@ -54,7 +54,23 @@ struct GemmParams {
     // so the tail wave keeps every SM busy. num_units = dp_tiles + rest * tail_split.
     int dp_tiles, tail_split, num_units;
     uint32_t idesc_tail;
+    // Split-K (FP32 accumulation only): unit u = tile (u / splits), k-blocks of split
+    // (u % splits); see splitk_store / splitk_arrive_reduce. splits == 1: off.
+    int splits;
+    float* ws_part;                // FP32 partial accumulators, splitk_slot() layout
+    unsigned long long* ws_count;  // arrival counters: (launch epoch << 32) | arrivals
+    unsigned int epoch;            // this launch's epoch, never 0 and never repeated
+    // 1-CTA kernels: bytes one stage's two TMA loads deliver. When all of M fits one tile the
+    // A box is only round_up(M, 8) rows high; the stale shared-memory rows below it feed
+    // accumulator rows >= M, which the epilogue never stores.
+    uint32_t stage_tx;
 };
+
+// k-blocks [kb0, kb1) of split s: an even share of the tile's num_kb k-blocks.
+__device__ __forceinline__ void split_range(const GemmParams& p, int s, int& kb0, int& kb1) {
+    kb0 = (int)((long long)s * p.num_kb / p.splits);
+    kb1 = (int)((long long)(s + 1) * p.num_kb / p.splits);
+}
 
 constexpr int kBM = 128;      // rows of A per CTA (UMMA M for cta_group::1)
 constexpr int kBK = 64;       // k-block: one 128-byte swizzle row of FP16
@@ -99,51 +115,6 @@ template <int BN>
 constexpr size_t gemm_smem_bytes(int stages) {
     return 1024 /* alignment slack */ + (size_t)stages * TileTraits<BN>::kStageBytes +
            kEpiBytes + sizeof(SmemCtl);
-}
-
-__device__ __forceinline__ float acc_value(uint32_t raw, int acc_f16) {
-    return acc_f16 ? __half2float(__ushort_as_half((unsigned short)(raw & 0xFFFFu)))
-                   : __uint_as_float(raw);
-}
-
-// Epilogue for 32 consecutive columns [col, col + 32) of one output row.
-__device__ __forceinline__ void store_row_chunk32(const GemmParams& p, int row, int col,
-                                                  const uint32_t (&r)[32]) {
-    if (row >= p.M || col >= p.N) return;
-    float v[32];
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = acc_value(r[j], p.acc_f16);
-    if (p.epilogue) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-            float x;
-            if (p.bias != nullptr) {
-                const int n = col + j < p.N ? col + j : p.N - 1;
-                x = fmaf(v[j], p.alpha, __half2float(p.bias[n]));
-            } else {
-                x = v[j] * p.alpha;
-            }
-            v[j] = x > 0.f ? x : 0.f;
-        }
-    }
-    __half* dst = p.D + (size_t)row * (size_t)p.ldd + col;
-    if (p.d_vec && col + 32 <= p.N) {
-        uint32_t h[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            __half2 t = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-            h[j] = *reinterpret_cast<uint32_t*>(&t);
-        }
-        uint4* d4 = reinterpret_cast<uint4*>(dst);
-        d4[0] = make_uint4(h[0], h[1], h[2], h[3]);
-        d4[1] = make_uint4(h[4], h[5], h[6], h[7]);
-        d4[2] = make_uint4(h[8], h[9], h[10], h[11]);
-        d4[3] = make_uint4(h[12], h[13], h[14], h[15]);
-    } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-            if (col + j < p.N) dst[j] = __float2half_rn(v[j]);
-    }
 }
 
 // The epilogue's per-element work uses only these scalars, read once from the kernel
@@ -194,70 +165,109 @@ __device__ __forceinline__ uint32_t epi_pack2(const EpiScalars& e, int col, uint
     return *reinterpret_cast<uint32_t*>(&t);
 }
 
-// One 64-column chunk already in registers: convert, stage and store. With d_tma the chunk
-// goes into a swizzled 32 x 64 staging box and lane 0 issues one TMA store (the tensor map
-// clips the M / N edges); otherwise each thread stores its own row with st.global.
+// Staging box of this warp for its next TMA store: waits (lane 0) until the store that last
+// read the box has finished reading it.
+__device__ __forceinline__ uint32_t epi_box_acquire(const EpiScalars& e, uint32_t stage0,
+                                                    uint32_t seq, int lane) {
+    const uint32_t box = stage0 + (e.bufs == 2 ? (seq & 1u) : 0u) * kEpiBoxBytes;
+    if (lane == 0) {
+        if (e.bufs == 2)
+            bulk_wait_read<1>();
+        else
+            bulk_wait_read<0>();
+    }
+    __syncwarp();
+    return box;
+}
+
+// Convert 32 accumulator columns [col + 32h, col + 32h + 32) of row `lane` and write them as
+// 16-byte groups j = 4h .. 4h + 3 of the box row (128-byte swizzle: group j of row r lives at
+// (j ^ (r & 7)) * 16).
 template <bool ACC16, bool EPI>
-__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, const EpiScalars& e,
-                                               const CUtensorMap* tmD, const uint32_t (&r)[64],
-                                               int row0, int col, uint32_t stage0, int lane,
-                                               uint32_t& seq) {
-    if (e.d_tma) {
-        const uint32_t box = stage0 + (e.bufs == 2 ? (seq & 1u) : 0u) * kEpiBoxBytes;
-        B2G_TIC(t_box);
-        if (lane == 0) {  // the store that last read `box` is done
-            if (e.bufs == 2)
-                bulk_wait_read<1>();
-            else
-                bulk_wait_read<0>();
-        }
-        __syncwarp();
-        B2G_TOC64(10, t_box);
-        B2G_TIC(t_cvt);
-        // row `lane` of the box = 128 bytes; 16-byte chunk j lives at (j ^ (row & 7)) * 16
-        const uint32_t rowaddr = box + (uint32_t)lane * 128u;
-        const uint32_t sw = (uint32_t)(lane & 7);
+__device__ __forceinline__ void epi_box_put32(const EpiScalars& e, uint32_t box, int col, int h,
+                                              const uint32_t (&r)[32], int lane) {
+    const uint32_t rowaddr = box + (uint32_t)lane * 128u;
+    const uint32_t sw = (uint32_t)(lane & 7);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int b = j * 8;
-            const int cc = col + b;
-            st_shared_v4(rowaddr + (((uint32_t)j ^ sw) << 4),
-                         epi_pack2<ACC16, EPI>(e, cc, r[b], r[b + 1]),
-                         epi_pack2<ACC16, EPI>(e, cc + 2, r[b + 2], r[b + 3]),
-                         epi_pack2<ACC16, EPI>(e, cc + 4, r[b + 4], r[b + 5]),
-                         epi_pack2<ACC16, EPI>(e, cc + 6, r[b + 6], r[b + 7]));
-        }
-        B2G_TOC64(9, t_cvt);
-        B2G_TIC(t_st);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-            tma_store_2d_hint(tmD, box, col, row0, e.store_pol);
-            bulk_commit();
-        }
-        B2G_TOC64(11, t_st);
-        ++seq;
-    } else {
-        store_row_chunk32(p, row0 + lane, col, *reinterpret_cast<const uint32_t(*)[32]>(&r[0]));
-        store_row_chunk32(p, row0 + lane, col + 32,
-                          *reinterpret_cast<const uint32_t(*)[32]>(&r[32]));
+    for (int jj = 0; jj < 4; ++jj) {
+        const int j = 4 * h + jj, b = jj * 8, cc = col + j * 8;
+        st_shared_v4(rowaddr + (((uint32_t)j ^ sw) << 4), epi_pack2<ACC16, EPI>(e, cc, r[b], r[b + 1]),
+                     epi_pack2<ACC16, EPI>(e, cc + 2, r[b + 2], r[b + 3]),
+                     epi_pack2<ACC16, EPI>(e, cc + 4, r[b + 4], r[b + 5]),
+                     epi_pack2<ACC16, EPI>(e, cc + 6, r[b + 6], r[b + 7]));
     }
 }
 
+// Issue the TMA store of a filled box (lane 0); the tensor map clips the M / N edges.
+__device__ __forceinline__ void epi_box_store(const EpiScalars& e, const CUtensorMap* tmD,
+                                              uint32_t box, int col, int row0, int lane,
+                                              uint32_t& seq) {
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d_hint(tmD, box, col, row0, e.store_pol);
+        bulk_commit();
+    }
+    ++seq;
+}
+
+// Write a filled staging box to D with plain stores, for D that TMA cannot address (base
+// not 16-byte aligned, or ldd not a multiple of 8): row by row, the lanes taking consecutive
+// columns, so every store instruction covers 64 contiguous bytes of one row.
+__device__ __forceinline__ void epi_box_store_rows(const GemmParams& p, const EpiScalars& e,
+                                                   uint32_t box, int col, int row0, int lane) {
+    __syncwarp();  // every lane's part of the box is written
+    __half* const D = p.D;
+    const long long ldd = p.ldd;
+#pragma unroll 1
+    for (int r = 0; r < 32 && row0 + r < e.M; ++r) {
+        __half* drow = D + (size_t)(row0 + r) * (size_t)ldd;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int c = hh * 32 + lane;  // column within the box
+            if (col + c < e.N) {
+                const uint32_t off = (uint32_t)r * 128u +
+                                     ((((uint32_t)c >> 3) ^ (uint32_t)(r & 7)) << 4) +
+                                     ((uint32_t)c & 7u) * 2u;
+                drow[col + c] = __ushort_as_half(ld_shared_u16(box + off));
+            }
+        }
+    }
+    __syncwarp();  // the box may be refilled
+}
+
+// Chunks c_first, c_first + e.c_step, ... (< nchunks) of 64 columns of this warp's 32 rows:
+// TMEM -> registers 32 columns at a time -> convert -> swizzled staging box -> one TMA store
+// per chunk (d_tma), or coalesced plain stores of the box's rows.
 template <bool ACC16, bool EPI>
 __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiScalars& e,
                                                 const CUtensorMap* tmD, uint32_t trow, int row0,
                                                 int n_first, int nchunks, int c_first,
                                                 uint32_t stage0, int lane, uint32_t& seq) {
-    uint32_t r[64];
+    uint32_t r[32];
 #pragma unroll 1
     for (int c = c_first; c < nchunks; c += e.c_step) {
-        B2G_TIC(t_ld);
-        tmem_ld_32x32b_x64(trow + (uint32_t)c * 64u, r);
-        tmem_ld_wait();
-        B2G_TOC64(8, t_ld);
+        const int col = n_first + c * 64;
+        B2G_TIC(t_box);
+        const uint32_t box = e.d_tma ? epi_box_acquire(e, stage0, seq, lane) : stage0;
+        B2G_TOC64(10, t_box);
         B2G_COUNT(12, threadIdx.x == 64 ? 1 : 0);
-        epilogue_chunk<ACC16, EPI>(p, e, tmD, r, row0, n_first + c * 64, stage0, lane, seq);
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+            B2G_TIC(t_ld);
+            tmem_ld_32x32b_x32(trow + (uint32_t)(c * 64 + h * 32), r);
+            tmem_ld_wait();
+            B2G_TOC64(8, t_ld);
+            B2G_TIC(t_cvt);
+            epi_box_put32<ACC16, EPI>(e, box, col, h, r, lane);
+            B2G_TOC64(9, t_cvt);
+        }
+        B2G_TIC(t_st);
+        if (e.d_tma)
+            epi_box_store(e, tmD, box, col, row0, lane, seq);
+        else
+            epi_box_store_rows(p, e, box, col, row0, lane);
+        B2G_TOC64(11, t_st);
     }
 }
 
@@ -293,6 +303,179 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiScal
     }
 }
 
+// ------------------------------------------------------------------------------------------
+// Split-K. Each split of a tile writes its FP32 partial accumulator to the workspace and then
+// counts itself in; the split that arrives last sums all partials in split order 0..S-1 (so
+// the result does not depend on which split finished last) and runs the normal epilogue.
+// Nothing ever waits for another CTA. Bookkeeping is per epilogue warp: warp w of every split
+// covers the same 32 rows and 64-column chunks, so warp w of the last split needs only the
+// partials of the other splits' warp w, and one counter per (tile, CTA of the pair, warp).
+// ------------------------------------------------------------------------------------------
+
+// Partial slot of (tile t, split s, CTA `rank`, lane quarter q): 32 rows x bn FP32, stored
+// [64-column chunk][float4 index 0..15][lane] so every warp-wide store / load is one
+// contiguous 512-byte run.
+__device__ __forceinline__ float4* splitk_slot(const GemmParams& p, int t, int s, int rank,
+                                               int ctas, int q, int bn) {
+    const size_t slot = (((size_t)t * p.splits + s) * ctas + rank) * 4 + q;
+    return reinterpret_cast<float4*>(p.ws_part + slot * 32 * (size_t)bn);
+}
+
+// Chunks [c_first, nchunks) step c_step of this warp's 32 rows, TMEM -> workspace partial.
+__device__ __forceinline__ void splitk_store(float4* slot, uint32_t trow, int nchunks,
+                                             int c_first, int c_step, int lane) {
+    uint32_t r[32];
+#pragma unroll 1
+    for (int c = c_first; c < nchunks; c += c_step) {
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+            tmem_ld_32x32b_x32(trow + (uint32_t)(c * 64 + h * 32), r);
+            tmem_ld_wait();
+            float4* dst = slot + (size_t)c * 16 * 32 + h * 8 * 32 + lane;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+                dst[v * 32] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                                          __uint_as_float(r[4 * v + 2]),
+                                          __uint_as_float(r[4 * v + 3]));
+        }
+    }
+}
+
+// Count this warp's split of its tile in; true in every lane if it was the last of the
+// `splits`. The counter holds (epoch << 32) | arrivals: the first arrival of a launch finds
+// an older epoch (or 0) and starts over at 1, so no counter has to be cleared between
+// launches, even after a launch that gave up half-way. Ordering: __syncwarp orders the
+// lanes' partial stores before lane 0's release CAS (cumulative at gpu scope); the last
+// arrival's CAS also acquires, and the lanes then read the other splits' partials from L2.
+__device__ __forceinline__ bool splitk_arrive(unsigned long long* cnt, unsigned int epoch,
+                                              int splits, int lane) {
+    __syncwarp();
+    int last = 0;
+    if (lane == 0) {
+        const unsigned long long tag = (unsigned long long)epoch << 32;
+        unsigned long long old = ld_relaxed_gpu_u64(cnt);
+        bool done = false;
+        for (int tries = 0; tries < (1 << 20) && !done; ++tries) {
+            const unsigned long long next = (old & ~0xffffffffull) == tag ? old + 1 : tag + 1;
+            const unsigned long long seen = atom_cas_acq_rel_gpu_u64(cnt, old, next);
+            if (seen == old) {
+                done = true;
+                last = (int)(next & 0xffffffffull) == splits;
+            } else {
+                old = seen;
+            }
+        }
+        if (!done) raise_status(kErrSplitCounter);
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();  // the lanes' partial loads are ordered after lane 0's acquire
+    return last != 0;
+}
+
+// Last split: sum the partials of every split in split order 0..S-1, 16 columns at a time
+// (the loads of four splits in flight together), and hand the sums to the
+// normal epilogue (alpha, bias, ReLU, FP16, TMA store of each 64-column chunk).
+template <bool EPI>
+__device__ __forceinline__ void splitk_reduce_t(const GemmParams& p, const EpiScalars& e,
+                                                const CUtensorMap* tmD, int t, int rank,
+                                                int ctas, int q, int bn, int row0, int n_first,
+                                                int nchunks, int c_first, uint32_t stage0,
+                                                int lane, uint32_t& seq) {
+    const size_t split_stride = (size_t)32 * ctas * bn;  // float4s between splits' slots
+    const float4* slot0 = splitk_slot(p, t, 0, rank, ctas, q, bn) + lane;
+#pragma unroll 1
+    for (int c = c_first; c < nchunks; c += e.c_step) {
+        const int col = n_first + c * 64;
+        const uint32_t box = e.d_tma ? epi_box_acquire(e, stage0, seq, lane) : stage0;
+#pragma unroll 1
+        for (int h = 0; h < 4; ++h) {
+            const float4* src = slot0 + (size_t)c * 512 + h * 128;
+            float acc[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) acc[j] = 0.f;
+            // up to four splits' 16 columns in flight at once, added in split order
+#pragma unroll 1
+            for (int s0 = 0; s0 < p.splits; s0 += 4) {
+                // splits past the last re-read split S - 1 (an L2 hit) and are not added
+                float4 x[4][4];
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    const float4* sg = src + (size_t)min(s0 + g, p.splits - 1) * split_stride;
+#pragma unroll
+                    for (int v = 0; v < 4; ++v) x[g][v] = __ldcg(sg + v * 32);
+                }
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    if (s0 + g < p.splits) {
+#pragma unroll
+                        for (int v = 0; v < 4; ++v) {
+                            acc[4 * v] += x[g][v].x;
+                            acc[4 * v + 1] += x[g][v].y;
+                            acc[4 * v + 2] += x[g][v].z;
+                            acc[4 * v + 3] += x[g][v].w;
+                        }
+                    }
+                }
+            }
+            uint32_t r[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(acc[j]);
+            // 16-byte groups j = 2h, 2h + 1 of row `lane` of the swizzled staging box
+            const uint32_t rowaddr = box + (uint32_t)lane * 128u;
+            const uint32_t sw = (uint32_t)(lane & 7);
+#pragma unroll
+            for (int jj = 0; jj < 2; ++jj) {
+                const int j = 2 * h + jj, b = jj * 8, cc = col + j * 8;
+                st_shared_v4(rowaddr + (((uint32_t)j ^ sw) << 4),
+                             epi_pack2<false, EPI>(e, cc, r[b], r[b + 1]),
+                             epi_pack2<false, EPI>(e, cc + 2, r[b + 2], r[b + 3]),
+                             epi_pack2<false, EPI>(e, cc + 4, r[b + 4], r[b + 5]),
+                             epi_pack2<false, EPI>(e, cc + 6, r[b + 6], r[b + 7]));
+            }
+        }
+        if (e.d_tma)
+            epi_box_store(e, tmD, box, col, row0, lane, seq);
+        else
+            epi_box_store_rows(p, e, box, col, row0, lane);
+    }
+}
+
+// Split-K epilogue of one warp for one unit: partial out, TMEM released through `release`
+// (called once the accumulator has been read), then the reduction if this split was last.
+template <class Release>
+__device__ __forceinline__ void splitk_epilogue(const GemmParams& p, const EpiScalars& e,
+                                                const CUtensorMap* tmD, uint32_t trow, int t,
+                                                int s, int rank, int ctas, int q, int wslot,
+                                                int bn, int row0, int n_first, int c_first,
+                                                uint32_t stage0, int lane, uint32_t& seq,
+                                                bool epi, Release release) {
+    // rows and chunks outside D are skipped identically by every split of the tile
+    int nchunks = bn / 64;
+    const int in_n = (e.N - n_first + 63) / 64;
+    if (in_n < nchunks) nchunks = in_n;
+    const bool active = row0 < e.M && nchunks > c_first;
+    B2G_TIC(t_ps);
+    if (active) splitk_store(splitk_slot(p, t, s, rank, ctas, q, bn), trow, nchunks, c_first,
+                             e.c_step, lane);
+    release();
+    B2G_TOC64(13, t_ps);
+    if (!active) return;
+    unsigned long long* cnt = p.ws_count + ((size_t)t * ctas + rank) * kMaxEpiWarps + wslot;
+    B2G_TIC(t_arr);
+    const bool last = splitk_arrive(cnt, p.epoch, p.splits, lane);
+    B2G_TOC64(14, t_arr);
+    if (!last) return;
+    B2G_TIC(t_red);
+    B2G_COUNT(15, threadIdx.x == 64 ? 1 : 0);
+    if (epi)
+        splitk_reduce_t<true>(p, e, tmD, t, rank, ctas, q, bn, row0, n_first, nchunks, c_first,
+                              stage0, lane, seq);
+    else
+        splitk_reduce_t<false>(p, e, tmD, t, rank, ctas, q, bn, row0, n_first, nchunks, c_first,
+                               stage0, lane, seq);
+    B2G_TOC64(12, t_red);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_1cta(const __grid_constant__ CUtensorMap tmA,
@@ -300,6 +483,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
     using TT = TileTraits<BN>;
     clock_mark(0);
+    B2G_TIC(t_life);
     extern __shared__ uint8_t smem_dyn[];
     // stage buffers must be 1024-byte aligned (128-byte swizzle atoms, base offset 0)
     const uint32_t raw = smem_u32(smem_dyn);
@@ -359,17 +543,21 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             uint32_t phase = 0;
             long long issued = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
-                int tm, tn;
+            for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+                const int t = u / p.splits;
+                int tm, tn, kb0, kb1;
                 tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
+                split_range(p, u - t * p.splits, kb0, kb1);
                 const int m0 = tm * kBM, n0 = tn * BN;
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    B2G_TIC(t_empty);
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, w)) {
                         ok = false;
                         break;
                     }
+                    B2G_TOC(0, t_empty);
                     const uint32_t fb = full0 + 8 * stage;
-                    mbar_arrive_expect_tx(fb, TT::kStageBytes);
+                    mbar_arrive_expect_tx(fb, p.stage_tx);
                     tma_load_2d(sA + stage * kAStageBytes, &tmA, fb, kb * kBK, m0);
                     tma_load_2d(sB + stage * TT::kBStageBytes, &tmB, fb, kb * kBK, n0);
                     ++issued;
@@ -409,24 +597,32 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             uint32_t phase = 0;
             int it = 0;
             bool ok = true;
-            for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x, ++it) {
+            for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x, ++it) {
                 const int buf = it & 1;
                 const uint32_t use = (uint32_t)(it >> 1) & 1u;
+                int kb0, kb1;
+                split_range(p, u % p.splits, kb0, kb1);
+                B2G_TIC(t_te);
                 if (!mbar_wait_warp(tempty0 + 8 * buf, use ^ 1u, w)) {
                     ok = false;
                     break;
                 }
+                if (lane == 0) B2G_TOC(2, t_te);
+                if (lane == 0) B2G_COUNT(7, 1);
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(buf * BN);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    B2G_TIC(t_full);
                     if (!mbar_wait_warp(full0 + 8 * stage, phase, w)) {
                         ok = false;
                         break;
                     }
+                    if (lane == 0) B2G_TOC(1, t_full);
+                    if (lane == 0) B2G_COUNT(6, 1);
                     const uint64_t ad = adesc0 + (uint64_t)((uint32_t)stage * kAStep);
                     const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kBStep);
                     if (elect_one()) {
-                        mma_f16_ss<1>(d_tmem, ad, bd, idesc, kb > 0 ? 1u : 0u);
+                        mma_f16_ss<1>(d_tmem, ad, bd, idesc, kb > kb0 ? 1u : 0u);
                         mma_f16_ss<1>(d_tmem, ad + 2, bd + 2, idesc, 1u);
                         mma_f16_ss<1>(d_tmem, ad + 4, bd + 4, idesc, 1u);
                         mma_f16_ss<1>(d_tmem, ad + 6, bd + 6, idesc, 1u);
@@ -459,20 +655,34 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const bool acc16 = p.acc_f16 != 0, epi = p.epilogue != 0;
         uint32_t seq = 0;
         int it = 0;
-        for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++it) {
+        for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {
             const int buf = it & 1;
             const uint32_t use = (uint32_t)(it >> 1) & 1u;
+            B2G_TIC(t_tf);
             const bool ok = mbar_wait(tfull0 + 8 * buf, use, w);
             if (!__all_sync(0xffffffffu, ok)) break;
+            if (warp == 2 && lane == 0) B2G_TOC(3, t_tf);
+            B2G_TIC(t_epi);
             tc_fence_after();
+            const int t = u / p.splits;
             int tm, tn;
             tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-            epilogue_rows(p, es, &tmD, tbase, tm * kBM + q * 32, tn * BN, BN, c_first, stage0,
-                          lane, seq, acc16, epi);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+            auto release = [&] {  // accumulator `buf` has been read: the MMA warp may reuse it
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
+            };
+            if (p.splits > 1) {
+                splitk_epilogue(p, es, &tmD, tbase, t, u - t * p.splits, 0, 1, q, warp - 2, BN,
+                                tm * kBM + q * 32, tn * BN, c_first, stage0, lane, seq, epi,
+                                release);
+            } else {
+                epilogue_rows(p, es, &tmD, tbase, tm * kBM + q * 32, tn * BN, BN, c_first, stage0,
+                              lane, seq, acc16, epi);
+                release();
+            }
+            if (warp == 2 && lane == 0) B2G_TOC(4, t_epi);
         }
         if (lane == 0) bulk_wait<0>();  // this warp's TMA stores have completed
         __syncwarp();
@@ -484,6 +694,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         tc_fence_after();
         tmem_dealloc<1>(tmem_base, TT::kTmemCols);
     }
+    if (threadIdx.x == 0) B2G_TOC(5, t_life);
     clock_mark(1);
 }
 

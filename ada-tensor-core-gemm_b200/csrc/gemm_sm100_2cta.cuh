@@ -41,11 +41,21 @@ constexpr size_t gemm2_smem_bytes(int stages) {
     return 1024 + (size_t)stages * kPairStageBytes + kEpiBytes + sizeof(SmemCtl);
 }
 
-// Work unit u -> output tile (tm, tn), first output column and width of the unit.
-__device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& tm, int& tn,
-                                          int& n_first, int& width, bool& tail) {
-    int t = u, sub = 0;
-    tail = u >= p.dp_tiles;
+// Work unit u -> tile index t, output tile (tm, tn), first output column and width of the
+// unit, whether it is a tail slice, and its split-K index (split-K and tail slices are never
+// combined: with splits > 1, unit u is split u % splits of tile u / splits).
+__device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& t, int& tm, int& tn,
+                                          int& n_first, int& width, bool& tail, int& split) {
+    t = u;
+    int sub = 0;
+    split = 0;
+    if (p.splits > 1) {
+        t = u / p.splits;
+        split = u - t * p.splits;
+        tail = false;
+    } else {
+        tail = u >= p.dp_tiles;
+    }
     if (tail) {
         const int v = u - p.dp_tiles;
         t = p.dp_tiles + v / p.tail_split;
@@ -128,15 +138,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
             uint32_t phase = 0;
             bool ok = true;
             for (int u = cluster_id; u < p.num_units && ok; u += num_clusters) {
-                int tm, tn, n_first, width;
+                int t, tm, tn, n_first, width, split, kb0, kb1;
                 bool tail;
-                pair_unit(p, u, tm, tn, n_first, width, tail);
+                pair_unit(p, u, t, tm, tn, n_first, width, tail, split);
+                split_range(p, split, kb0, kb1);
                 const int m0 = tm * kPairBM + (int)rank * 128;
                 const int n0 = n_first + (int)rank * (width >> 1);
                 const CUtensorMap* mapB = tail ? &tmBt : &tmB;
                 // pair total: 2 x (A half 16 KiB + B half width/2 rows x 128 B)
                 const uint32_t bytes = 2u * (kHalfBytes + (uint32_t)(width >> 1) * 128u);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     B2G_TIC(t_empty);
                     if (!mbar_wait<true>(empty0 + 8 * stage, phase ^ 1u, w)) {
                         ok = false;
@@ -177,7 +188,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
             int it = 0;
             bool ok = true;
             for (int u = cluster_id; u < p.num_units && ok; u += num_clusters, ++it) {
-                const uint32_t idesc = u >= p.dp_tiles ? p.idesc_tail : p.idesc;
+                int t, tm, tn, n_first, width, split, kb0, kb1;
+                bool tail;
+                pair_unit(p, u, t, tm, tn, n_first, width, tail, split);
+                split_range(p, split, kb0, kb1);
+                const uint32_t idesc = tail ? p.idesc_tail : p.idesc;
                 const int buf = it & 1;
                 const uint32_t use = (uint32_t)(it >> 1) & 1u;
                 B2G_TIC(t_te);
@@ -189,7 +204,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                 if (lane == 0) B2G_COUNT(7, 1);
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kPairBN);
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     B2G_TIC(t_full);
                     if (!mbar_wait_warp(full0 + 8 * stage, phase, w)) {
                         ok = false;
@@ -200,7 +215,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                     const uint64_t ad = adesc0 + (uint64_t)((uint32_t)stage * kStageStep);
                     const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kStageStep);
                     if (elect_one()) {
-                        mma_f16_ss<2>(d_tmem, ad, bd, idesc, kb > 0 ? 1u : 0u);
+                        mma_f16_ss<2>(d_tmem, ad, bd, idesc, kb > kb0 ? 1u : 0u);
                         mma_f16_ss<2>(d_tmem, ad + 2, bd + 2, idesc, 1u);
                         mma_f16_ss<2>(d_tmem, ad + 4, bd + 4, idesc, 1u);
                         mma_f16_ss<2>(d_tmem, ad + 6, bd + 6, idesc, 1u);
@@ -240,19 +255,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
             if (!__all_sync(0xffffffffu, ok)) break;
             if (warp == 2 && lane == 0) B2G_TOC(3, t_tf);
             tc_fence_after();
-            int tm, tn, n_first, width;
+            int t, tm, tn, n_first, width, split;
             bool tail;
-            pair_unit(p, u, tm, tn, n_first, width, tail);
+            pair_unit(p, u, t, tm, tn, n_first, width, tail, split);
             const int row0 = tm * kPairBM + (int)rank * 128 + q * 32;
             const uint32_t tbase =
                 tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kPairBN);
+            auto release = [&] {  // accumulator `buf` has been read: the leader may reuse it
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_remote(tempty0_leader + 8 * buf);
+            };
             B2G_TIC(t_epi);
-            epilogue_rows(p, es, &tmD, tbase, row0, n_first, width, c_first, stage0, lane, seq,
-                          acc16, epi);
+            if (p.splits > 1) {
+                splitk_epilogue(p, es, &tmD, tbase, t, split, (int)rank, 2, q, warp - 2, kPairBN,
+                                row0, n_first, c_first, stage0, lane, seq, epi, release);
+            } else {
+                epilogue_rows(p, es, &tmD, tbase, row0, n_first, width, c_first, stage0, lane,
+                              seq, acc16, epi);
+                release();
+            }
             if (warp == 2 && lane == 0) B2G_TOC(4, t_epi);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_remote(tempty0_leader + 8 * buf);
         }
         if (lane == 0) bulk_wait<0>();  // this warp's TMA stores have completed
         __syncwarp();

@@ -19,7 +19,8 @@ enum : uint32_t {
     kErrWaitEpilogue = 1u << 2,  // epilogue gave up waiting for a finished accumulator
     kErrWaitSelftest = 1u << 3,  // the self-test's deliberately unsatisfied wait
     kErrWaitDrain = 1u << 4,     // teardown gave up waiting for in-flight async work
-    kErrWaitProbe = 1u << 5      // issue-rate probe gave up waiting for its MMAs
+    kErrWaitProbe = 1u << 5,     // issue-rate probe gave up waiting for its MMAs
+    kErrSplitCounter = 1u << 6   // a split-K arrival counter update did not go through
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -139,7 +140,8 @@ __device__ __forceinline__ void clock_mark(int at_exit) {
 // lifetime. Slots: 0 producer/empty, 1 MMA/full, 2 MMA/tmem_empty, 3 epilogue/tmem_full
 // (warp 2), 4 epilogue work (warp 2), 5 CTA lifetime, 6 k-blocks issued, 7 units;
 // epilogue chunk phases of thread 64 (warp 2, lane 0): 8 TMEM load + wait, 9 convert +
-// shared stores, 10 wait for the staging box, 11 fence + store issue, 12 chunks.
+// shared stores, 10 wait for the staging box, 11 fence + store issue, 12 chunks; split-K
+// units instead: 12 reduction cycles, 13 partial store + release, 14 arrival, 15 reductions.
 #ifdef B2G_INSTRUMENT
 constexpr int kInstrSlots = 16;
 __device__ unsigned long long g_b2g_instr[1024][kInstrSlots];
@@ -234,6 +236,29 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
         " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1)
         : "memory");
+}
+
+__device__ __forceinline__ unsigned short ld_shared_u16(uint32_t addr) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+// gpu-scope relaxed load and acquire-release compare-and-swap (split-K arrival counters).
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ unsigned long long atom_cas_acq_rel_gpu_u64(unsigned long long* p,
+                                                                       unsigned long long cmp,
+                                                                       unsigned long long val) {
+    unsigned long long old;
+    asm volatile("atom.acq_rel.gpu.global.cas.b64 %0, [%1], %2, %3;"
+                 : "=l"(old)
+                 : "l"(p), "l"(cmp), "l"(val)
+                 : "memory");
+    return old;
 }
 
 // L2 cache policies (createpolicy) for the `.L2::cache_hint` forms below.

@@ -86,6 +86,24 @@ int b2g_gemm(const void* A, const void* B, void* D, const void* bias, int M, int
              long long lda, long long ldb, long long ldd, int b_layout, int acc, int epilogue,
              float alpha, int tile, int stages, int group, void* stream);
 
+/* b2g_gemm with an explicit split-K factor. No counterpart in the reference, whose kernel
+ * collapses on skinny shapes (docs/RESULTS.md:249-265: M = 1..128 with N = K = 4096 keep
+ * 0.4-44% of its square-GEMM throughput) and names split-K as the fix.
+ *   splits : 0 = automatic (what b2g_gemm does: split only when the output tiles fill less
+ *            than half of the SMs, FP32 accumulation only), 1 = never, S >= 2 = split the
+ *            K range of every tile into S even parts (S <= ceil(K / 64); acc must be
+ *            B2G_ACC_F32, else B2G_ERR_UNSUPPORTED).
+ * Each split writes its FP32 partial tile to a workspace; the split that finishes last sums
+ * the partials in split order 0..S-1 (deterministic) and applies the epilogue. The workspace
+ * belongs to the library, one per (device, stream), allocated with cudaMalloc on first use
+ * and grown when a larger one is needed (after synchronising that stream). Growing is
+ * refused with B2G_ERR_UNSUPPORTED while the stream is being captured, so run a call of
+ * each split shape once before capturing it into a CUDA graph. */
+int b2g_gemm_splitk(const void* A, const void* B, void* D, const void* bias, int M, int N,
+                    int K, long long lda, long long ldb, long long ldd, int b_layout, int acc,
+                    int epilogue, float alpha, int tile, int stages, int group, int splits,
+                    void* stream);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* b2g_last_error(void);
 
@@ -109,13 +127,14 @@ int b2g_kernel_clock(double* sm_mhz, double* cta0_us);
 int b2g_config_info(int tile, int stages, int* threads, int* regs, int* smem_bytes,
                     int* ctas_per_sm, int* tmem_cols, int* stages_used);
 
-/* The most recent GEMM kernel launch made by b2g_gemm on the calling host thread: grid
- * size, threads per CTA (64 + 32 x epilogue warps: 8 epilogue warps when K <= 1024, else
- * 4), the tile and stage count chosen, and the work units (tiles plus tail slices). The
- * reference prints the same launch facts per configuration (src/gemm_bench.cu:458-472);
- * here they depend on the shape, so they are read back after the call. Any output pointer
- * may be NULL; B2G_ERR_ARG if this thread has not launched a GEMM yet. */
-int b2g_last_launch(int* grid, int* threads, int* tile, int* stages, int* units);
+/* The most recent GEMM kernel launch made by b2g_gemm / b2g_gemm_splitk on the calling host
+ * thread: grid size, threads per CTA (64 + 32 x epilogue warps: 8 epilogue warps when
+ * K <= 1024, else 4), the tile and stage count chosen, the work units (tiles x splits, plus
+ * tail slices) and the split-K factor. The reference prints the same launch facts per
+ * configuration (src/gemm_bench.cu:458-472); here they depend on the shape, so they are read
+ * back after the call. Any output pointer may be NULL; B2G_ERR_ARG if this thread has not
+ * launched a GEMM yet. */
+int b2g_last_launch(int* grid, int* threads, int* tile, int* stages, int* units, int* splits);
 
 /* cuBLAS comparison column: exactly the reference's call (src/gemm_bench.cu:625-633):
  * cublasGemmEx(OP_T, OP_N, N, M, K, alpha, B, 16F, K, A, 16F, K, beta=0, D, 16F, N,

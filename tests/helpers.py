@@ -32,7 +32,7 @@ def to_host(t):
 
 def run(torch, A, B, bias=None, *, acc=b2g.ACC_F32, epilogue=b2g.EPI_NONE, alpha=1.0,
         tile=b2g.TILE_AUTO, stages=0, group=1, lda=None, ldb=None, ldd=None,
-        b_layout=b2g.B_NK):
+        b_layout=b2g.B_NK, splits=None):
     """Run the library GEMM on host inputs; returns D (numpy uint16, M x N)."""
     M, K = A.shape
     N = B.shape[0] if b_layout == b2g.B_NK else B.shape[1]
@@ -44,7 +44,7 @@ def run(torch, A, B, bias=None, *, acc=b2g.ACC_F32, epilogue=b2g.EPI_NONE, alpha
     else:
         dD = torch.full((M, ldd), float("nan"), dtype=torch.float16, device="cuda")[:, :N]
     b2g.gemm(dA, dB, dD, dbias, b_layout=b_layout, acc=acc, epilogue=epilogue, alpha=alpha,
-             tile=tile, stages=stages, group=group)
+             tile=tile, stages=stages, group=group, splits=splits)
     b2g.sync_status()
     return to_host(dD)
 

@@ -74,9 +74,10 @@ def test_pair_tail_slices(cuda, shape):
 @pytest.mark.parametrize("K,warps", [(1024, 8), (1088, 4), (64, 8)])
 @pytest.mark.parametrize("mode", ["plain", "fused", "f16acc"])
 def test_epilogue_warps_by_k(cuda, tile, K, warps, mode):
-    """K <= 1024 launches 8 epilogue warps (two per TMEM lane quarter, alternate 64-column
-    chunks, one staging box each), longer K launches 4 (two boxes each); both give the same
-    result in every epilogue mode, including the 128-column tail slices of the 2-CTA kernel."""
+    """Without split-K, K <= 1024 launches 8 epilogue warps (two per TMEM lane quarter,
+    alternate 64-column chunks, one staging box each) and longer K launches 4 (two boxes
+    each); both give the same result in every epilogue mode, including the 64-column tail
+    slices of the 2-CTA kernel."""
     M, N = 640, 704
     A, B, bias = inputs(M, N, K, seed=21, lo=-0.5, hi=0.5)
     kw = {}
@@ -84,7 +85,7 @@ def test_epilogue_warps_by_k(cuda, tile, K, warps, mode):
         kw = dict(epilogue=b2g.EPI_BIAS_RELU, alpha=0.75)
     elif mode == "f16acc":
         kw = dict(acc=b2g.ACC_F16)
-    D = run(cuda, A, B, bias if mode == "fused" else None, tile=tile, **kw)
+    D = run(cuda, A, B, bias if mode == "fused" else None, tile=tile, splits=1, **kw)
     launch = b2g.last_launch()
     assert launch["threads"] == 64 + 32 * warps, launch
     assert launch["tile"] == tile
@@ -171,6 +172,28 @@ def test_unaligned_output_ld(cuda):
     D = run(cuda, A, B, ldd=301)
     frob, maxrel = check_rows(A, B, D, list(range(200)))
     assert frob <= FROB_F32 and maxrel <= ELEM_F32
+
+
+@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_256x256_2SM])
+@pytest.mark.parametrize("fused", [False, True])
+def test_unaligned_output_base(cuda, tile, fused):
+    """D starting 2 bytes past a 16-byte boundary (no TMA store possible): the staging box is
+    written out with plain row stores; neighbours outside D stay untouched."""
+    torch = cuda
+    M, N, K = 333, 520, 192
+    A, B, bias = inputs(M, N, K, seed=8)
+    buf = torch.full((M, N + 8), float("nan"), dtype=torch.float16, device="cuda")
+    dD = buf[:, 1:N + 1]
+    kw = dict(epilogue=b2g.EPI_BIAS_RELU, alpha=1.5) if fused else {}
+    b2g.gemm(to_dev(torch, A), to_dev(torch, B), dD, to_dev(torch, bias) if fused else None,
+             tile=tile, **kw)
+    b2g.sync_status()
+    out = to_host(buf)
+    frob, maxrel = check_rows(A, B, np.ascontiguousarray(out[:, 1:N + 1]), list(range(M)),
+                              bias=bias if fused else None, alpha=kw.get("alpha", 1.0),
+                              epilogue=fused)
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+    assert np.isnan(O.f16_to_f32(out[:, 0])).all() and np.isnan(O.f16_to_f32(out[:, N + 1:])).all()
 
 
 def test_k_zero_and_empty(cuda):

@@ -1,0 +1,116 @@
+"""Split-K GPU tests (b2g_gemm_splitk and the automatic split in b2g_gemm), against the FP64
+oracle. The reference has no split-K; its skinny-M collapse (docs/RESULTS.md:249-265, M = 1..128
+with N = K = 4096) is the case split-K exists for, so those shapes are checked here too."""
+import numpy as np
+import pytest
+
+import b2g
+import oracle as O
+from helpers import check_rows, inputs, run, sample_rows, to_dev, to_host
+
+pytestmark = pytest.mark.gpu
+
+FROB_F32 = 1e-3
+ELEM_F32 = 2 * 2.0 ** -11
+
+
+@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM])
+@pytest.mark.parametrize("splits", [2, 3, 7, 16])
+@pytest.mark.parametrize("fused", [False, True])
+def test_forced_splits(cuda, tile, splits, fused):
+    """Every tile kernel with S splits of K = 1000 (16 k-blocks, uneven shares, a ragged last
+    k-block) on ragged M and N, with and without the fused alpha/bias/ReLU epilogue."""
+    M, N, K = 300, 520, 1000
+    A, B, bias = inputs(M, N, K, seed=31)
+    lda = (K + 7) // 8 * 8
+    kw = dict(epilogue=b2g.EPI_BIAS_RELU, alpha=0.5) if fused else {}
+    D = run(cuda, A, B, bias if fused else None, tile=tile, splits=splits, lda=lda, ldb=lda, **kw)
+    launch = b2g.last_launch()
+    assert launch["splits"] == splits and launch["units"] % splits == 0, launch
+    frob, maxrel = check_rows(A, B, D, list(range(M)), bias=bias if fused else None,
+                              alpha=kw.get("alpha", 1.0), epilogue=fused)
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+@pytest.mark.parametrize("splits", [2, 4])
+def test_split_unaligned_output(cuda, splits):
+    """Split-K with an output pitch TMA cannot store (ldd = N + 3): the last split writes
+    its sums through the plain-store path."""
+    M, N, K = 200, 300, 1024
+    A, B, _ = inputs(M, N, K, seed=39)
+    D = run(cuda, A, B, tile=b2g.TILE_128x128, splits=splits, ldd=N + 3)
+    frob, maxrel = check_rows(A, B, D, list(range(M)))
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+def test_split_result_is_deterministic_and_close_to_unsplit(cuda):
+    """The last split sums partials in split order, so repeated runs are bit-identical; the
+    split sum differs from the single-pass accumulation only by FP32 rounding."""
+    M, N, K = 256, 768, 4096
+    A, B, _ = inputs(M, N, K, seed=32)
+    outs = [run(cuda, A, B, splits=8) for _ in range(3)]
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+    one = run(cuda, A, B, splits=1)
+    d = np.abs(O.f16_to_f32(outs[0]) - O.f16_to_f32(one))
+    assert d.max() <= 2.0 ** -9 * max(1.0, np.abs(O.f16_to_f32(one)).max()), d.max()
+
+
+@pytest.mark.parametrize("M,split", [(1, True), (8, True), (32, True), (128, True),
+                                     (512, False)])
+def test_skinny_decode_auto_split(cuda, M, split):
+    """The reference's Phase 6 shapes (N = K = 4096): b2g_gemm splits K automatically when
+    128 x 128 tiles leave most SMs idle (M <= 128 here); 2-CTA pair tiles (M = 512) are
+    never split automatically."""
+    N = K = 4096
+    A, B, _ = inputs(M, N, K, seed=33)
+    D = run(cuda, A, B)
+    launch = b2g.last_launch()
+    assert (launch["splits"] > 1) == split, launch
+    rows = sample_rows(M, 32)
+    frob, maxrel = check_rows(A, B, D, rows)
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+def test_split_rejections(cuda):
+    A, B, _ = inputs(64, 64, 128, seed=34)
+    with pytest.raises(b2g.B2GError) as e:
+        run(cuda, A, B, acc=b2g.ACC_F16, splits=2)
+    assert e.value.code == b2g.ERR_UNSUPPORTED
+    with pytest.raises(b2g.B2GError) as e:
+        run(cuda, A, B, splits=3)  # K = 128 has 2 k-blocks
+    assert e.value.code == b2g.ERR_ARG
+    with pytest.raises(b2g.B2GError) as e:
+        run(cuda, A, B, splits=-1)
+    assert e.value.code == b2g.ERR_ARG
+    # FP16 accumulation never splits automatically
+    A, B, _ = inputs(8, 512, 4096, seed=35, lo=-0.5, hi=0.5)
+    run(cuda, A, B, acc=b2g.ACC_F16)
+    assert b2g.last_launch()["splits"] == 1
+
+
+def test_workspace_growth_and_streams(cuda):
+    """Shapes that need a larger workspace in turn, then two streams at once: each stream
+    has its own partials and counters, so concurrent split GEMMs do not interfere."""
+    torch = cuda
+    cases = [(64, 256, 512, 2), (128, 2048, 2048, 8), (256, 4096, 4096, 4), (64, 256, 512, 2)]
+    for M, N, K, S in cases:
+        A, B, _ = inputs(M, N, K, seed=36)
+        D = run(cuda, A, B, splits=S)
+        frob, maxrel = check_rows(A, B, D, sample_rows(M, 16))
+        assert frob <= FROB_F32 and maxrel <= ELEM_F32, (M, N, K, S, frob, maxrel)
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    jobs = []
+    for seed, st in ((37, s1), (38, s2)):
+        A, B, _ = inputs(128, 2048, 2048, seed=seed)
+        dA, dB = to_dev(torch, A), to_dev(torch, B)
+        dD = torch.empty(128, 2048, dtype=torch.float16, device="cuda")
+        jobs.append((A, B, dA, dB, dD, st))
+    torch.cuda.synchronize()
+    for rep in range(4):
+        for A, B, dA, dB, dD, st in jobs:
+            b2g.gemm(dA, dB, dD, stream=st, splits=8)
+    torch.cuda.synchronize()
+    b2g.sync_status()
+    for A, B, dA, dB, dD, st in jobs:
+        frob, maxrel = check_rows(A, B, to_host(dD), sample_rows(128, 16))
+        assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
