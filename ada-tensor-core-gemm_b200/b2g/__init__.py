@@ -38,7 +38,7 @@ EXPORTS = (
     "b2g_max_rel_diff", "b2g_bias_relu", "b2g_probe_tcgen05", "b2g_probe_hbm",
     "b2g_fill_lcg_f16", "b2g_fill_uniform_f16", "b2g_tile_coord",
     "b2g_selftest_wait_timeout", "b2g_set_wait_timeout_us", "b2g_version",
-    "b2g_kernel_clock", "b2g_last_launch", "b2g_gemm_splitk",
+    "b2g_kernel_clock", "b2g_last_launch", "b2g_gemm_splitk", "b2g_gemm_splitk_noalloc",
 )
 
 
@@ -71,6 +71,8 @@ def lib():
         L.b2g_gemm_splitk.restype = i
         L.b2g_gemm_splitk.argtypes = [vp, vp, vp, vp, i, i, i, ll, ll, ll, i, i, i, f, i, i, i,
                                       i, vp]
+        L.b2g_gemm_splitk_noalloc.restype = i
+        L.b2g_gemm_splitk_noalloc.argtypes = L.b2g_gemm_splitk.argtypes
         L.b2g_last_error.restype = C.c_char_p
         L.b2g_last_error.argtypes = []
         L.b2g_sync_status.restype = i
@@ -178,6 +180,22 @@ def gemm(A, B, D, bias=None, *, b_layout: int = B_NK, acc: int = ACC_F32,
     gemm_raw(_ptr(A), _ptr(B), _ptr(D), _ptr(bias), M, N, K, A.stride(0), B.stride(0),
              D.stride(0), b_layout, acc, epilogue, alpha, tile, stages, group,
              _stream_ptr(stream), splits)
+
+
+def gemm_noalloc(A, B, D, bias=None, *, b_layout: int = B_NK, acc: int = ACC_F32,
+                 epilogue: int = EPI_NONE, alpha: float = 1.0, tile: int = TILE_AUTO,
+                 stages: int = 0, group: int = 1, stream=None, splits: int = 0) -> None:
+    """:func:`gemm` through b2g_gemm_splitk_noalloc: no device memory is allocated; split-K
+    uses the library's fixed static scratch (B2GError ERR_ARG if a split needs more).
+    Calls that can overlap on one device share that scratch, so serialise them."""
+    M, K = A.shape
+    N = B.shape[0] if b_layout == B_NK else B.shape[1]
+    if tuple(D.shape) != (M, N):
+        raise B2GError(ERR_ARG, f"D shape {tuple(D.shape)} != ({M}, {N})")
+    _check(lib().b2g_gemm_splitk_noalloc(_ptr(A), _ptr(B), _ptr(D), _ptr(bias), M, N, K,
+                                         A.stride(0), B.stride(0), D.stride(0), b_layout, acc,
+                                         epilogue, alpha, tile, stages, group, splits,
+                                         _stream_ptr(stream)))
 
 
 def sync_status(stream=None) -> None:

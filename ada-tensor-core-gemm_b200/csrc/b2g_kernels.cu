@@ -356,6 +356,58 @@ int managed_scratch(const DeviceInfo& di, cudaStream_t s, size_t part_bytes, siz
     return B2G_OK;
 }
 
+// ---------------------------------------------------------------------------------------
+// No-allocation split-K scratch (b2g_gemm_splitk_noalloc)
+// ---------------------------------------------------------------------------------------
+// For callers that must not allocate device memory at call time (a process that has handed
+// all free HBM to its own caching allocator or to a fixed memory budget, or code running in
+// a context where an allocation or the stream synchronisation that growing a workspace needs
+// is not acceptable). The scratch is this file-scope array, created with the module when the
+// library is first used on a device; the library never frees or grows it.
+//   [counters: kNoAllocCounters x 8 bytes][FP32 partials: kNoAllocPartBytes]
+// The counters must start at zero, and do: a __device__ array without an initializer is
+// zero-filled when the module is loaded. They never need clearing afterwards (epoch tags,
+// see splitk_arrive); epochs of this scratch start at 1. The partials need no initial value.
+constexpr size_t kNoAllocCounters = 32768;                  // (tile, CTA) groups x 8 warps
+constexpr size_t kNoAllocPartBytes = (size_t)16 << 20;      // 16 MiB of FP32 partials
+constexpr size_t kNoAllocCounterBytes = kNoAllocCounters * sizeof(unsigned long long);
+static __device__ __align__(256) unsigned char
+    g_b2g_noalloc_scratch[kNoAllocCounterBytes + kNoAllocPartBytes];
+
+// Scratch of one launch from the static array of the current device. The array's address is
+// looked up once per device (with that device current, as here). One array per device is
+// shared by every call of b2g_gemm_splitk_noalloc on that device, so calls that may overlap
+// on the GPU (different streams or host threads) race on it.
+int static_scratch(const DeviceInfo& di, size_t part_bytes, size_t count_entries,
+                   SplitScratch* out) {
+    if (part_bytes > kNoAllocPartBytes || count_entries > kNoAllocCounters)
+        return fail(B2G_ERR_ARG,
+                    "split-K needs %zu bytes of partials and %zu counters, more than the "
+                    "no-allocation scratch holds (%zu bytes, %zu counters): use fewer splits "
+                    "or tiles, or b2g_gemm_splitk",
+                    part_bytes, count_entries, kNoAllocPartBytes, kNoAllocCounters);
+    if (di.device < 0 || di.device >= kMaxDevices)
+        return fail(B2G_ERR_ARG, "device %d is beyond the no-allocation scratch table (%d)",
+                    di.device, kMaxDevices);
+    static std::mutex mu;
+    static void* base[kMaxDevices] = {};
+    static unsigned int epoch[kMaxDevices] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (base[di.device] == nullptr) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_b2g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr)
+            return fail(B2G_ERR_CUDA, "cudaGetSymbolAddress(no-allocation split-K scratch): %s",
+                        cudaGetErrorString(e));
+        base[di.device] = p;
+    }
+    if (++epoch[di.device] == 0) epoch[di.device] = 1;
+    unsigned char* b = static_cast<unsigned char*>(base[di.device]);
+    *out = SplitScratch{reinterpret_cast<float*>(b + kNoAllocCounterBytes),
+                        reinterpret_cast<unsigned long long*>(b), epoch[di.device]};
+    return B2G_OK;
+}
+
 int elementwise_grid(size_t n, int sm_count) {
     const size_t blocks = (n + 255) / 256;
     const size_t cap = (size_t)sm_count * 8;
@@ -373,11 +425,14 @@ using namespace b2g;
 namespace b2g {
 namespace {
 
-// Everything of b2g_gemm / b2g_gemm_splitk after argument decoding. `splits`: 0 = automatic,
-// 1 = no split-K, >= 2 = that many K splits (FP32 accumulation only).
+// Everything of b2g_gemm / b2g_gemm_splitk / b2g_gemm_splitk_noalloc after argument
+// decoding. `splits`: 0 = automatic, 1 = no split-K, >= 2 = that many K splits (FP32
+// accumulation only). `noalloc`: split-K scratch from the static array instead of the
+// library-managed per-stream workspace.
 int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, int N, int K,
               long long lda, long long ldb, long long ldd, int b_layout, int acc, int epilogue,
-              float alpha, int tile, int stages, int group, int splits, cudaStream_t s) {
+              float alpha, int tile, int stages, int group, int splits, cudaStream_t s,
+              bool noalloc = false) {
     if (M < 0 || N < 0 || K < 0)
         return fail(B2G_ERR_ARG, "negative shape M=%d N=%d K=%d", M, N, K);
     if (b_layout != B2G_B_NK && b_layout != B2G_B_KN)
@@ -484,7 +539,9 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         const size_t part = (size_t)p.num_tiles * splits * g.ctas * 128 * g.bn * sizeof(float);
         const size_t counters = (size_t)p.num_tiles * g.ctas * kMaxEpiWarps;
         SplitScratch sc{};
-        if (int rc = managed_scratch(di, s, part, counters, &sc)) return rc;
+        if (int rc = noalloc ? static_scratch(di, part, counters, &sc)
+                             : managed_scratch(di, s, part, counters, &sc))
+            return rc;
         p.ws_part = sc.part;
         p.ws_count = sc.count;
         p.epoch = sc.epoch;
@@ -539,6 +596,16 @@ B2G_EXPORT int b2g_gemm_splitk(const void* A, const void* B, void* D, const void
     clear_error();
     return gemm_impl(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc, epilogue, alpha, tile,
                      stages, group, splits, (cudaStream_t)stream);
+}
+
+B2G_EXPORT int b2g_gemm_splitk_noalloc(const void* A, const void* B, void* D, const void* bias,
+                                       int M, int N, int K, long long lda, long long ldb,
+                                       long long ldd, int b_layout, int acc, int epilogue,
+                                       float alpha, int tile, int stages, int group, int splits,
+                                       void* stream) {
+    clear_error();
+    return gemm_impl(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc, epilogue, alpha, tile,
+                     stages, group, splits, (cudaStream_t)stream, true);
 }
 
 B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, int* smem_bytes,

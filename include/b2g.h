@@ -104,6 +104,26 @@ int b2g_gemm_splitk(const void* A, const void* B, void* D, const void* bias, int
                     int epilogue, float alpha, int tile, int stages, int group, int splits,
                     void* stream);
 
+/* b2g_gemm_splitk that allocates no device memory. No counterpart in the reference (which
+ * has no split-K and no workspace). For callers that cannot allocate at call time: a
+ * process whose free device memory is all held by its own caching allocator or a fixed
+ * memory budget, or code where a cudaMalloc, a cudaFree or the stream synchronisation that
+ * growing b2g_gemm_splitk's workspace needs is not acceptable.
+ * Same arguments and results as b2g_gemm_splitk. The split-K scratch is a static device
+ * array inside the library, one per device, of fixed size: 16 MiB of FP32 partials (a split
+ * GEMM needs tiles x splits x 128 x 128 x 4 bytes on 128 x 128 tiles, x 2 x 2 on 2-CTA
+ * 256 x 256 tiles) and 32768 counters (tiles x CTAs per tile x 8). A call needing more
+ * returns B2G_ERR_ARG (with the sizes in the message) and launches nothing; calls that do
+ * not split need no scratch. The counters must start at zero: they are zero-filled when the
+ * library's module is loaded on the device and never need clearing later.
+ * Limits: calls that can overlap on the same device (other streams, other host threads)
+ * share the one array and race, so serialise them; make the first call on each device before
+ * any stream capture, since it looks up the array's address (cudaGetSymbolAddress). */
+int b2g_gemm_splitk_noalloc(const void* A, const void* B, void* D, const void* bias, int M,
+                            int N, int K, long long lda, long long ldb, long long ldd,
+                            int b_layout, int acc, int epilogue, float alpha, int tile,
+                            int stages, int group, int splits, void* stream);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* b2g_last_error(void);
 
