@@ -690,6 +690,11 @@ B2G_EXPORT int b2g_instr_read(unsigned long long* out, int n_ctas) {
     return cudaMemcpyToSymbol(g_b2g_instr, zeros, sizeof(zeros)) == cudaSuccess ? B2G_OK
                                                                                 : B2G_ERR_CUDA;
 }
+B2G_EXPORT int b2g_instr_timeline(unsigned long long* out16) {
+    return cudaMemcpyFromSymbol(out16, g_b2g_tl, sizeof(unsigned long long) * 16) == cudaSuccess
+               ? B2G_OK
+               : B2G_ERR_CUDA;
+}
 #endif
 
 B2G_EXPORT int b2g_kernel_clock(double* sm_mhz, double* cta0_us) {

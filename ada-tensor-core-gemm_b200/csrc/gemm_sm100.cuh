@@ -251,6 +251,7 @@ __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiSc
         B2G_TIC(t_box);
         const uint32_t box = e.d_tma ? epi_box_acquire(e, stage0, seq, lane) : stage0;
         B2G_TOC64(10, t_box);
+        if (threadIdx.x == 64 && seq == 0) B2G_MARK(13);
         B2G_COUNT(12, threadIdx.x == 64 ? 1 : 0);
 #pragma unroll 1
         for (int h = 0; h < 2; ++h) {
@@ -262,12 +263,14 @@ __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiSc
             epi_box_put32<ACC16, EPI>(e, box, col, h, r, lane);
             B2G_TOC64(9, t_cvt);
         }
+        if (threadIdx.x == 64 && seq == 0) B2G_MARK(14);
         B2G_TIC(t_st);
         if (e.d_tma)
             epi_box_store(e, tmD, box, col, row0, lane, seq);
         else
             epi_box_store_rows(p, e, box, col, row0, lane);
         B2G_TOC64(11, t_st);
+        if (threadIdx.x == 64 && seq == 1) B2G_MARK(15);
     }
 }
 

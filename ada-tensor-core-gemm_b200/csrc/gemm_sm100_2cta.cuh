@@ -73,6 +73,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                     const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
     clock_mark(0);
     B2G_TIC(t_life);
+    if (threadIdx.x == 0) B2G_MARK(0);
     extern __shared__ uint8_t smem_dyn[];
     const uint32_t raw = smem_u32(smem_dyn);
     const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
@@ -127,8 +128,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
     const uint32_t full0_leader = mapa_shared(full0, 0);
     const uint32_t tempty0_leader = mapa_shared(tempty0, 0);
     // everything above overlapped the previous kernel; global memory only from here on
+    if (threadIdx.x == 0) B2G_MARK(1);
     grid_dep_wait();
     grid_dep_launch();
+    if (threadIdx.x == 0) B2G_MARK(2);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -147,6 +150,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                 const CUtensorMap* mapB = tail ? &tmBt : &tmB;
                 // pair total: 2 x (A half 16 KiB + B half width/2 rows x 128 B)
                 const uint32_t bytes = 2u * (kHalfBytes + (uint32_t)(width >> 1) * 128u);
+                if (u == cluster_id) B2G_MARK(10);
                 for (int kb = kb0; kb < kb1; ++kb) {
                     B2G_TIC(t_empty);
                     if (!mbar_wait<true>(empty0 + 8 * stage, phase ^ 1u, w)) {
@@ -154,10 +158,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                         break;
                     }
                     B2G_TOC(0, t_empty);
+                    if (kb == kb0 && u == cluster_id) B2G_MARK(11);
                     if (leader) mbar_arrive_expect_tx(full0 + 8 * stage, bytes);
                     const uint32_t fb = full0_leader + 8 * stage;
                     tma_load_2d_pair(sA + stage * kHalfBytes, &tmA, fb, kb * kBK, m0);
+                    if (kb == kb0 && u == cluster_id) B2G_MARK(12);
                     tma_load_2d_pair(sB + stage * kHalfBytes, mapB, fb, kb * kBK, n0);
+                    if (kb == kb0 && u == cluster_id) B2G_MARK(3);
                     if (++stage == p.stages) {
                         stage = 0;
                         phase ^= 1u;
@@ -212,6 +219,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                     }
                     if (lane == 0) B2G_TOC(1, t_full);
                     if (lane == 0) B2G_COUNT(6, 1);
+                    if (lane == 0 && kb == kb0 && it == 0) B2G_MARK(4);
                     const uint64_t ad = adesc0 + (uint64_t)((uint32_t)stage * kStageStep);
                     const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kStageStep);
                     if (elect_one()) {
@@ -230,6 +238,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                 if (!ok) break;
                 if (elect_one()) mma_commit_pair(tfull0 + 8 * buf, 0x3);  // final in both CTAs
                 __syncwarp();
+                if (lane == 0) B2G_MARK(5);
             }
             const WaitCtx wd{p.timeout_ns, no_abort, kErrWaitDrain};
             if (elect_one()) mma_commit_2(drain);
@@ -254,6 +263,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
             const bool ok = mbar_wait<true>(tfull0 + 8 * buf, use, w);
             if (!__all_sync(0xffffffffu, ok)) break;
             if (warp == 2 && lane == 0) B2G_TOC(3, t_tf);
+            if (warp == 2 && lane == 0) B2G_MARK(6);
             tc_fence_after();
             int t, tm, tn, n_first, width, split;
             bool tail;
@@ -276,9 +286,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                 release();
             }
             if (warp == 2 && lane == 0) B2G_TOC(4, t_epi);
+            if (warp == 2 && lane == 0) B2G_MARK(7);
         }
         if (lane == 0) bulk_wait<0>();  // this warp's TMA stores have completed
         __syncwarp();
+        if (warp == 2 && lane == 0) B2G_MARK(8);
     }
 
     // teardown: no CTA may leave while its peer can still signal its barriers or while
@@ -292,6 +304,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
         tmem_dealloc<2>(tmem_base, kPairTmemCols);
     }
     if (threadIdx.x == 0) B2G_TOC(5, t_life);
+    if (threadIdx.x == 0) B2G_MARK(9);
     clock_mark(1);
 }
 

@@ -151,7 +151,12 @@ __device__ unsigned long long g_b2g_instr[1024][kInstrSlots];
 #define B2G_COUNT(slot, n) atomicAdd(&g_b2g_instr[blockIdx.x][slot], (unsigned long long)(n))
 #define B2G_TOC64(slot, v) \
     if (threadIdx.x == 64) B2G_TOC(slot, v)
+// Timeline of CTA 0 (globaltimer ns): mark i is written by whichever thread reaches it.
+__device__ unsigned long long g_b2g_tl[16];
+#define B2G_MARK(i) \
+    if (blockIdx.x == 0) g_b2g_tl[i] = globaltimer_ns()
 #else
+#define B2G_MARK(i)
 #define B2G_TOC64(slot, v)
 #define B2G_TIC(v)
 #define B2G_TOC(slot, v)

@@ -53,6 +53,17 @@ WORKLOADS = {
                     name="configs[4]: 32768x32768x8192 FP16 in, FP32 acc, M split over GPUs"),
 }
 
+# BASELINE configs[3] shape sweep (FP16 in, FP32 acc, U[-1,1], seed = 100 + index), and the
+# reference's Phase 6 decode sweep (docs/RESULTS.md:249-265: M = 1..4096, N = K = 4096).
+SWEEPS = {
+    "config4": [(256, 256, 256), (512, 512, 512), (1024, 1024, 1024), (2048, 2048, 2048),
+                (4096, 4096, 4096), (8192, 8192, 8192), (16384, 16384, 16384),
+                (4095, 4095, 4095), (5000, 3000, 2000), (16384, 16384, 256),
+                (256, 16384, 16384)],
+    "decode": [(m, 4096, 4096) for m in (1, 8, 32, 128, 512, 2048, 4096)],
+}
+SWEEPS["all"] = SWEEPS["config4"] + SWEEPS["decode"]
+
 NVML_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                 0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
                 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
@@ -74,6 +85,13 @@ def parse():
                    help="target CPU time of the bounded cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--allgather", action="store_true")
+    p.add_argument("--sweep", choices=tuple(SWEEPS), default=None,
+                   help="per-shape table (one JSON line per shape, then a markdown table) "
+                        "instead of the single bench line")
+    p.add_argument("--soak", type=float, default=0.0,
+                   help="seconds of back-to-back GEMMs of --workload in windows, with clock, "
+                        "power and temperature telemetry (SOAK, lines + a summary line)")
+    p.add_argument("--window", type=float, default=2.0, help="soak window seconds")
     return p.parse_args()
 
 
@@ -526,10 +544,289 @@ def ref_kernel_on_gpu(R, A, B, M, N, K, wl, args):
             "build": "compute_89 PTX from src/gemm_bench.cu, JIT by the driver"}
 
 
+# ---------------------------------------------------------------------------------------
+# shape sweep and soak -- single GPU, rank 0
+# ---------------------------------------------------------------------------------------
+def _ld8(k):
+    return (k + 7) // 8 * 8  # TMA row strides are multiples of 16 bytes: pad odd K
+
+
+def _time_launches(launch, steps, warmup, stream):
+    """Mean device ms per launch of back-to-back launches; launch(i) uses input set i % n,
+    the sets together larger than L2, so no launch finds its inputs in L2."""
+    import torch
+
+    for i in range(warmup):
+        launch(i + 7919)  # sets far from the first timed ones
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        launch(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def sweep_ours(args):
+    """Per shape: our kernel and cuBLAS (device-timed), roofline fraction against
+    min(measured tensor peak, AI x measured HBM bandwidth), HBM GB/s, max-rel vs cuBLAS, and
+    a blocked FP32 CPU GEMM on a bounded row sample (the cpu_baseline leg)."""
+    import numpy as np
+    import torch
+
+    import b2g
+
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    peaks, peak_src = measured_peaks()
+    bw = peaks["hbm_gbs"]
+    ptc = peaks["bf16_tflops"]
+    rows_out = []
+    for idx, (M, N, K) in enumerate(SWEEPS[args.sweep]):
+        seed = 100 + idx
+        ld = _ld8(K)
+        hA = np.zeros((M, ld), np.uint16)
+        hB = np.zeros((N, ld), np.uint16)
+        hA[:, :K] = b2g.fill_uniform(M * K, seed, 0, -1.0, 1.0).reshape(M, K)
+        hB[:, :K] = b2g.fill_uniform(N * K, seed, 1, -1.0, 1.0).reshape(N, K)
+        # rotating input sets whose total exceeds twice the L2 (at least 2 sets)
+        set_bytes = 2 * (M * ld + N * ld + M * N)
+        nbuf = max(2, min(4096, math.ceil(2 * L2_BYTES / set_bytes)))
+        dA0 = torch.from_numpy(hA.view(np.float16)).cuda()
+        dB0 = torch.from_numpy(hB.view(np.float16)).cuda()
+        sets = [(dA0.clone(), dB0.clone(), torch.empty((M, N), dtype=torch.float16,
+                                                       device="cuda")) for _ in range(nbuf)]
+        del dA0, dB0
+        flop = 2.0 * M * N * K
+        # every set at least once per timed run (a set comes round again only after sets
+        # totalling > 2 x L2 have been read), and about a second of GPU time at most
+        steps = max(5, min(args.steps, int(2e15 / max(flop, 1) / 1000) + 5), min(nbuf, 4096))
+        warm = max(3, min(args.warmup, steps))
+
+        def ours(i):
+            dA, dB, dD = sets[i % nbuf]
+            b2g.gemm_raw(dA.data_ptr(), dB.data_ptr(), dD.data_ptr(), None, M, N, K, ld, ld, N,
+                         b2g.B_NK, b2g.ACC_F32, b2g.EPI_NONE, 1.0, args.tile, args.stages,
+                         args.group, sptr)
+
+        ms = _time_launches(ours, steps, warm, stream)
+        b2g.sync_status(sptr)
+        launch = b2g.last_launch()
+        kmhz, _ = b2g.kernel_clock()
+        # the reference's cuBLAS call takes lda = ldb = K: unpadded copies when K % 8 != 0
+        csets = sets if ld == K else [(a[:, :K].contiguous(), b[:, :K].contiguous(), d)
+                                      for a, b, d in sets]
+
+        def cub(i):
+            dA, dB, dD = csets[i % nbuf]
+            b2g.cublas_gemm(dA, dB, dD, sptr)
+
+        dRef = torch.empty((M, N), dtype=torch.float16, device="cuda")
+        b2g.cublas_gemm(csets[0][0], csets[0][1], dRef, sptr)
+        ours(0)
+        err = torch.zeros(1, dtype=torch.float32, device="cuda")
+        b2g.max_rel_diff(sets[0][2], dRef, err, sptr)
+        maxrel = float(err.item())
+        del dRef
+        cublas_ms = _time_launches(cub, steps, warm, stream)
+        del csets
+        alg_bytes = 2.0 * (M * K + N * K + M * N)
+        ai = flop / alg_bytes
+        roof = min(ptc, ai * bw / 1e3)  # TFLOP/s
+        tf = flop / (ms * 1e-3) / 1e12
+        row = {
+            "M": M, "N": N, "K": K, "seed": seed, "ms": round(ms, 5), "tflops": round(tf, 2),
+            "cublas_tflops": round(flop / (cublas_ms * 1e-3) / 1e12, 2) if cublas_ms else None,
+            "maxrel_vs_cublas": maxrel,
+            "roofline": {"bound": "tensor" if ai * bw / 1e3 >= ptc else "hbm",
+                         "ai_flop_per_byte": round(ai, 1), "peak_tflops": round(roof, 1),
+                         "frac": round(tf / roof, 4)},
+            "hbm_gbs_algorithmic": round(alg_bytes / (ms * 1e-3) / 1e9, 1),
+            "launch": launch, "kernel_sm_mhz": round(kmhz),
+            "l2": f"{nbuf} rotating input sets, {nbuf * set_bytes / 2**20:.0f} MiB > 2 x L2",
+        }
+        if not args.no_cpu_baseline:
+            row["cpu_baseline"] = cpu_baseline(hA[:, :K].copy(), hB[:, :K].copy(), N, K,
+                                               min(args.cpu_seconds, 2.0),
+                                               {"M": M})
+        print(json.dumps(row), flush=True)
+        rows_out.append(row)
+        del sets
+        torch.cuda.empty_cache()
+    print(f"\n| M | N | K | ours TFLOP/s | cuBLAS | ours/cuBLAS | bound | frac of roofline "
+          f"({peak_src} {ptc:.0f} TF/s, {bw:.0f} GB/s) | HBM GB/s | CPU FP32 TFLOP/s |")
+    print("|---:|---:|---:|---:|---:|---:|---|---:|---:|---:|")
+    for r in rows_out:
+        c = r["cublas_tflops"]
+        cpu = r.get("cpu_baseline", {}).get("value")
+        print(f"| {r['M']} | {r['N']} | {r['K']} | {r['tflops']:.1f} | "
+              f"{c if c is not None else '-'} | "
+              f"{(r['tflops'] / c) if c else float('nan'):.3f} | {r['roofline']['bound']} | "
+              f"{r['roofline']['frac']:.3f} | {r['hbm_gbs_algorithmic']:.0f} | "
+              f"{cpu if cpu is not None else '-'} |")
+
+
+def sweep_reference(args):
+    """Per shape: the reference's sm_89 kernel JIT-run on this B200 (README best config) and
+    its CPU code (cpu_spot_check's FP64 dot products) on the host cores."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+
+    if not O.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref.so not built"}))
+        return
+    R = O.ref()
+    try:
+        threads = len(os.sched_getaffinity(0))
+    except AttributeError:
+        threads = os.cpu_count() or 1
+    for idx, (M, N, K) in enumerate(SWEEPS[args.sweep]):
+        seed = 100 + idx
+        row = {"impl": "reference", "M": M, "N": N, "K": K, "seed": seed}
+        if K % 32 or N % 2:  # the reference's own requirement (src/gemm_bench.cu:746)
+            row["ref_sm89_on_b200"] = {"skip": "the reference requires K % 32 == 0"}
+        else:
+            A = O.fill_uniform((M, K), seed, 0, -1.0, 1.0)
+            B = O.fill_uniform((N, K), seed, 1, -1.0, 1.0)
+            wl = {"acc": "f32"}
+            a2 = argparse.Namespace(steps=max(3, min(args.steps, 20)), warmup=3)
+            try:
+                row["ref_sm89_on_b200"] = ref_kernel_on_gpu(R, A, B, M, N, K, wl, a2)
+            except Exception as e:  # noqa: BLE001
+                row["ref_sm89_on_b200"] = {"unavailable": str(e)[:200]}
+            import numpy as np
+
+            D = np.zeros((M, N), np.uint16)
+            rows = min(M, threads)
+            t = R.ref_cpu_rows(A, B, D, M, N, K, 0, rows, threads)
+            row["reference_cpu"] = {"tflops": round(2.0 * rows * N * K / max(t, 1e-9) / 1e12, 6),
+                                    "cores": threads, "sample": f"{rows} output rows"}
+        print(json.dumps(row), flush=True)
+
+
+class Telemetry(ClockSampler):
+    """ClockSampler plus memory clock, power, temperature and utilisation (soak)."""
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append((
+                    time.perf_counter(), nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM),
+                    self._reasons(), nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_MEM),
+                    nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0,
+                    nv.nvmlDeviceGetTemperature(self.h, nv.NVML_TEMPERATURE_GPU),
+                    nv.nvmlDeviceGetUtilizationRates(self.h).gpu))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
+
+
+def soak_ours(args):
+    """Back-to-back GEMMs of --workload for --soak seconds in --window windows (the
+    reference's soak mode, src/gemm_bench.cu SOAK lines and scripts/soak.ps1 telemetry)."""
+    import torch
+
+    import b2g
+
+    wl = WORKLOADS[args.workload]
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    acc = b2g.ACC_F32 if wl["acc"] == "f32" else b2g.ACC_F16
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    nbuf = 3
+    sets = []
+    hA = b2g.fill_uniform(M * K, wl["seed"], 0, wl["lo"], wl["hi"]).reshape(M, K)
+    hB = b2g.fill_uniform(N * K, wl["seed"], 1, wl["lo"], wl["hi"]).reshape(N, K)
+    import numpy as np
+
+    for _ in range(nbuf):
+        sets.append((torch.from_numpy(hA.view(np.float16)).cuda(),
+                     torch.from_numpy(hB.view(np.float16)).cuda(),
+                     torch.empty((M, N), dtype=torch.float16, device="cuda")))
+    flop = 2.0 * M * N * K
+
+    def launch(i):
+        dA, dB, dD = sets[i % nbuf]
+        b2g.gemm_raw(dA.data_ptr(), dB.data_ptr(), dD.data_ptr(), None, M, N, K, K, K, N,
+                     b2g.B_NK, acc, b2g.EPI_NONE, 1.0, args.tile, args.stages, args.group, sptr)
+
+    for i in range(max(3, args.warmup)):
+        launch(i)
+    b2g.sync_status(sptr)
+    tel = Telemetry(0, period_s=0.2)
+    tel.start()
+    print(f"# soak {args.soak:.0f} s, window {args.window:.1f} s, {wl['name']}")
+    print("SOAK,elapsed_s,window_ms,iters,tflops,ms_per_iter", flush=True)
+    t_start = time.perf_counter()
+    wins = []
+    i = 0
+    while time.perf_counter() - t_start < args.soak:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        n = 0
+        w0 = time.perf_counter()
+        while time.perf_counter() - w0 < args.window:
+            launch(i)
+            i += 1
+            n += 1
+            if n % 64 == 0:
+                e1.record(stream)
+                e1.synchronize()
+        e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        tf = flop * n / (ms * 1e-3) / 1e12
+        wins.append(tf)
+        print(f"SOAK,{time.perf_counter() - t_start:.2f},{ms:.1f},{n},{tf:.2f},{ms / n:.5f}",
+              flush=True)
+    tel.stop()
+    b2g.sync_status(sptr)
+    busy = [s for s in tel.samples if len(s) > 6 and s[6] >= 50]
+
+    def stat(k):
+        v = [s[k] for s in busy]
+        return {"avg": round(statistics.mean(v), 1), "min": min(v), "max": max(v)} if v else None
+
+    def drift(vals):
+        k = len(vals) // 3
+        if k < 1:
+            return None
+        a, b = statistics.mean(vals[:k]), statistics.mean(vals[-k:])
+        return {"first_third": round(a, 2), "last_third": round(b, 2),
+                "pct": round(100 * (b - a) / a, 2) if a else None}
+
+    bits = [s[2] for s in busy]
+    reasons = {n: sum(1 for b in bits if b & m) for m, n in NVML_REASONS.items() if m != 0x1}
+    out = {"soak": {
+        "workload": wl["name"], "seconds": args.soak, "window_s": args.window,
+        "windows": len(wins), "sustained_tflops": round(statistics.mean(wins), 2) if wins else None,
+        "tflops_min": round(min(wins), 2) if wins else None,
+        "tflops_max": round(max(wins), 2) if wins else None,
+        "tflops_drift": drift(wins),
+        "busy_samples": len(busy), "sm_mhz": stat(1), "mem_mhz": stat(3), "power_w": stat(4),
+        "temp_c": stat(5),
+        "sm_mhz_drift": drift([s[1] for s in busy]), "power_drift": drift([s[4] for s in busy]),
+        "temp_drift": drift([s[5] for s in busy]),
+        "reason_samples": {k: v for k, v in reasons.items() if v},
+    }}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
-        run_reference(args)
+        if args.sweep:
+            sweep_reference(args)
+        else:
+            run_reference(args)
+    elif args.sweep:
+        sweep_ours(args)
+    elif args.soak > 0:
+        soak_ours(args)
     else:
         run_ours(args)
 
