@@ -68,20 +68,6 @@ int make_tmap(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer, 
 // ---------------------------------------------------------------------------------------
 constexpr int kMaxDevices = 64;
 
-template <class K>
-int prepare_kernel(K kern, int device, size_t dyn_smem, bool (&done)[kMaxDevices],
-                   std::mutex& mu) {
-    std::lock_guard<std::mutex> lock(mu);
-    if (device >= 0 && device < kMaxDevices && done[device]) return B2G_OK;
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn_smem);
-    if (e != cudaSuccess)
-        return fail(B2G_ERR_CUDA, "cudaFuncSetAttribute(max dynamic smem %zu): %s", dyn_smem,
-                    cudaGetErrorString(e));
-    if (device >= 0 && device < kMaxDevices) done[device] = true;
-    return B2G_OK;
-}
-
 // Geometry of the three GEMM kernels: output tile, CTAs per tile, TMA box rows per CTA.
 struct TileGeom {
     int bm, bn;        // output tile of one CTA (1-CTA kernels) or of one CTA pair
@@ -169,10 +155,11 @@ int max_pair_clusters(const DeviceInfo& di, size_t smem) {
 // costs more than 1/split of a tile because every slice reloads the tile's whole A panel
 // (per k-block 16 KiB of A + 128 B x width/2 of B per CTA): measured on B200, a 128-column
 // slice takes ~0.55 and a 64-column slice ~0.4 of a whole tile's time.
-int tail_split_for(int rest, int clusters) {
+int tail_split_for(int rest, int clusters, int max_split) {
     int best = 1;
     double best_t = 1.0;
     for (const auto& sc : {std::pair<int, double>{2, 0.55}, std::pair<int, double>{4, 0.40}}) {
+        if (sc.first > max_split) continue;
         const double t = (double)((rest * sc.first + clusters - 1) / clusters) * sc.second;
         if (t < best_t - 1e-9) {
             best_t = t;
@@ -480,8 +467,6 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
                     "lda (%lld) and ldb (%lld) must be multiples of 8 elements: TMA row "
                     "strides are multiples of 16 bytes (pad the leading dimension)",
                     lda, ldb);
-    if (b_layout == B2G_B_KN)
-        return fail(B2G_ERR_UNSUPPORTED, "b_layout K x N is not built yet");
 
     // one CTA per 128 x 128 tile when either side is small (no half-empty 256-row pair
     // tiles for skinny M, fewer idle columns for narrow N), else 2-CTA 256 x 256 pairs
@@ -512,7 +497,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     p.stage_tx = (a_rows + g.box_b) * kBK * 2;
     p.group = group > 0 ? group : auto_group(g, p.tiles_m, K);
     p.stages = stages;
-    p.idesc = idesc_f16(g.bm, g.bn, acc == B2G_ACC_F32, false);
+    const bool b_mn = b_layout == B2G_B_KN;
+    p.idesc = idesc_f16(g.bm, g.bn, acc == B2G_ACC_F32, b_mn);
     p.acc_f16 = acc == B2G_ACC_F16;
     p.epilogue = epilogue;
     p.alpha = alpha;
@@ -520,7 +506,7 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     p.D = (__half*)D;
     p.ldd = ldd;
     p.d_tma = (((uintptr_t)D & 15) == 0) && (ldd % 8 == 0);
-    p.b_mn_major = 0;
+    p.b_mn_major = b_mn ? 1 : 0;
     p.dp_tiles = p.num_tiles;
     p.tail_split = 1;
     p.num_units = p.num_tiles;
@@ -550,12 +536,13 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         // cut the tiles of the last, partial wave into column slices (see pair_unit)
         const int clusters = max_pair_clusters(di, smem);
         const int rest = p.num_tiles % clusters;
-        const int split = rest ? tail_split_for(rest, clusters) : 1;
+        // K x N B loads 64-column boxes: a slice needs >= 64 columns per CTA (split <= 2)
+        const int split = rest ? tail_split_for(rest, clusters, b_mn ? 2 : 4) : 1;
         if (split > 1) {
             p.dp_tiles = p.num_tiles - rest;
             p.tail_split = split;
             p.num_units = p.dp_tiles + rest * split;
-            p.idesc_tail = idesc_f16(g.bm, g.bn / split, acc == B2G_ACC_F32, false);
+            p.idesc_tail = idesc_f16(g.bm, g.bn / split, acc == B2G_ACC_F32, b_mn);
         }
     }
     p.timeout_ns = wait_timeout_ns();
@@ -563,10 +550,13 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     CUtensorMap tmA, tmB;
     if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK, a_rows, "A"))
         return rc;
-    if (int rc = make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, g.box_b, "B"))
+    // B: N x K in 128-row x 64-k boxes, or K x N in 64-column x 64-k-row boxes (MN-major)
+    if (int rc = b_mn ? make_tmap(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, kBK, "B")
+                      : make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, g.box_b,
+                                  "B"))
         return rc;
     CUtensorMap tmBt = tmB;  // B boxes of the tail slices (width / 2 rows per CTA)
-    if (p.tail_split > 1)
+    if (p.tail_split > 1 && !b_mn)
         if (int rc = make_tmap(&tmBt, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK,
                                (uint32_t)(g.box_b / p.tail_split), "B tail"))
             return rc;

@@ -91,6 +91,19 @@ constexpr uint32_t kAStageBytes = kBM * kBK * 2;  // 16 KiB
 constexpr uint32_t kEpiBoxBytes = 32 * 64 * 2;
 constexpr uint32_t kEpiBytes = 8 * kEpiBoxBytes;  // 32 KiB
 
+// B operand layouts in shared memory (128-byte swizzle in both):
+//   K-major (B stored N x K): rows of 64 k-values (128 B), 8-row atoms 1024 B apart (SBO);
+//     a K step of 16 moves the start address by 32 B.
+//   MN-major (B stored K x N): boxes of 64 n-values (128 B) x 64 k-rows, 8 KiB each and
+//     placed back to back along N (LBO = 8 KiB between 64-column groups); 8 k-rows form a
+//     1024 B atom (SBO); a K step of 16 moves the start address by 16 rows = 2 KiB.
+constexpr uint32_t kMnBoxBytes = 64 * 64 * 2;
+__device__ __forceinline__ uint64_t b_desc0(uint32_t sB, int b_mn_major) {
+    return b_mn_major ? sdesc_sw128(sB, kMnBoxBytes, 1024) : sdesc_sw128(sB, 16, 1024);
+}
+// descriptor units (16 B) per UMMA K step of 16
+__device__ __forceinline__ uint32_t b_kstep(int b_mn_major) { return b_mn_major ? 128u : 2u; }
+
 template <int BN>
 struct TileTraits {
     static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "BN must be 64..256, step 64");
@@ -562,7 +575,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     const uint32_t fb = full0 + 8 * stage;
                     mbar_arrive_expect_tx(fb, p.stage_tx);
                     tma_load_2d(sA + stage * kAStageBytes, &tmA, fb, kb * kBK, m0);
-                    tma_load_2d(sB + stage * TT::kBStageBytes, &tmB, fb, kb * kBK, n0);
+                    const uint32_t sBs = sB + stage * TT::kBStageBytes;
+                    if (p.b_mn_major) {
+                        // B is K x N: BN / 64 boxes of 64 columns x 64 k-rows (8 KiB each)
+#pragma unroll
+                        for (int j = 0; j < BN / 64; ++j)
+                            tma_load_2d(sBs + (uint32_t)j * kMnBoxBytes, &tmB, fb, n0 + 64 * j,
+                                        kb * kBK);
+                    } else {
+                        tma_load_2d(sBs, &tmB, fb, kb * kBK, n0);
+                    }
                     ++issued;
                     if (++stage == p.stages) {
                         stage = 0;
@@ -593,7 +615,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             // descriptors are advanced by adds (all operand addresses < 256 KiB).
             const WaitCtx w{p.timeout_ns, abort_flag, kErrWaitMma};
             const uint64_t adesc0 = sdesc_sw128(sA, 16, 1024);
-            const uint64_t bdesc0 = sdesc_sw128(sB, 16, 1024);
+            const uint64_t bdesc0 = b_desc0(sB, p.b_mn_major);
+            const uint32_t bk = b_kstep(p.b_mn_major);
             constexpr uint32_t kAStep = kAStageBytes >> 4, kBStep = TT::kBStageBytes >> 4;
             const uint32_t idesc = p.idesc;
             int stage = 0;
@@ -626,9 +649,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kBStep);
                     if (elect_one()) {
                         mma_f16_ss<1>(d_tmem, ad, bd, idesc, kb > kb0 ? 1u : 0u);
-                        mma_f16_ss<1>(d_tmem, ad + 2, bd + 2, idesc, 1u);
-                        mma_f16_ss<1>(d_tmem, ad + 4, bd + 4, idesc, 1u);
-                        mma_f16_ss<1>(d_tmem, ad + 6, bd + 6, idesc, 1u);
+                        mma_f16_ss<1>(d_tmem, ad + 2, bd + bk, idesc, 1u);
+                        mma_f16_ss<1>(d_tmem, ad + 4, bd + 2 * bk, idesc, 1u);
+                        mma_f16_ss<1>(d_tmem, ad + 6, bd + 3 * bk, idesc, 1u);
                         mma_commit(empty0 + 8 * stage);  // frees the stage once these retire
                     }
                     __syncwarp();

@@ -163,7 +163,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                     const uint32_t fb = full0_leader + 8 * stage;
                     tma_load_2d_pair(sA + stage * kHalfBytes, &tmA, fb, kb * kBK, m0);
                     if (kb == kb0 && u == cluster_id) B2G_MARK(12);
-                    tma_load_2d_pair(sB + stage * kHalfBytes, mapB, fb, kb * kBK, n0);
+                    if (p.b_mn_major) {
+                        // B is K x N: (width / 2) / 64 boxes of 64 columns x 64 k-rows
+                        for (int j = 0; j < (width >> 7); ++j)
+                            tma_load_2d_pair(sB + stage * kHalfBytes + (uint32_t)j * kMnBoxBytes,
+                                             mapB, fb, n0 + 64 * j, kb * kBK);
+                    } else {
+                        tma_load_2d_pair(sB + stage * kHalfBytes, mapB, fb, kb * kBK, n0);
+                    }
                     if (kb == kb0 && u == cluster_id) B2G_MARK(3);
                     if (++stage == p.stages) {
                         stage = 0;
@@ -188,7 +195,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
             // operand address is below 256 KiB, so the 14-bit field never carries.
             const WaitCtx w{p.timeout_ns, abort_flag, kErrWaitMma};
             const uint64_t adesc0 = sdesc_sw128(sA, 16, 1024);
-            const uint64_t bdesc0 = sdesc_sw128(sB, 16, 1024);
+            const uint64_t bdesc0 = b_desc0(sB, p.b_mn_major);
+            const uint32_t bk = b_kstep(p.b_mn_major);
             constexpr uint32_t kStageStep = kHalfBytes >> 4;  // descriptor units per stage
             int stage = 0;
             uint32_t phase = 0;
@@ -224,9 +232,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                     const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kStageStep);
                     if (elect_one()) {
                         mma_f16_ss<2>(d_tmem, ad, bd, idesc, kb > kb0 ? 1u : 0u);
-                        mma_f16_ss<2>(d_tmem, ad + 2, bd + 2, idesc, 1u);
-                        mma_f16_ss<2>(d_tmem, ad + 4, bd + 4, idesc, 1u);
-                        mma_f16_ss<2>(d_tmem, ad + 6, bd + 6, idesc, 1u);
+                        mma_f16_ss<2>(d_tmem, ad + 2, bd + bk, idesc, 1u);
+                        mma_f16_ss<2>(d_tmem, ad + 4, bd + 2 * bk, idesc, 1u);
+                        mma_f16_ss<2>(d_tmem, ad + 6, bd + 3 * bk, idesc, 1u);
                         mma_commit_pair(empty0 + 8 * stage, 0x3);  // frees the stage in both CTAs
                     }
                     __syncwarp();

@@ -17,7 +17,8 @@
  *   - Layouts (reference src/gemm_bench.cu:8-15):
  *       A: M x K row-major, leading dimension lda >= K
  *       B: b_layout B2G_B_NK: N x K row-major (ldb >= K), the reference's "TN" layout
- *          b_layout B2G_B_KN: K x N row-major (ldb >= N)
+ *          b_layout B2G_B_KN: K x N row-major (ldb >= N; not in the reference, whose kernel
+ *          takes only the TN layout): read as an MN-major operand, same results bit for bit
  *       D: M x N row-major, ldd >= N
  *   - Launch entry points are asynchronous and never call exit(). They return a b2g_status;
  *     b2g_last_error() gives the message of the last failure on the calling thread.

@@ -291,3 +291,38 @@ def test_probe_hbm(cuda):
     gbs = b2g.probe_hbm(src, dst, n, reps=10)
     print(f"hbm copy {gbs:.1f} GB/s")
     assert gbs > 2000
+
+
+@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM])
+@pytest.mark.parametrize("shape", [(384, 512, 256), (300, 520, 200), (1000, 64, 1000),
+                                   (129, 1000, 72), (2304, 4352, 128)])
+def test_b_kn_layout(cuda, tile, shape):
+    """B stored K x N (b_layout B_KN, MN-major UMMA operand): every tile kernel, ragged M, N
+    and K, and 2-CTA shapes whose last wave is cut into 128-column slices."""
+    M, N, K = shape
+    A, Bnk, _ = inputs(M, N, K, seed=51)
+    Bkn = np.ascontiguousarray(Bnk.T)  # K x N
+    ldb = (N + 7) // 8 * 8
+    lda = (K + 7) // 8 * 8
+    D = run(cuda, A, Bkn, tile=tile, b_layout=b2g.B_KN, lda=lda, ldb=ldb)
+    frob, maxrel = check_rows(A, Bkn, D, sample_rows(M, 96), b_layout=1)
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+    # identical to the N x K layout of the same matrix (same MMAs, same order)
+    Dnk = run(cuda, A, Bnk, tile=tile, lda=lda, ldb=lda)
+    assert np.array_equal(D, Dnk)
+
+
+@pytest.mark.parametrize("mode", ["fused", "f16acc", "split"])
+def test_b_kn_layout_modes(cuda, mode):
+    M, N, K = 256, 768, 2048
+    A, Bnk, bias = inputs(M, N, K, seed=52, lo=-0.5, hi=0.5)
+    Bkn = np.ascontiguousarray(Bnk.T)
+    kw = {"fused": dict(epilogue=b2g.EPI_BIAS_RELU, alpha=0.5), "f16acc": dict(acc=b2g.ACC_F16),
+          "split": dict(splits=4, tile=b2g.TILE_128x128)}[mode]
+    b = bias if mode == "fused" else None
+    D = run(cuda, A, Bkn, b, b_layout=b2g.B_KN, **kw)
+    Dnk = run(cuda, A, Bnk, b, **kw)
+    assert np.array_equal(D, Dnk)
+    frob, maxrel = check_rows(A, Bkn, D, sample_rows(M, 64), bias=b, alpha=kw.get("alpha", 1.0),
+                              epilogue=mode == "fused", b_layout=1)
+    assert frob <= (FROB_F16 if mode == "f16acc" else FROB_F32), (frob, maxrel)
