@@ -10,6 +10,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -79,6 +80,7 @@ TileGeom geom(int tile) {
     switch (tile) {
         case B2G_TILE_128x128: return {128, 128, 1, 128, 128};
         case B2G_TILE_128x256: return {128, 256, 1, 128, 256};
+        case B2G_TILE_128x64: return {128, 64, 1, 128, 64};
         default: return {kPairBM, kPairBN, 2, 128, 128};
     }
 }
@@ -87,6 +89,7 @@ const void* kernel_ptr(int tile) {
     switch (tile) {
         case B2G_TILE_128x128: return (const void*)gemm_sm100_1cta<128>;
         case B2G_TILE_128x256: return (const void*)gemm_sm100_1cta<256>;
+        case B2G_TILE_128x64: return (const void*)gemm_sm100_1cta<64>;
         default: return (const void*)gemm_sm100_2cta;
     }
 }
@@ -95,6 +98,7 @@ size_t smem_needed(int tile, int stages) {
     switch (tile) {
         case B2G_TILE_128x128: return gemm_smem_bytes<128>(stages);
         case B2G_TILE_128x256: return gemm_smem_bytes<256>(stages);
+        case B2G_TILE_128x64: return gemm_smem_bytes<64>(stages);
         default: return gemm2_smem_bytes(stages);
     }
 }
@@ -114,7 +118,7 @@ int max_stages_for(int tile, int smem_optin) {
 }
 
 int ensure_kernel_attrs(int tile, const DeviceInfo& di) {
-    static bool done[3][kMaxDevices] = {};
+    static bool done[4][kMaxDevices] = {};
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
     if (di.device < kMaxDevices && done[tile][di.device]) return B2G_OK;
@@ -170,11 +174,13 @@ int tail_split_for(int rest, int clusters, int max_split) {
 }
 
 // L2 rasterization: the band of `group` M-tiles walked column-major keeps its A rows
-// resident while B streams through, so pick the largest band whose A panel fills less than
-// about 45% of the 126 MB L2 (capped at the number of M-tiles).
+// resident while B streams through. The band's A panel is sized to ~30% of the 126 MB L2
+// (rounded, capped at the number of M-tiles): measured on B200 with 256 x 256 tiles, 8192^3
+// runs best at 8 M-tiles (32 MiB of A; DRAM reads 1.09 GB vs 1.27 GB at 14), 16384^2 x 4096
+// at 16, 16384^3 at 5-6; larger bands lose the streaming B panels from L2.
 int auto_group(const TileGeom& g, int tiles_m, int K) {
     const double panel = (double)g.bm * (double)K * 2.0;  // bytes of A per M-tile
-    int grp = (int)(0.45 * 126.0 * 1024 * 1024 / panel);
+    int grp = (int)std::lround(0.30 * 126.0 * 1024 * 1024 / panel);
     grp = std::max(1, std::min(grp, tiles_m));
     return grp;
 }
@@ -240,6 +246,10 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
         case B2G_TILE_128x256:
             grid = std::min(p.num_units, di.sm_count);
             e = launch_ex(gemm_sm100_1cta<256>, grid, threads, smem, s, tmA, tmB, tmD, p);
+            break;
+        case B2G_TILE_128x64:
+            grid = std::min(p.num_units, di.sm_count);
+            e = launch_ex(gemm_sm100_1cta<64>, grid, threads, smem, s, tmA, tmB, tmD, p);
             break;
         default:
             grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
@@ -429,8 +439,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     if (epilogue != B2G_EPI_NONE && epilogue != B2G_EPI_BIAS_RELU)
         return fail(B2G_ERR_ARG, "epilogue must be 0 (none) or 1 (bias+ReLU), got %d", epilogue);
     if (tile != B2G_TILE_AUTO && tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 &&
-        tile != B2G_TILE_256x256_2SM)
-        return fail(B2G_ERR_ARG, "tile must be -1 (auto), 0, 1 or 2, got %d", tile);
+        tile != B2G_TILE_256x256_2SM && tile != B2G_TILE_128x64)
+        return fail(B2G_ERR_ARG, "tile must be -1 (auto), 0, 1, 2 or 3, got %d", tile);
     if (stages != 0 && (stages < 2 || stages > kMaxStages))
         return fail(B2G_ERR_ARG, "stages must be 0 (auto) or 2..%d, got %d", kMaxStages, stages);
     if (group < 0) return fail(B2G_ERR_ARG, "group must be >= 0, got %d", group);
@@ -446,6 +456,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
 
     DeviceInfo di;
     if (int rc = current_device(di)) return rc;
+    const bool auto_tile = tile == B2G_TILE_AUTO;
+    const int stages_arg = stages, group_arg = group, requested_splits = splits;
 
     if (K == 0) {  // zero accumulator: only the epilogue remains
         const size_t n = (size_t)M * N;
@@ -468,10 +480,17 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
                     "strides are multiples of 16 bytes (pad the leading dimension)",
                     lda, ldb);
 
-    // one CTA per 128 x 128 tile when either side is small (no half-empty 256-row pair
-    // tiles for skinny M, fewer idle columns for narrow N), else 2-CTA 256 x 256 pairs
-    if (tile == B2G_TILE_AUTO)
-        tile = (N <= 128 || M <= 128) ? B2G_TILE_128x128 : B2G_TILE_256x256_2SM;
+    // One CTA per 128 x 128 tile when either side is small (no half-empty 256-row pair
+    // tiles for skinny M, fewer idle columns for narrow N), or when 256 x 256 pair tiles would
+    // occupy under half of the pairs while 128 x 128 tiles fit one wave (measured on B200:
+    // 1024^3 245 -> 258 TFLOP/s, 512^3 38 -> 42; the pair kernel's tail slices reload A);
+    // else 2-CTA 256 x 256 pairs.
+    if (tile == B2G_TILE_AUTO) {
+        const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
+        const long long small_tiles = (long long)((M + 127) / 128) * ((N + 127) / 128);
+        const bool sparse_pairs = 2 * pair_tiles < di.sm_count / 2 && small_tiles <= di.sm_count;
+        tile = (N <= 128 || M <= 128 || sparse_pairs) ? B2G_TILE_128x128 : B2G_TILE_256x256_2SM;
+    }
     const TileGeom g = geom(tile);
     const int max_st = max_stages_for(tile, di.smem_optin);
     if (stages == 0) stages = max_st;
@@ -519,6 +538,13 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         return fail(B2G_ERR_ARG, "splits (%d) > k-blocks of 64 (%d)", splits, p.num_kb);
     if ((long long)p.num_tiles * splits > 0x7fffffffLL)
         return fail(B2G_ERR_ARG, "too many work units (%d tiles x %d splits)", p.num_tiles, splits);
+    // Small problems on 128 x 128 tiles that leave more than half the SMs idle and gain
+    // nothing from split-K (short K) take 128 x 64 tiles instead (auto tile and split only;
+    // measured on B200: 512^3 42.0 -> 44.9, 1024^3 242.8 -> 255.4 TFLOP/s).
+    if (auto_tile && requested_splits == 0 && splits == 1 && tile == B2G_TILE_128x128 &&
+        2LL * p.num_tiles <= di.sm_count)
+        return gemm_impl(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc, epilogue, alpha,
+                         B2G_TILE_128x64, stages_arg, group_arg, requested_splits, s, noalloc);
     p.splits = splits;
     p.num_units = p.num_tiles * splits;
     if (splits > 1) {
@@ -602,7 +628,8 @@ B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, in
                                int* ctas_per_sm, int* tmem_cols, int* stages_used) {
     clear_error();
     if (tile == B2G_TILE_AUTO) tile = B2G_TILE_256x256_2SM;
-    if (tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 && tile != B2G_TILE_256x256_2SM)
+    if (tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 && tile != B2G_TILE_256x256_2SM &&
+        tile != B2G_TILE_128x64)
         return fail(B2G_ERR_UNSUPPORTED, "tile %d is not built", tile);
     DeviceInfo di;
     if (int rc = current_device(di)) return rc;

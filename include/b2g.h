@@ -54,6 +54,8 @@ enum { B2G_EPI_NONE = 0, B2G_EPI_BIAS_RELU = 1 }; /* epilogue                   
  * (src/gemm_bench.cu:413-425), which are Ada warp tilings with no meaning on tcgen05.
  *   B2G_TILE_128x128   : one CTA, UMMA 128x128x16, TMEM 2 x 128 columns
  *   B2G_TILE_128x256   : one CTA, UMMA 128x256x16, TMEM 2 x 256 columns
+ *   B2G_TILE_128x64    : one CTA, UMMA 128x64x16, TMEM 2 x 64 columns (small problems:
+ *                        twice the tiles of 128x128)
  *   B2G_TILE_256x256_2SM : a 2-CTA cluster (cta_group::2), UMMA 256x256x16, each CTA loads
  *                        its own 128 rows of A and 128 rows of B (no multicast)
  *   B2G_TILE_AUTO      : chosen from the shape                                           */
@@ -61,6 +63,7 @@ enum {
     B2G_TILE_128x128 = 0,
     B2G_TILE_128x256 = 1,
     B2G_TILE_256x256_2SM = 2,
+    B2G_TILE_128x64 = 3,
     B2G_TILE_AUTO = -1
 };
 
@@ -76,7 +79,7 @@ enum {
  *   tile     : B2G_TILE_* ; stages: shared-memory ring depth, 0 = deepest that fits
  *   group    : L2 rasterization, `group` M-tiles walked column-major (1 = row-major),
  *              same mapping as src/gemm_bench.cu:237-250; 0 = the largest band whose A
- *              rows fill under ~45% of the L2
+ *              rows fill ~30% of the L2 (measured best on B200)
  * Requirements: A, B 16-byte aligned; lda, ldb multiples of 8 elements (TMA strides are
  * multiples of 16 bytes). D and ldd have no alignment rule (unaligned D takes a scalar
  * store path). M, N, K >= 0; K == 0 writes the epilogue of a zero accumulator.

@@ -35,7 +35,8 @@ def test_config1_512_elementwise_vs_fp32_triple_loop(cuda):
     assert O.frobenius_rel(D, O.gemm_f64(A, B)) <= FROB_F32
 
 
-@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM])
+@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
+                                  b2g.TILE_128x64])
 @pytest.mark.parametrize("shape", [(1, 1, 8), (1, 1, 1), (7, 9, 13), (128, 128, 64),
                                    (129, 257, 72), (300, 200, 100), (256, 512, 1000),
                                    (1000, 33, 64), (64, 640, 4096)])
@@ -48,7 +49,8 @@ def test_shapes_small(cuda, tile, shape):
     assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
 
 
-@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM])
+@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
+                                  b2g.TILE_128x64])
 @pytest.mark.parametrize("stages", [2, 3, 4, 0])
 @pytest.mark.parametrize("group", [1, 2, 8])
 def test_tiles_stages_groups(cuda, tile, stages, group):
@@ -70,7 +72,8 @@ def test_pair_tail_slices(cuda, shape):
     assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
 
 
-@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM])
+@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
+                                  b2g.TILE_128x64])
 @pytest.mark.parametrize("K,warps", [(1024, 8), (1088, 4), (64, 8)])
 @pytest.mark.parametrize("mode", ["plain", "fused", "f16acc"])
 def test_epilogue_warps_by_k(cuda, tile, K, warps, mode):
@@ -293,7 +296,8 @@ def test_probe_hbm(cuda):
     assert gbs > 2000
 
 
-@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM])
+@pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
+                                  b2g.TILE_128x64])
 @pytest.mark.parametrize("shape", [(384, 512, 256), (300, 520, 200), (1000, 64, 1000),
                                    (129, 1000, 72), (2304, 4352, 128)])
 def test_b_kn_layout(cuda, tile, shape):
@@ -326,3 +330,23 @@ def test_b_kn_layout_modes(cuda, mode):
     frob, maxrel = check_rows(A, Bkn, D, sample_rows(M, 64), bias=b, alpha=kw.get("alpha", 1.0),
                               epilogue=mode == "fused", b_layout=1)
     assert frob <= (FROB_F16 if mode == "f16acc" else FROB_F32), (frob, maxrel)
+
+
+@pytest.mark.parametrize("shape,tile,splits", [
+    ((1024, 1024, 1024), b2g.TILE_128x64, 1),      # sparse 128x128 tiles, short K
+    ((512, 512, 512), b2g.TILE_128x64, 1),
+    ((1024, 1024, 4096), b2g.TILE_128x128, 2),     # long K: split instead
+    ((128, 4096, 4096), b2g.TILE_128x128, 4),      # decode-shaped
+    ((2048, 1024, 1024), b2g.TILE_128x128, 1),     # 128 tiles: a full wave of 128x128
+    ((4096, 4096, 4096), b2g.TILE_256x256_2SM, 1),  # the headline shape
+])
+def test_auto_tile_choice(cuda, shape, tile, splits):
+    """The automatic configuration (tile kernel and split factor) for representative shapes,
+    each choice measured fastest on B200; the result is checked as well."""
+    M, N, K = shape
+    A, B, _ = inputs(M, N, K, seed=61)
+    D = run(cuda, A, B)
+    launch = b2g.last_launch()
+    assert (launch["tile"], launch["splits"]) == (tile, splits), launch
+    frob, maxrel = check_rows(A, B, D, sample_rows(M, 32))
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
