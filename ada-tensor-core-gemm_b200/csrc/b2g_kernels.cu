@@ -81,6 +81,7 @@ TileGeom geom(int tile) {
         case B2G_TILE_128x128: return {128, 128, 1, 128, 128};
         case B2G_TILE_128x256: return {128, 256, 1, 128, 256};
         case B2G_TILE_128x64: return {128, 64, 1, 128, 64};
+        case B2G_TILE_256x512_2SM: return {kPairBM, 512, 2, 128, 128};
         default: return {kPairBM, kPairBN, 2, 128, 128};
     }
 }
@@ -90,7 +91,8 @@ const void* kernel_ptr(int tile) {
         case B2G_TILE_128x128: return (const void*)gemm_sm100_1cta<128>;
         case B2G_TILE_128x256: return (const void*)gemm_sm100_1cta<256>;
         case B2G_TILE_128x64: return (const void*)gemm_sm100_1cta<64>;
-        default: return (const void*)gemm_sm100_2cta;
+        case B2G_TILE_256x512_2SM: return (const void*)gemm_sm100_2cta<512>;
+        default: return (const void*)gemm_sm100_2cta<256>;
     }
 }
 
@@ -99,7 +101,8 @@ size_t smem_needed(int tile, int stages) {
         case B2G_TILE_128x128: return gemm_smem_bytes<128>(stages);
         case B2G_TILE_128x256: return gemm_smem_bytes<256>(stages);
         case B2G_TILE_128x64: return gemm_smem_bytes<64>(stages);
-        default: return gemm2_smem_bytes(stages);
+        case B2G_TILE_256x512_2SM: return gemm2_smem_bytes<512>(stages);
+        default: return gemm2_smem_bytes<256>(stages);
     }
 }
 
@@ -118,7 +121,7 @@ int max_stages_for(int tile, int smem_optin) {
 }
 
 int ensure_kernel_attrs(int tile, const DeviceInfo& di) {
-    static bool done[4][kMaxDevices] = {};
+    static bool done[5][kMaxDevices] = {};
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
     if (di.device < kMaxDevices && done[tile][di.device]) return B2G_OK;
@@ -143,7 +146,7 @@ int max_pair_clusters(const DeviceInfo& di, size_t smem) {
     cfg.blockDim = dim3(kMaxThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_sm100_2cta, &cfg) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_sm100_2cta<256>, &cfg) != cudaSuccess ||
         n <= 0) {
         cudaGetLastError();
         n = di.sm_count / 2;
@@ -159,10 +162,13 @@ int max_pair_clusters(const DeviceInfo& di, size_t smem) {
 // costs more than 1/split of a tile because every slice reloads the tile's whole A panel
 // (per k-block 16 KiB of A + 128 B x width/2 of B per CTA): measured on B200, a 128-column
 // slice takes ~0.55 and a 64-column slice ~0.4 of a whole tile's time.
-int tail_split_for(int rest, int clusters, int max_split) {
+// For 256 x 512 tiles a 256-column slice is an ordinary 256 x 256 pair unit (~0.5 of the
+// tile) and a 128-column slice ~0.3.
+int tail_split_for(int rest, int clusters, int max_split, bool wide) {
     int best = 1;
     double best_t = 1.0;
-    for (const auto& sc : {std::pair<int, double>{2, 0.55}, std::pair<int, double>{4, 0.40}}) {
+    const double c2 = wide ? 0.50 : 0.55, c4 = wide ? 0.30 : 0.40;
+    for (const auto& sc : {std::pair<int, double>{2, c2}, std::pair<int, double>{4, c4}}) {
         if (sc.first > max_split) continue;
         const double t = (double)((rest * sc.first + clusters - 1) / clusters) * sc.second;
         if (t < best_t - 1e-9) {
@@ -200,13 +206,15 @@ bool pdl_enabled() {
 // Epilogue warps of a launch: 8 when K <= 1024 (at most 16 k-blocks per tile: the next
 // tile's mainloop is too short to hide a 4-warp epilogue, and D's writes dominate), else 4.
 // B2G_EPI_WARPS=4 or 8 in the environment forces one (read once per process).
-int epi_warps_for(int num_kb, int splits) {
+int epi_warps_for(int num_kb, int splits, bool wide) {
     static const int forced = [] {
         const char* e = std::getenv("B2G_EPI_WARPS");
         return e ? std::atoi(e) : 0;
     }();
     if (forced == 4 || forced == 8) return forced;
-    return (num_kb <= 16 || splits > 1) ? 8 : 4;  // split-K: the reduction wants 8 as well
+    // split-K: the reduction wants 8 as well; 256 x 512 tiles: the MMA warp waits for the
+    // epilogue of half 1 at the start of every tile
+    return (num_kb <= 16 || splits > 1 || wide) ? 8 : 4;
 }
 
 // The most recent GEMM launch of this host thread (b2g_last_launch).
@@ -236,7 +244,8 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
                 const DeviceInfo& di, size_t smem, cudaStream_t s) {
     if (int rc = ensure_kernel_attrs(tile, di)) return rc;
     int grid = 0;
-    const int threads = gemm_threads(epi_warps_for(p.num_kb, p.splits));
+    const int threads =
+        gemm_threads(epi_warps_for(p.num_kb, p.splits, tile == B2G_TILE_256x512_2SM));
     cudaError_t e = cudaSuccess;
     switch (tile) {
         case B2G_TILE_128x128:
@@ -251,9 +260,13 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
             grid = std::min(p.num_units, di.sm_count);
             e = launch_ex(gemm_sm100_1cta<64>, grid, threads, smem, s, tmA, tmB, tmD, p);
             break;
+        case B2G_TILE_256x512_2SM:
+            grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
+            e = launch_ex(gemm_sm100_2cta<512>, grid, threads, smem, s, tmA, tmB, tmBt, tmD, p);
+            break;
         default:
             grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
-            e = launch_ex(gemm_sm100_2cta, grid, threads, smem, s, tmA, tmB, tmBt, tmD, p);
+            e = launch_ex(gemm_sm100_2cta<256>, grid, threads, smem, s, tmA, tmB, tmBt, tmD, p);
             break;
     }
     if (e == cudaSuccess) e = cudaGetLastError();
@@ -439,8 +452,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     if (epilogue != B2G_EPI_NONE && epilogue != B2G_EPI_BIAS_RELU)
         return fail(B2G_ERR_ARG, "epilogue must be 0 (none) or 1 (bias+ReLU), got %d", epilogue);
     if (tile != B2G_TILE_AUTO && tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 &&
-        tile != B2G_TILE_256x256_2SM && tile != B2G_TILE_128x64)
-        return fail(B2G_ERR_ARG, "tile must be -1 (auto), 0, 1, 2 or 3, got %d", tile);
+        tile != B2G_TILE_256x256_2SM && tile != B2G_TILE_128x64 && tile != B2G_TILE_256x512_2SM)
+        return fail(B2G_ERR_ARG, "tile must be -1 (auto) or 0..4, got %d", tile);
     if (stages != 0 && (stages < 2 || stages > kMaxStages))
         return fail(B2G_ERR_ARG, "stages must be 0 (auto) or 2..%d, got %d", kMaxStages, stages);
     if (group < 0) return fail(B2G_ERR_ARG, "group must be >= 0, got %d", group);
@@ -517,7 +530,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     p.group = group > 0 ? group : auto_group(g, p.tiles_m, K);
     p.stages = stages;
     const bool b_mn = b_layout == B2G_B_KN;
-    p.idesc = idesc_f16(g.bm, g.bn, acc == B2G_ACC_F32, b_mn);
+    const bool wide = tile == B2G_TILE_256x512_2SM;
+    p.idesc = idesc_f16(g.bm, std::min(g.bn, kPairBN), acc == B2G_ACC_F32, b_mn);
     p.acc_f16 = acc == B2G_ACC_F16;
     p.epilogue = epilogue;
     p.alpha = alpha;
@@ -536,6 +550,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         splits = acc == B2G_ACC_F32 ? splitk_auto(p.num_tiles, concurrent, p.num_kb, g.ctas) : 1;
     if (splits > p.num_kb)
         return fail(B2G_ERR_ARG, "splits (%d) > k-blocks of 64 (%d)", splits, p.num_kb);
+    if (wide && splits > 1)
+        return fail(B2G_ERR_UNSUPPORTED, "split-K is not built for the 256 x 512 tile (tile 4)");
     if ((long long)p.num_tiles * splits > 0x7fffffffLL)
         return fail(B2G_ERR_ARG, "too many work units (%d tiles x %d splits)", p.num_tiles, splits);
     // Small problems on 128 x 128 tiles that leave more than half the SMs idle and gain
@@ -562,13 +578,14 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         // cut the tiles of the last, partial wave into column slices (see pair_unit)
         const int clusters = max_pair_clusters(di, smem);
         const int rest = p.num_tiles % clusters;
-        // K x N B loads 64-column boxes: a slice needs >= 64 columns per CTA (split <= 2)
-        const int split = rest ? tail_split_for(rest, clusters, b_mn ? 2 : 4) : 1;
+        // K x N B loads 64-column boxes: a slice needs >= 64 columns per CTA
+        const int split = rest ? tail_split_for(rest, clusters, (b_mn && !wide) ? 2 : 4, wide) : 1;
         if (split > 1) {
             p.dp_tiles = p.num_tiles - rest;
             p.tail_split = split;
             p.num_units = p.dp_tiles + rest * split;
-            p.idesc_tail = idesc_f16(g.bm, g.bn / split, acc == B2G_ACC_F32, b_mn);
+            p.idesc_tail = idesc_f16(g.bm, std::min(g.bn / split, kPairBN), acc == B2G_ACC_F32,
+                                     b_mn);
         }
     }
     p.timeout_ns = wait_timeout_ns();
@@ -581,10 +598,10 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
                       : make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, g.box_b,
                                   "B"))
         return rc;
-    CUtensorMap tmBt = tmB;  // B boxes of the tail slices (width / 2 rows per CTA)
+    CUtensorMap tmBt = tmB;  // B boxes of the tail slices (min(width, 256) / 2 rows per CTA)
     if (p.tail_split > 1 && !b_mn)
         if (int rc = make_tmap(&tmBt, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK,
-                               (uint32_t)(g.box_b / p.tail_split), "B tail"))
+                               (uint32_t)(std::min(g.bn / p.tail_split, kPairBN) / 2), "B tail"))
             return rc;
     CUtensorMap tmD = tmA;  // D in 32-row x 64-column boxes (unused without d_tma)
     if (p.d_tma)
@@ -629,7 +646,7 @@ B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, in
     clear_error();
     if (tile == B2G_TILE_AUTO) tile = B2G_TILE_256x256_2SM;
     if (tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 && tile != B2G_TILE_256x256_2SM &&
-        tile != B2G_TILE_128x64)
+        tile != B2G_TILE_128x64 && tile != B2G_TILE_256x512_2SM)
         return fail(B2G_ERR_UNSUPPORTED, "tile %d is not built", tile);
     DeviceInfo di;
     if (int rc = current_device(di)) return rc;

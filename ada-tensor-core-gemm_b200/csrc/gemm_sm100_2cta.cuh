@@ -8,10 +8,17 @@
 // in its own TMEM, double-buffered (2 x 256 columns). No TMA multicast is used: each CTA
 // loads its halves itself (this code also runs on multi-GPU jobs).
 //
-// Work list: whole 256 x 256 tiles first, then the tiles of the last, partial wave cut into
-// `tail_split` (2 or 4) column slices of 128 or 64 columns (UMMA 256 x 128 / 256 x 64, B
-// read through a second tensor map with a 64- or 32-row box), so the tail wave keeps every
-// SM pair busy instead of leaving most of them idle. No workspace or reduction is needed.
+// BNP = 512 ("wide" pair tile, 256 x 512): each CTA's 128 x 512 accumulator fills all 512
+// TMEM columns, as two 256-column halves issued as separate UMMA 256 x 256 x 16. Per k-block
+// a CTA then loads 16 KiB of A and 32 KiB of B for twice the work, so the L2 -> SM traffic per
+// FLOP drops by a quarter. There is no second accumulator; instead the halves are released
+// separately: the epilogue drains half 0, frees it, then half 1, while the MMA warp starts
+// the next tile on half 0 and waits for half 1 only before its first half-1 MMA.
+//
+// Work list: whole tiles first, then the tiles of the last, partial wave cut into
+// `tail_split` (2 or 4) column slices (UMMA N = slice width <= 256; B read through a second
+// tensor map whose box matches the slice), so the tail wave keeps every SM pair busy
+// instead of leaving most of them idle. No workspace or reduction is needed.
 //
 // Roles (64 + 32 x 4 or 8 epilogue warps threads per CTA):
 //   warp 0, one thread, both CTAs: TMA producer. Waits for its stage's `empty` barrier,
@@ -32,18 +39,37 @@
 namespace b2g {
 
 constexpr int kPairBM = 256;                       // pair tile rows (128 per CTA)
-constexpr int kPairBN = 256;                       // pair tile columns = UMMA N
+constexpr int kPairBN = 256;                       // UMMA N of one pair MMA
 constexpr uint32_t kHalfBytes = 128 * kBK * 2;     // one operand half per k-block: 16 KiB
-constexpr uint32_t kPairStageBytes = 2 * kHalfBytes;  // per CTA: A half + B half
-constexpr uint32_t kPairTmemCols = 2 * kPairBN;    // double-buffered accumulator
+constexpr uint32_t kPairTmemCols = 512;            // 2 x 256 columns: buffers or halves
 
+// Per-CTA shared memory of one stage: A half (16 KiB) + this CTA's BNP / 2 rows of B.
+template <int BNP>
+struct PairTraits {
+    static_assert(BNP == 256 || BNP == 512, "pair tile width 256 or 512");
+    static constexpr uint32_t kBStageBytes = (uint32_t)BNP / 2 * kBK * 2;  // 16 or 32 KiB
+    static constexpr uint32_t kStageBytes = kHalfBytes + kBStageBytes;
+    static constexpr bool kWide = BNP == 512;
+};
+
+template <int BNP>
 constexpr size_t gemm2_smem_bytes(int stages) {
-    return 1024 + (size_t)stages * kPairStageBytes + kEpiBytes + sizeof(SmemCtl);
+    return 1024 + (size_t)stages * PairTraits<BNP>::kStageBytes + kEpiBytes + sizeof(SmemCtl);
+}
+
+// Four UMMA 256 x N x 16 of one k-block into `d_tmem` (K steps: +32 B for A, +bk for B).
+__device__ __forceinline__ void mma_kblock_pair(uint32_t d_tmem, uint64_t ad, uint64_t bd,
+                                                uint32_t bk, uint32_t idesc, uint32_t acc0) {
+    mma_f16_ss<2>(d_tmem, ad, bd, idesc, acc0);
+    mma_f16_ss<2>(d_tmem, ad + 2, bd + bk, idesc, 1u);
+    mma_f16_ss<2>(d_tmem, ad + 4, bd + 2 * bk, idesc, 1u);
+    mma_f16_ss<2>(d_tmem, ad + 6, bd + 3 * bk, idesc, 1u);
 }
 
 // Work unit u -> tile index t, output tile (tm, tn), first output column and width of the
 // unit, whether it is a tail slice, and its split-K index (split-K and tail slices are never
 // combined: with splits > 1, unit u is split u % splits of tile u / splits).
+template <int BNP>
 __device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& t, int& tm, int& tn,
                                           int& n_first, int& width, bool& tail, int& split) {
     t = u;
@@ -62,10 +88,11 @@ __device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& t, in
         sub = v - (t - p.dp_tiles) * p.tail_split;
     }
     tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
-    width = tail ? kPairBN / p.tail_split : kPairBN;
-    n_first = tn * kPairBN + sub * width;
+    width = tail ? BNP / p.tail_split : BNP;
+    n_first = tn * BNP + sub * width;
 }
 
+template <int BNP>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_2cta(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
@@ -77,11 +104,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
     extern __shared__ uint8_t smem_dyn[];
     const uint32_t raw = smem_u32(smem_dyn);
     const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
+    using PT = PairTraits<BNP>;
     const uint32_t sA = raw + pad;
     const uint32_t sB = sA + (uint32_t)p.stages * kHalfBytes;
-    const uint32_t sEpi = sA + (uint32_t)p.stages * kPairStageBytes;
+    const uint32_t sEpi = sA + (uint32_t)p.stages * PT::kStageBytes;
     SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad +
-                                              (size_t)p.stages * kPairStageBytes + kEpiBytes);
+                                              (size_t)p.stages * PT::kStageBytes + kEpiBytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
@@ -143,10 +171,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
             for (int u = cluster_id; u < p.num_units && ok; u += num_clusters) {
                 int t, tm, tn, n_first, width, split, kb0, kb1;
                 bool tail;
-                pair_unit(p, u, t, tm, tn, n_first, width, tail, split);
+                pair_unit<BNP>(p, u, t, tm, tn, n_first, width, tail, split);
                 split_range(p, split, kb0, kb1);
                 const int m0 = tm * kPairBM + (int)rank * 128;
-                const int n0 = n_first + (int)rank * (width >> 1);
+                // B of the unit in 256-column halves; this CTA loads hw rows of each
+                const int nh = width > kPairBN ? 2 : 1;
+                const int hw = (width > kPairBN ? kPairBN : width) >> 1;
                 const CUtensorMap* mapB = tail ? &tmBt : &tmB;
                 // pair total: 2 x (A half 16 KiB + B half width/2 rows x 128 B)
                 const uint32_t bytes = 2u * (kHalfBytes + (uint32_t)(width >> 1) * 128u);
@@ -163,13 +193,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                     const uint32_t fb = full0_leader + 8 * stage;
                     tma_load_2d_pair(sA + stage * kHalfBytes, &tmA, fb, kb * kBK, m0);
                     if (kb == kb0 && u == cluster_id) B2G_MARK(12);
-                    if (p.b_mn_major) {
-                        // B is K x N: (width / 2) / 64 boxes of 64 columns x 64 k-rows
-                        for (int j = 0; j < (width >> 7); ++j)
-                            tma_load_2d_pair(sB + stage * kHalfBytes + (uint32_t)j * kMnBoxBytes,
-                                             mapB, fb, n0 + 64 * j, kb * kBK);
-                    } else {
-                        tma_load_2d_pair(sB + stage * kHalfBytes, mapB, fb, kb * kBK, n0);
+                    for (int h = 0; h < nh; ++h) {
+                        const int n0 = n_first + h * kPairBN + (int)rank * hw;
+                        const uint32_t dst = sB + stage * PT::kBStageBytes + (uint32_t)h * kHalfBytes;
+                        if (p.b_mn_major) {
+                            // B is K x N: hw / 64 boxes of 64 columns x 64 k-rows
+                            for (int j = 0; j < (hw >> 6); ++j)
+                                tma_load_2d_pair(dst + (uint32_t)j * kMnBoxBytes, mapB, fb,
+                                                 n0 + 64 * j, kb * kBK);
+                        } else {
+                            tma_load_2d_pair(dst, mapB, fb, kb * kBK, n0);
+                        }
                     }
                     if (kb == kb0 && u == cluster_id) B2G_MARK(3);
                     if (++stage == p.stages) {
@@ -197,7 +231,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
             const uint64_t adesc0 = sdesc_sw128(sA, 16, 1024);
             const uint64_t bdesc0 = b_desc0(sB, p.b_mn_major);
             const uint32_t bk = b_kstep(p.b_mn_major);
-            constexpr uint32_t kStageStep = kHalfBytes >> 4;  // descriptor units per stage
+            constexpr uint32_t kAStep = kHalfBytes >> 4;         // descriptor units per stage
+            constexpr uint32_t kBStep = PT::kBStageBytes >> 4;
+            constexpr uint32_t kBHalf = kHalfBytes >> 4;         // second 256-column half of B
             int stage = 0;
             uint32_t phase = 0;
             int it = 0;
@@ -205,11 +241,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
             for (int u = cluster_id; u < p.num_units && ok; u += num_clusters, ++it) {
                 int t, tm, tn, n_first, width, split, kb0, kb1;
                 bool tail;
-                pair_unit(p, u, t, tm, tn, n_first, width, tail, split);
+                pair_unit<BNP>(p, u, t, tm, tn, n_first, width, tail, split);
                 split_range(p, split, kb0, kb1);
                 const uint32_t idesc = tail ? p.idesc_tail : p.idesc;
-                const int buf = it & 1;
-                const uint32_t use = (uint32_t)(it >> 1) & 1u;
+                const bool two_halves = PT::kWide && width > kPairBN;
+                // 256-wide: double-buffered accumulators (buffer it & 1, reused every 2nd unit);
+                // 512-wide: halves 0 / 1 of one accumulator, each freed once per unit
+                const int buf = PT::kWide ? 0 : (it & 1);
+                const uint32_t use = PT::kWide ? ((uint32_t)it & 1u) : ((uint32_t)(it >> 1) & 1u);
                 B2G_TIC(t_te);
                 if (!mbar_wait_warp<true>(tempty0 + 8 * buf, use ^ 1u, w)) {
                     ok = false;
@@ -228,15 +267,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                     if (lane == 0) B2G_TOC(1, t_full);
                     if (lane == 0) B2G_COUNT(6, 1);
                     if (lane == 0 && kb == kb0 && it == 0) B2G_MARK(4);
-                    const uint64_t ad = adesc0 + (uint64_t)((uint32_t)stage * kStageStep);
-                    const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kStageStep);
-                    if (elect_one()) {
-                        mma_f16_ss<2>(d_tmem, ad, bd, idesc, kb > kb0 ? 1u : 0u);
-                        mma_f16_ss<2>(d_tmem, ad + 2, bd + bk, idesc, 1u);
-                        mma_f16_ss<2>(d_tmem, ad + 4, bd + 2 * bk, idesc, 1u);
-                        mma_f16_ss<2>(d_tmem, ad + 6, bd + 3 * bk, idesc, 1u);
-                        mma_commit_pair(empty0 + 8 * stage, 0x3);  // frees the stage in both CTAs
+                    const uint64_t ad = adesc0 + (uint64_t)((uint32_t)stage * kAStep);
+                    const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kBStep);
+                    const uint32_t acc0 = kb > kb0 ? 1u : 0u;
+                    if (elect_one()) mma_kblock_pair(d_tmem, ad, bd, bk, idesc, acc0);
+                    __syncwarp();
+                    if (two_halves) {
+                        // half 1: before its first MMA of this unit, wait until the epilogue of
+                        // the previous unit has read it
+                        if (kb == kb0) {
+                            if (!mbar_wait_warp<true>(tempty0 + 8, use ^ 1u, w)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                        }
+                        if (elect_one())
+                            mma_kblock_pair(d_tmem + (uint32_t)kPairBN, ad, bd + kBHalf, bk, idesc,
+                                            acc0);
+                        __syncwarp();
                     }
+                    if (elect_one()) mma_commit_pair(empty0 + 8 * stage, 0x3);  // stage free in both CTAs
                     __syncwarp();
                     if (++stage == p.stages) {
                         stage = 0;
@@ -265,8 +316,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
         uint32_t seq = 0;
         int it = 0;
         for (int u = cluster_id; u < p.num_units; u += num_clusters, ++it) {
-            const int buf = it & 1;
-            const uint32_t use = (uint32_t)(it >> 1) & 1u;
+            const int buf = PT::kWide ? 0 : (it & 1);
+            const uint32_t use = PT::kWide ? ((uint32_t)it & 1u) : ((uint32_t)(it >> 1) & 1u);
             B2G_TIC(t_tf);
             const bool ok = mbar_wait<true>(tfull0 + 8 * buf, use, w);
             if (!__all_sync(0xffffffffu, ok)) break;
@@ -275,23 +326,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
             tc_fence_after();
             int t, tm, tn, n_first, width, split;
             bool tail;
-            pair_unit(p, u, t, tm, tn, n_first, width, tail, split);
+            pair_unit<BNP>(p, u, t, tm, tn, n_first, width, tail, split);
             const int row0 = tm * kPairBM + (int)rank * 128 + q * 32;
-            const uint32_t tbase =
-                tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kPairBN);
-            auto release = [&] {  // accumulator `buf` has been read: the leader may reuse it
+            const uint32_t tq = tmem_base + ((uint32_t)(q * 32) << 16);
+            // accumulator buffer / half `b` has been read: the leader may reuse it
+            auto release = [&](int b) {
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_remote(tempty0_leader + 8 * buf);
+                if (lane == 0) mbar_arrive_remote(tempty0_leader + 8 * b);
             };
             B2G_TIC(t_epi);
-            if (p.splits > 1) {
-                splitk_epilogue(p, es, &tmD, tbase, t, split, (int)rank, 2, q, warp - 2, kPairBN,
-                                row0, n_first, c_first, stage0, lane, seq, epi, release);
+            if constexpr (PT::kWide) {
+                // half 0 (columns [0, 256) of the unit), freed, then half 1; a unit of at most
+                // 256 columns has an empty half 1, which is freed all the same so that both
+                // halves complete one phase per unit
+                for (int h = 0; h < 2; ++h) {
+                    const int hw = width - h * kPairBN;
+                    if (hw > 0)
+                        epilogue_rows(p, es, &tmD, tq + (uint32_t)(h * kPairBN), row0,
+                                      n_first + h * kPairBN, hw < kPairBN ? hw : kPairBN, c_first,
+                                      stage0, lane, seq, acc16, epi);
+                    release(h);
+                }
             } else {
-                epilogue_rows(p, es, &tmD, tbase, row0, n_first, width, c_first, stage0, lane,
-                              seq, acc16, epi);
-                release();
+                const uint32_t tbase = tq + (uint32_t)(buf * kPairBN);
+                if (p.splits > 1) {
+                    splitk_epilogue(p, es, &tmD, tbase, t, split, (int)rank, 2, q, warp - 2,
+                                    kPairBN, row0, n_first, c_first, stage0, lane, seq, epi,
+                                    [&] { release(buf); });
+                } else {
+                    epilogue_rows(p, es, &tmD, tbase, row0, n_first, width, c_first, stage0, lane,
+                                  seq, acc16, epi);
+                    release(buf);
+                }
             }
             if (warp == 2 && lane == 0) B2G_TOC(4, t_epi);
             if (warp == 2 && lane == 0) B2G_MARK(7);

@@ -56,6 +56,10 @@ enum { B2G_EPI_NONE = 0, B2G_EPI_BIAS_RELU = 1 }; /* epilogue                   
  *   B2G_TILE_128x256   : one CTA, UMMA 128x256x16, TMEM 2 x 256 columns
  *   B2G_TILE_128x64    : one CTA, UMMA 128x64x16, TMEM 2 x 64 columns (small problems:
  *                        twice the tiles of 128x128)
+ *   B2G_TILE_256x512_2SM : a 2-CTA cluster computing a 256 x 512 tile as two UMMA
+ *                        256x256x16 halves (all 512 TMEM columns, halves released to the
+ *                        next tile separately); a quarter less L2 traffic per FLOP than
+ *                        256x256 (large problems; no split-K)
  *   B2G_TILE_256x256_2SM : a 2-CTA cluster (cta_group::2), UMMA 256x256x16, each CTA loads
  *                        its own 128 rows of A and 128 rows of B (no multicast)
  *   B2G_TILE_AUTO      : chosen from the shape                                           */
@@ -64,6 +68,7 @@ enum {
     B2G_TILE_128x256 = 1,
     B2G_TILE_256x256_2SM = 2,
     B2G_TILE_128x64 = 3,
+    B2G_TILE_256x512_2SM = 4,
     B2G_TILE_AUTO = -1
 };
 

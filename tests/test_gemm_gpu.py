@@ -36,7 +36,7 @@ def test_config1_512_elementwise_vs_fp32_triple_loop(cuda):
 
 
 @pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
-                                  b2g.TILE_128x64])
+                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM])
 @pytest.mark.parametrize("shape", [(1, 1, 8), (1, 1, 1), (7, 9, 13), (128, 128, 64),
                                    (129, 257, 72), (300, 200, 100), (256, 512, 1000),
                                    (1000, 33, 64), (64, 640, 4096)])
@@ -50,7 +50,7 @@ def test_shapes_small(cuda, tile, shape):
 
 
 @pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
-                                  b2g.TILE_128x64])
+                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM])
 @pytest.mark.parametrize("stages", [2, 3, 4, 0])
 @pytest.mark.parametrize("group", [1, 2, 8])
 def test_tiles_stages_groups(cuda, tile, stages, group):
@@ -73,7 +73,7 @@ def test_pair_tail_slices(cuda, shape):
 
 
 @pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
-                                  b2g.TILE_128x64])
+                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM])
 @pytest.mark.parametrize("K,warps", [(1024, 8), (1088, 4), (64, 8)])
 @pytest.mark.parametrize("mode", ["plain", "fused", "f16acc"])
 def test_epilogue_warps_by_k(cuda, tile, K, warps, mode):
@@ -90,6 +90,8 @@ def test_epilogue_warps_by_k(cuda, tile, K, warps, mode):
         kw = dict(acc=b2g.ACC_F16)
     D = run(cuda, A, B, bias if mode == "fused" else None, tile=tile, splits=1, **kw)
     launch = b2g.last_launch()
+    if tile == b2g.TILE_256x512_2SM:
+        warps = 8  # always: the next tile's half-1 MMAs wait for this epilogue
     assert launch["threads"] == 64 + 32 * warps, launch
     assert launch["tile"] == tile
     rows = sample_rows(M, 96)
@@ -297,7 +299,7 @@ def test_probe_hbm(cuda):
 
 
 @pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
-                                  b2g.TILE_128x64])
+                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM])
 @pytest.mark.parametrize("shape", [(384, 512, 256), (300, 520, 200), (1000, 64, 1000),
                                    (129, 1000, 72), (2304, 4352, 128)])
 def test_b_kn_layout(cuda, tile, shape):
@@ -350,3 +352,33 @@ def test_auto_tile_choice(cuda, shape, tile, splits):
     assert (launch["tile"], launch["splits"]) == (tile, splits), launch
     frob, maxrel = check_rows(A, B, D, sample_rows(M, 32))
     assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+@pytest.mark.parametrize("shape", [(2304, 4352, 320), (1024, 1536, 1000), (4096, 3000, 512),
+                                   (520, 700, 128)])
+@pytest.mark.parametrize("b_layout", [b2g.B_NK, b2g.B_KN])
+def test_wide_pair_tile(cuda, shape, b_layout):
+    """256 x 512 pair tiles (tile 4): two 256-column accumulator halves released separately
+    to the next tile, with tail slices of 256 and 128 columns, ragged N, both B layouts; the
+    output is bit-identical to the 256 x 256 kernel's (same K order per element)."""
+    M, N, K = shape
+    A, Bnk, _ = inputs(M, N, K, seed=71)
+    lda = (K + 7) // 8 * 8
+    if b_layout == b2g.B_KN:
+        B = np.ascontiguousarray(Bnk.T)
+        ldb = (N + 7) // 8 * 8
+    else:
+        B, ldb = Bnk, lda
+    D = run(cuda, A, B, tile=b2g.TILE_256x512_2SM, b_layout=b_layout, lda=lda, ldb=ldb)
+    assert b2g.last_launch()["tile"] == b2g.TILE_256x512_2SM
+    frob, maxrel = check_rows(A, B, D, sample_rows(M, 96), b_layout=b_layout)
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+    D2 = run(cuda, A, B, tile=b2g.TILE_256x256_2SM, b_layout=b_layout, lda=lda, ldb=ldb)
+    assert np.array_equal(D, D2)
+
+
+def test_wide_pair_tile_rejects_split(cuda):
+    A, B, _ = inputs(512, 512, 1024, seed=72)
+    with pytest.raises(b2g.B2GError) as e:
+        run(cuda, A, B, tile=b2g.TILE_256x512_2SM, splits=2)
+    assert e.value.code == b2g.ERR_UNSUPPORTED
