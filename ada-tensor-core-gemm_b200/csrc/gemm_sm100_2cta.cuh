@@ -258,6 +258,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                 if (lane == 0) B2G_COUNT(7, 1);
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(buf * kPairBN);
+                // 512-wide: the half-1 MMAs of the first k-blocks are deferred (their stages
+                // held) while half 1 is still being drained by the previous unit's epilogue,
+                // so the tensor pipe keeps working on half 0 meanwhile
+                const int max_defer = two_halves ? (p.stages - 1 < 3 ? p.stages - 1 : 3) : 0;
+                int deferred = 0, defer_stage = 0;
+                bool half1_ready = !two_halves;
+                // issue the deferred half-1 k-blocks (in k order) and free their stages
+                auto flush_deferred = [&]() -> bool {
+                    if (!mbar_wait_warp<true>(tempty0 + 8, use ^ 1u, w)) return false;
+                    tc_fence_after();
+                    half1_ready = true;
+                    int st = defer_stage;
+                    for (int i = 0; i < deferred; ++i) {
+                        const uint64_t ad = adesc0 + (uint64_t)((uint32_t)st * kAStep);
+                        const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)st * kBStep);
+                        if (elect_one()) {
+                            mma_kblock_pair(d_tmem + (uint32_t)kPairBN, ad, bd + kBHalf, bk, idesc,
+                                            i > 0 ? 1u : 0u);
+                            mma_commit_pair(empty0 + 8 * st, 0x3);
+                        }
+                        __syncwarp();
+                        if (++st == p.stages) st = 0;
+                    }
+                    deferred = 0;
+                    return true;
+                };
                 for (int kb = kb0; kb < kb1; ++kb) {
                     B2G_TIC(t_full);
                     if (!mbar_wait_warp(full0 + 8 * stage, phase, w)) {
@@ -272,28 +298,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                     const uint32_t acc0 = kb > kb0 ? 1u : 0u;
                     if (elect_one()) mma_kblock_pair(d_tmem, ad, bd, bk, idesc, acc0);
                     __syncwarp();
+                    bool commit = true;
                     if (two_halves) {
-                        // half 1: before its first MMA of this unit, wait until the epilogue of
-                        // the previous unit has read it
-                        if (kb == kb0) {
-                            if (!mbar_wait_warp<true>(tempty0 + 8, use ^ 1u, w)) {
+                        if (!half1_ready && deferred < max_defer) {
+                            if (deferred == 0) defer_stage = stage;
+                            ++deferred;
+                            commit = false;  // held until its half-1 MMAs are issued
+                        } else {
+                            if (!half1_ready && !flush_deferred()) {
                                 ok = false;
                                 break;
                             }
-                            tc_fence_after();
+                            if (elect_one())
+                                mma_kblock_pair(d_tmem + (uint32_t)kPairBN, ad, bd + kBHalf, bk,
+                                                idesc, acc0);
+                            __syncwarp();
                         }
-                        if (elect_one())
-                            mma_kblock_pair(d_tmem + (uint32_t)kPairBN, ad, bd + kBHalf, bk, idesc,
-                                            acc0);
+                    }
+                    if (commit) {
+                        if (elect_one()) mma_commit_pair(empty0 + 8 * stage, 0x3);  // both CTAs
                         __syncwarp();
                     }
-                    if (elect_one()) mma_commit_pair(empty0 + 8 * stage, 0x3);  // stage free in both CTAs
-                    __syncwarp();
                     if (++stage == p.stages) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
+                // a unit shorter than the deferral window ends with half-1 work pending
+                if (ok && two_halves && !half1_ready && !flush_deferred()) ok = false;
                 if (!ok) break;
                 if (elect_one()) mma_commit_pair(tfull0 + 8 * buf, 0x3);  // final in both CTAs
                 __syncwarp();

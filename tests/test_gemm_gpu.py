@@ -341,6 +341,7 @@ def test_b_kn_layout_modes(cuda, mode):
     ((128, 4096, 4096), b2g.TILE_128x128, 4),      # decode-shaped
     ((2048, 1024, 1024), b2g.TILE_128x128, 1),     # 128 tiles: a full wave of 128x128
     ((4096, 4096, 4096), b2g.TILE_256x256_2SM, 1),  # the headline shape
+    ((8192, 8192, 8192), b2g.TILE_256x512_2SM, 1),  # long K, >= 4 waves of 256 x 512
 ])
 def test_auto_tile_choice(cuda, shape, tile, splits):
     """The automatic configuration (tile kernel and split factor) for representative shapes,
