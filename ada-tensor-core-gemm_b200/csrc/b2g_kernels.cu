@@ -21,6 +21,7 @@
 #include "aux_sm100.cuh"
 #include "gemm_sm100.cuh"
 #include "gemm_sm100_2cta.cuh"
+#include "gemm_sm100_swap.cuh"
 #include "probe_sm100.cuh"
 
 namespace b2g {
@@ -82,6 +83,7 @@ TileGeom geom(int tile) {
         case B2G_TILE_128x256: return {128, 256, 1, 128, 256};
         case B2G_TILE_128x64: return {128, 64, 1, 128, 64};
         case B2G_TILE_256x512_2SM: return {kPairBM, 512, 2, 128, 128};
+        case B2G_TILE_SWAP_AB: return {64, 128, 1, 64, 128};  // largest MT, for reports only
         default: return {kPairBM, kPairBN, 2, 128, 128};
     }
 }
@@ -92,6 +94,7 @@ const void* kernel_ptr(int tile) {
         case B2G_TILE_128x256: return (const void*)gemm_sm100_1cta<256>;
         case B2G_TILE_128x64: return (const void*)gemm_sm100_1cta<64>;
         case B2G_TILE_256x512_2SM: return (const void*)gemm_sm100_2cta<512>;
+        case B2G_TILE_SWAP_AB: return (const void*)gemm_sm100_swap<64>;
         default: return (const void*)gemm_sm100_2cta<256>;
     }
 }
@@ -102,6 +105,7 @@ size_t smem_needed(int tile, int stages) {
         case B2G_TILE_128x256: return gemm_smem_bytes<256>(stages);
         case B2G_TILE_128x64: return gemm_smem_bytes<64>(stages);
         case B2G_TILE_256x512_2SM: return gemm2_smem_bytes<512>(stages);
+        case B2G_TILE_SWAP_AB: return gemm_swap_smem_bytes<64>(stages);
         default: return gemm2_smem_bytes<256>(stages);
     }
 }
@@ -121,7 +125,7 @@ int max_stages_for(int tile, int smem_optin) {
 }
 
 int ensure_kernel_attrs(int tile, const DeviceInfo& di) {
-    static bool done[5][kMaxDevices] = {};
+    static bool done[6][kMaxDevices] = {};
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
     if (di.device < kMaxDevices && done[tile][di.device]) return B2G_OK;
@@ -274,6 +278,72 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
         return fail(B2G_ERR_CUDA, "GEMM launch (tile %d, grid %d, smem %zu): %s", tile, grid, smem,
                     cudaGetErrorString(e));
     g_last_launch = LaunchRecord{grid, threads, tile, p.stages, p.num_units, p.splits};
+    return B2G_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// Swapped-operand kernel for small M (tile B2G_TILE_SWAP_AB)
+// ---------------------------------------------------------------------------------------
+// MT (UMMA N = rows of A per CTA) so that the grid has about one CTA per SM: 128-column
+// blocks of D times ceil(M / MT) row blocks.
+int swap_mt_for(int M, int N, int sm_count) {
+    const int n_tiles = (N + 127) / 128;
+    const int target = std::max(1, sm_count / std::max(1, n_tiles));
+    const int rows = (M + target - 1) / target;
+    return rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+}
+
+template <int MT>
+int launch_swap(const void* A, const void* B, int M, int N, int K, long long lda, long long ldb,
+                GemmParams& p, int stages, const DeviceInfo& di, cudaStream_t s) {
+    using ST = SwapTraits<MT>;
+    static bool done[kMaxDevices] = {};
+    static std::mutex mu;
+    const void* kern = (const void*)gemm_sm100_swap<MT>;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!(di.device < kMaxDevices && done[di.device])) {
+            cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 di.smem_optin);
+            if (e != cudaSuccess)
+                return fail(B2G_ERR_CUDA, "cudaFuncSetAttribute(swap kernel): %s",
+                            cudaGetErrorString(e));
+            if (di.device < kMaxDevices) done[di.device] = true;
+        }
+    }
+    if (stages == 0) {
+        stages = kMaxStages;
+        while (stages > 2 && gemm_swap_smem_bytes<MT>(stages) > (size_t)di.smem_optin) --stages;
+    }
+    if (gemm_swap_smem_bytes<MT>(stages) > (size_t)di.smem_optin)
+        return fail(B2G_ERR_SMEM, "smem over per-block opt-in limit (swap kernel, %d stages)",
+                    stages);
+    const size_t smem =
+        std::max(gemm_swap_smem_bytes<MT>(stages), (size_t)di.smem_per_sm / 2 + 1024);
+    p.stages = stages;
+    p.tiles_m = (M + MT - 1) / MT;
+    p.tiles_n = (N + 127) / 128;
+    const long long nt = (long long)p.tiles_m * p.tiles_n;
+    if (nt > 0x7fffffffLL) return fail(B2G_ERR_ARG, "too many tiles (%lld)", nt);
+    p.num_tiles = p.num_units = p.dp_tiles = (int)nt;
+    p.tail_split = 1;
+    p.splits = 1;
+    p.idesc = p.idesc_tail = idesc_f16(128, MT, p.acc_f16 == 0, false);
+    p.stage_tx = ST::kStageBytes;
+    if (p.group <= 0) p.group = 1;
+    CUtensorMap tmA, tmB;
+    if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK, MT, "A"))
+        return rc;
+    if (int rc = make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, 128, "B"))
+        return rc;
+    const int grid = std::min(p.num_units, di.sm_count);
+    const int threads = gemm_threads(4);
+    cudaError_t e = launch_ex(gemm_sm100_swap<MT>, grid, threads, smem, s, tmA, tmB, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return fail(B2G_ERR_CUDA, "swap GEMM launch (MT %d, grid %d): %s", MT, grid,
+                    cudaGetErrorString(e));
+    g_last_launch = LaunchRecord{grid, threads, B2G_TILE_SWAP_AB, p.stages, p.num_units, 1};
     return B2G_OK;
 }
 
@@ -452,8 +522,9 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     if (epilogue != B2G_EPI_NONE && epilogue != B2G_EPI_BIAS_RELU)
         return fail(B2G_ERR_ARG, "epilogue must be 0 (none) or 1 (bias+ReLU), got %d", epilogue);
     if (tile != B2G_TILE_AUTO && tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 &&
-        tile != B2G_TILE_256x256_2SM && tile != B2G_TILE_128x64 && tile != B2G_TILE_256x512_2SM)
-        return fail(B2G_ERR_ARG, "tile must be -1 (auto) or 0..4, got %d", tile);
+        tile != B2G_TILE_256x256_2SM && tile != B2G_TILE_128x64 &&
+        tile != B2G_TILE_256x512_2SM && tile != B2G_TILE_SWAP_AB)
+        return fail(B2G_ERR_ARG, "tile must be -1 (auto) or 0..5, got %d", tile);
     if (stages != 0 && (stages < 2 || stages > kMaxStages))
         return fail(B2G_ERR_ARG, "stages must be 0 (auto) or 2..%d, got %d", kMaxStages, stages);
     if (group < 0) return fail(B2G_ERR_ARG, "group must be >= 0, got %d", group);
@@ -509,6 +580,38 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         const long long wide_tiles = (long long)((M + 255) / 256) * ((N + 511) / 512);
         if (tile == B2G_TILE_256x256_2SM && K >= 8192 && wide_tiles >= 2LL * di.sm_count)
             tile = B2G_TILE_256x512_2SM;
+        // Tiny M with N wide enough that 128-column blocks alone give ~one CTA per SM (no
+        // split-K needed): the swapped-operand kernel skips the 128-row tile's padding
+        // (measured on B200: 16 x 16384 x 4096 77.8 -> 84.7 TFLOP/s; with N = 4096 its 32
+        // CTAs are slower than 128 x 128 tiles with split-K, so it is not used there).
+        const long long n_blocks = (N + 127) / 128;
+        if (M <= 32 && b_layout == B2G_B_NK && requested_splits <= 1 &&
+            2 * n_blocks > di.sm_count && 3 * n_blocks >= 2LL * di.sm_count)
+            tile = B2G_TILE_SWAP_AB;
+    }
+    if (tile == B2G_TILE_SWAP_AB) {
+        if (b_layout != B2G_B_NK)
+            return fail(B2G_ERR_UNSUPPORTED, "the swapped-operand kernel takes B as N x K only");
+        if (splits > 1)
+            return fail(B2G_ERR_UNSUPPORTED, "split-K is not built for the swapped-operand kernel");
+        GemmParams p{};
+        p.M = M;
+        p.N = N;
+        p.K = K;
+        p.num_kb = (K + kBK - 1) / kBK;
+        p.group = group;
+        p.acc_f16 = acc == B2G_ACC_F16;
+        p.epilogue = epilogue;
+        p.alpha = alpha;
+        p.bias = (const __half*)bias;
+        p.D = (__half*)D;
+        p.ldd = ldd;
+        p.timeout_ns = wait_timeout_ns();
+        switch (swap_mt_for(M, N, di.sm_count)) {
+            case 16: return launch_swap<16>(A, B, M, N, K, lda, ldb, p, stages, di, s);
+            case 32: return launch_swap<32>(A, B, M, N, K, lda, ldb, p, stages, di, s);
+            default: return launch_swap<64>(A, B, M, N, K, lda, ldb, p, stages, di, s);
+        }
     }
     const TileGeom g = geom(tile);
     const int max_st = max_stages_for(tile, di.smem_optin);
@@ -652,7 +755,7 @@ B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, in
     clear_error();
     if (tile == B2G_TILE_AUTO) tile = B2G_TILE_256x256_2SM;
     if (tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 && tile != B2G_TILE_256x256_2SM &&
-        tile != B2G_TILE_128x64 && tile != B2G_TILE_256x512_2SM)
+        tile != B2G_TILE_128x64 && tile != B2G_TILE_256x512_2SM && tile != B2G_TILE_SWAP_AB)
         return fail(B2G_ERR_UNSUPPORTED, "tile %d is not built", tile);
     DeviceInfo di;
     if (int rc = current_device(di)) return rc;
@@ -678,7 +781,7 @@ B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, in
     if (regs) *regs = fa.numRegs;
     if (smem_bytes) *smem_bytes = (int)need;
     if (ctas_per_sm) *ctas_per_sm = occ;
-    if (tmem_cols) *tmem_cols = 2 * geom(tile).bn;
+    if (tmem_cols) *tmem_cols = tile == B2G_TILE_SWAP_AB ? 2 * 64 : std::min(2 * geom(tile).bn, 512);
     if (stages_used) *stages_used = stages;
     return B2G_OK;
 }

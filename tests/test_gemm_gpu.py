@@ -342,6 +342,8 @@ def test_b_kn_layout_modes(cuda, mode):
     ((2048, 1024, 1024), b2g.TILE_128x128, 1),     # 128 tiles: a full wave of 128x128
     ((4096, 4096, 4096), b2g.TILE_256x256_2SM, 1),  # the headline shape
     ((8192, 8192, 8192), b2g.TILE_256x512_2SM, 1),  # long K, >= 4 waves of 256 x 512
+    ((16, 16384, 1024), b2g.TILE_SWAP_AB, 1),       # tiny M, wide N: swapped operands
+    ((16, 4096, 4096), b2g.TILE_128x128, 4),        # tiny M, N = 4096: split-K instead
 ])
 def test_auto_tile_choice(cuda, shape, tile, splits):
     """The automatic configuration (tile kernel and split factor) for representative shapes,
