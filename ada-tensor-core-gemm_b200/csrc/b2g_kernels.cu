@@ -99,14 +99,21 @@ const void* kernel_ptr(int tile) {
     }
 }
 
-size_t smem_needed(int tile, int stages) {
+// Epilogue staging boxes (4 KiB each) of a launch, shared out among its epilogue warps. 8
+// for every shape: measured on B200, 16-32 boxes (fewer ring stages) gave nothing even where
+// D's writes dominate (16384^2 x 256: 810-813 TFLOP/s with 8-24 boxes) and cost up to 15%
+// at K >= 512, so the store path is not limited by stores in flight per warp.
+int epi_boxes_for(int /*num_kb*/) { return 8; }
+
+size_t smem_needed(int tile, int stages, int epi_boxes = 8) {
+    const uint32_t epi = (uint32_t)epi_boxes * kEpiBoxBytes;
     switch (tile) {
-        case B2G_TILE_128x128: return gemm_smem_bytes<128>(stages);
-        case B2G_TILE_128x256: return gemm_smem_bytes<256>(stages);
-        case B2G_TILE_128x64: return gemm_smem_bytes<64>(stages);
-        case B2G_TILE_256x512_2SM: return gemm2_smem_bytes<512>(stages);
+        case B2G_TILE_128x128: return gemm_smem_bytes<128>(stages, epi);
+        case B2G_TILE_128x256: return gemm_smem_bytes<256>(stages, epi);
+        case B2G_TILE_128x64: return gemm_smem_bytes<64>(stages, epi);
+        case B2G_TILE_256x512_2SM: return gemm2_smem_bytes<512>(stages, epi);
         case B2G_TILE_SWAP_AB: return gemm_swap_smem_bytes<64>(stages);
-        default: return gemm2_smem_bytes<256>(stages);
+        default: return gemm2_smem_bytes<256>(stages, epi);
     }
 }
 
@@ -114,13 +121,13 @@ size_t smem_needed(int tile, int stages) {
 // one GEMM CTA is resident per SM. Every GEMM CTA allocates 2 x BN TMEM columns; two
 // co-resident CTAs of 2-CTA clusters could otherwise each hold the TMEM the other's peer
 // waits for.
-size_t smem_request(int tile, int stages, const DeviceInfo& di) {
-    return std::max(smem_needed(tile, stages), (size_t)di.smem_per_sm / 2 + 1024);
+size_t smem_request(int tile, int stages, const DeviceInfo& di, int epi_boxes = 8) {
+    return std::max(smem_needed(tile, stages, epi_boxes), (size_t)di.smem_per_sm / 2 + 1024);
 }
 
-int max_stages_for(int tile, int smem_optin) {
+int max_stages_for(int tile, int smem_optin, int epi_boxes = 8) {
     int s = kMaxStages;
-    while (s > 2 && smem_needed(tile, s) > (size_t)smem_optin) --s;
+    while (s > 2 && smem_needed(tile, s, epi_boxes) > (size_t)smem_optin) --s;
     return s;
 }
 
@@ -245,11 +252,10 @@ cudaError_t launch_ex(Kern kern, int grid, int threads, size_t smem, cudaStream_
 
 int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
                 const CUtensorMap& tmBt, const CUtensorMap& tmD, const GemmParams& p,
-                const DeviceInfo& di, size_t smem, cudaStream_t s) {
+                const DeviceInfo& di, size_t smem, cudaStream_t s, int epi_warps) {
     if (int rc = ensure_kernel_attrs(tile, di)) return rc;
     int grid = 0;
-    const int threads =
-        gemm_threads(epi_warps_for(p.num_kb, p.splits, tile == B2G_TILE_256x512_2SM));
+    const int threads = gemm_threads(epi_warps);
     cudaError_t e = cudaSuccess;
     switch (tile) {
         case B2G_TILE_128x128:
@@ -614,12 +620,13 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         }
     }
     const TileGeom g = geom(tile);
-    const int max_st = max_stages_for(tile, di.smem_optin);
+    const int epi_boxes = epi_boxes_for((K + kBK - 1) / kBK);
+    const int max_st = max_stages_for(tile, di.smem_optin, epi_boxes);
     if (stages == 0) stages = max_st;
-    if (smem_needed(tile, stages) > (size_t)di.smem_optin)
+    if (smem_needed(tile, stages, epi_boxes) > (size_t)di.smem_optin)
         return fail(B2G_ERR_SMEM, "smem over per-block opt-in limit: %zu > %d (tile %d, %d stages)",
-                    smem_needed(tile, stages), di.smem_optin, tile, stages);
-    const size_t smem = smem_request(tile, stages, di);
+                    smem_needed(tile, stages, epi_boxes), di.smem_optin, tile, stages);
+    const size_t smem = smem_request(tile, stages, di, epi_boxes);
 
     GemmParams p{};
     p.M = M;
@@ -716,7 +723,9 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     if (p.d_tma)
         if (int rc = make_tmap(&tmD, D, (uint64_t)N, (uint64_t)M, (uint64_t)ldd, 64, 32, "D"))
             return rc;
-    return launch_gemm(tile, tmA, tmB, tmBt, tmD, p, di, smem, s);
+    const int epi_warps = epi_warps_for(p.num_kb, p.splits, wide);
+    p.epi_bufs = std::max(1, std::min(kMaxEpiBufs, epi_boxes / epi_warps));
+    return launch_gemm(tile, tmA, tmB, tmBt, tmD, p, di, smem, s, epi_warps);
 }
 
 }  // namespace

@@ -64,6 +64,9 @@ struct GemmParams {
     // A box is only round_up(M, 8) rows high; the stale shared-memory rows below it feed
     // accumulator rows >= M, which the epilogue never stores.
     uint32_t stage_tx;
+    // Epilogue staging: boxes of 4 KiB per epilogue warp (1..4), used in turn; the staging
+    // area is epilogue warps x epi_bufs x 4 KiB, after the operand ring.
+    int epi_bufs;
 };
 
 // k-blocks [kb0, kb1) of split s: an even share of the tile's num_kb k-blocks.
@@ -85,11 +88,15 @@ constexpr int kMaxEpiWarps = 8;
 constexpr int kMaxThreads = 64 + 32 * kMaxEpiWarps;
 __host__ __device__ constexpr int gemm_threads(int epi_warps) { return 64 + 32 * epi_warps; }
 constexpr uint32_t kAStageBytes = kBM * kBK * 2;  // 16 KiB
-// Epilogue staging for TMA stores: eight 32-row x 64-column FP16 boxes (4 KiB each,
-// 128-byte swizzle). With 4 epilogue warps each owns two, used in turn so the conversion of
-// one chunk overlaps the bulk store of the previous one; with 8 warps each owns one.
+// Epilogue staging for TMA stores: 32-row x 64-column FP16 boxes (4 KiB each, 128-byte
+// swizzle), `epi_bufs` per epilogue warp, used in turn so the conversion of one chunk
+// overlaps the bulk stores of the previous ones. Default 8 boxes in all (2 per warp with 4
+// epilogue warps, 1 with 8); short-K launches trade ring stages for more boxes.
 constexpr uint32_t kEpiBoxBytes = 32 * 64 * 2;
-constexpr uint32_t kEpiBytes = 8 * kEpiBoxBytes;  // 32 KiB
+constexpr int kMaxEpiBufs = 4;
+__host__ __device__ constexpr uint32_t epi_bytes(int epi_warps, int epi_bufs) {
+    return (uint32_t)(epi_warps * epi_bufs) * kEpiBoxBytes;
+}
 
 // B operand layouts in shared memory (128-byte swizzle in both):
 //   K-major (B stored N x K): rows of 64 k-values (128 B), 8-row atoms 1024 B apart (SBO);
@@ -125,9 +132,9 @@ struct SmemCtl {
 
 // Dynamic shared memory: [align slack][stages x (A, B)][epilogue staging][SmemCtl]
 template <int BN>
-constexpr size_t gemm_smem_bytes(int stages) {
-    return 1024 /* alignment slack */ + (size_t)stages * TileTraits<BN>::kStageBytes +
-           kEpiBytes + sizeof(SmemCtl);
+constexpr size_t gemm_smem_bytes(int stages, uint32_t epi) {
+    return 1024 /* alignment slack */ + (size_t)stages * TileTraits<BN>::kStageBytes + epi +
+           sizeof(SmemCtl);
 }
 
 // The epilogue's per-element work uses only these scalars, read once from the kernel
@@ -139,13 +146,13 @@ struct EpiScalars {
     const __half* bias;
     int d_tma;
     uint64_t store_pol;  // L2 policy of the TMA stores of D: evict_first (D is not re-read)
-    int bufs;            // staging boxes of this warp (2 with 4 epilogue warps, 1 with 8)
+    int bufs;            // staging boxes of this warp (1..4)
     int c_step;          // 64-column chunk stride of this warp (1 with 4 warps, 2 with 8)
 };
 
 __device__ __forceinline__ EpiScalars epi_scalars(const GemmParams& p, int epi_warps) {
-    return EpiScalars{p.M, p.N, p.alpha, p.bias, p.d_tma, l2_policy_evict_first(),
-                      8 / epi_warps, epi_warps / 4};
+    return EpiScalars{p.M, p.N, p.alpha, p.bias, p.d_tma, l2_policy_evict_first(), p.epi_bufs,
+                      epi_warps / 4};
 }
 
 // alpha * acc + bias + ReLU (EPI) and round to FP16, two columns per word; ACC16: the
@@ -182,12 +189,14 @@ __device__ __forceinline__ uint32_t epi_pack2(const EpiScalars& e, int col, uint
 // read the box has finished reading it.
 __device__ __forceinline__ uint32_t epi_box_acquire(const EpiScalars& e, uint32_t stage0,
                                                     uint32_t seq, int lane) {
-    const uint32_t box = stage0 + (e.bufs == 2 ? (seq & 1u) : 0u) * kEpiBoxBytes;
-    if (lane == 0) {
-        if (e.bufs == 2)
-            bulk_wait_read<1>();
-        else
-            bulk_wait_read<0>();
+    const uint32_t box = stage0 + (seq % (uint32_t)e.bufs) * kEpiBoxBytes;
+    if (lane == 0) {  // at most bufs - 1 of this warp's stores may still be reading smem
+        switch (e.bufs) {
+            case 1: bulk_wait_read<0>(); break;
+            case 2: bulk_wait_read<1>(); break;
+            case 3: bulk_wait_read<2>(); break;
+            default: bulk_wait_read<3>(); break;
+        }
     }
     __syncwarp();
     return box;
@@ -507,11 +516,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const uint32_t sA = raw + pad;
     const uint32_t sB = sA + (uint32_t)p.stages * kAStageBytes;
     const uint32_t sEpi = raw + pad + (uint32_t)p.stages * TT::kStageBytes;
+    const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
     SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * TT::kStageBytes +
-                                              kEpiBytes);
+                                              epi_bytes(epi_warps, p.epi_bufs));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
     const uint32_t full0 = smem_u32(&ctl->full[0]);
     const uint32_t empty0 = smem_u32(&ctl->empty[0]);
     const uint32_t tfull0 = smem_u32(&ctl->tmem_full[0]);

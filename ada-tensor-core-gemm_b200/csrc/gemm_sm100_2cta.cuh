@@ -53,8 +53,8 @@ struct PairTraits {
 };
 
 template <int BNP>
-constexpr size_t gemm2_smem_bytes(int stages) {
-    return 1024 + (size_t)stages * PairTraits<BNP>::kStageBytes + kEpiBytes + sizeof(SmemCtl);
+constexpr size_t gemm2_smem_bytes(int stages, uint32_t epi) {
+    return 1024 + (size_t)stages * PairTraits<BNP>::kStageBytes + epi + sizeof(SmemCtl);
 }
 
 // Four UMMA 256 x N x 16 of one k-block into `d_tmem` (K steps: +32 B for A, +bk for B).
@@ -108,11 +108,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
     const uint32_t sA = raw + pad;
     const uint32_t sB = sA + (uint32_t)p.stages * kHalfBytes;
     const uint32_t sEpi = sA + (uint32_t)p.stages * PT::kStageBytes;
-    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad +
-                                              (size_t)p.stages * PT::kStageBytes + kEpiBytes);
+    const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * PT::kStageBytes +
+                                              epi_bytes(epi_warps, p.epi_bufs));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
     const int cluster_id = blockIdx.x >> 1, num_clusters = gridDim.x >> 1;
