@@ -102,3 +102,37 @@ def test_generator_panels_are_slices_of_the_full_matrix():
     for first, n in [(0, 100), (48 * 10, 48 * 7), (64 * 48 - 5, 5)]:
         assert np.array_equal(b2g.fill_uniform(n, 3, 0, first=first), full[first:first + n])
         assert np.array_equal(O.fill_uniform((n,), 3, 0, first=first), full[first:first + n])
+
+
+def test_splitk_argument_validation_without_gpu():
+    """b2g_gemm_splitk / _noalloc reject bad split requests before touching the device."""
+    L = b2g.lib()
+    for fn in (L.b2g_gemm_splitk, L.b2g_gemm_splitk_noalloc):  # argtypes set by b2g.lib()
+        args = [None, None, None, None, 4, 4, 64, 64, 64, 4, 0, 0, 0, 1.0, -1, 0, 1]
+        assert fn(*args, -1, None) == b2g.ERR_ARG           # negative split factor
+        assert "splits" in b2g.last_error()
+        acc16 = list(args)
+        acc16[11] = b2g.ACC_F16
+        assert fn(*acc16, 2, None) == b2g.ERR_UNSUPPORTED    # split-K needs FP32 accumulation
+        bad_tile = list(args)
+        bad_tile[14] = 6
+        assert fn(*bad_tile, 0, None) == b2g.ERR_ARG         # tiles are -1 .. 5
+
+
+def test_last_launch_before_any_launch():
+    """b2g_last_launch reports an error on a thread that has launched nothing."""
+    import threading
+
+    out = {}
+
+    def probe():
+        try:
+            b2g.last_launch()
+            out["rc"] = b2g.OK
+        except b2g.B2GError as e:
+            out["rc"] = e.code
+
+    t = threading.Thread(target=probe)
+    t.start()
+    t.join()
+    assert out["rc"] == b2g.ERR_ARG
