@@ -31,7 +31,7 @@ B_NK, B_KN = 0, 1
 ACC_F32, ACC_F16 = 0, 1
 EPI_NONE, EPI_BIAS_RELU = 0, 1
 TILE_AUTO, TILE_128x128, TILE_128x256, TILE_256x256_2SM, TILE_128x64, TILE_256x512_2SM, \
-    TILE_SWAP_AB = -1, 0, 1, 2, 3, 4, 5
+    TILE_SWAP_AB, TILE_256x128_2SM = -1, 0, 1, 2, 3, 4, 5, 6
 
 # Every symbol include/b2g.h declares (the CPU tests check the library exports them all).
 EXPORTS = (

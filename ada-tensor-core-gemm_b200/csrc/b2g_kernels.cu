@@ -84,6 +84,7 @@ TileGeom geom(int tile) {
         case B2G_TILE_128x64: return {128, 64, 1, 128, 64};
         case B2G_TILE_256x512_2SM: return {kPairBM, 512, 2, 128, 128};
         case B2G_TILE_SWAP_AB: return {64, 128, 1, 64, 128};  // largest MT, for reports only
+        case B2G_TILE_256x128_2SM: return {kPairBM, 128, 2, 128, 64};
         default: return {kPairBM, kPairBN, 2, 128, 128};
     }
 }
@@ -95,15 +96,16 @@ const void* kernel_ptr(int tile) {
         case B2G_TILE_128x64: return (const void*)gemm_sm100_1cta<64>;
         case B2G_TILE_256x512_2SM: return (const void*)gemm_sm100_2cta<512>;
         case B2G_TILE_SWAP_AB: return (const void*)gemm_sm100_swap<64>;
+        case B2G_TILE_256x128_2SM: return (const void*)gemm_sm100_2cta<128>;
         default: return (const void*)gemm_sm100_2cta<256>;
     }
 }
 
-// Epilogue staging boxes (4 KiB each) of a launch, shared out among its epilogue warps. 8
-// for every shape: measured on B200, 16-32 boxes (fewer ring stages) gave nothing even where
-// D's writes dominate (16384^2 x 256: 810-813 TFLOP/s with 8-24 boxes) and cost up to 15%
-// at K >= 512, so the store path is not limited by stores in flight per warp.
-int epi_boxes_for(int /*num_kb*/) { return 8; }
+// Epilogue staging boxes (4 KiB each) of a launch, shared out among its epilogue warps: 16
+// for K <= 256 (two per warp, so the 8 epilogue warps store chunks in fenced pairs: 16384^2 x
+// 256 803 -> 827 TFLOP/s), else 8 (more boxes cost ring stages: -2% at K = 512, up to -15%
+// at K >= 1024 with 24-32 boxes; stores in flight per warp are not the limit).
+int epi_boxes_for(int num_kb) { return num_kb <= 4 ? 16 : 8; }
 
 size_t smem_needed(int tile, int stages, int epi_boxes = 8) {
     const uint32_t epi = (uint32_t)epi_boxes * kEpiBoxBytes;
@@ -113,6 +115,7 @@ size_t smem_needed(int tile, int stages, int epi_boxes = 8) {
         case B2G_TILE_128x64: return gemm_smem_bytes<64>(stages, epi);
         case B2G_TILE_256x512_2SM: return gemm2_smem_bytes<512>(stages, epi);
         case B2G_TILE_SWAP_AB: return gemm_swap_smem_bytes<64>(stages);
+        case B2G_TILE_256x128_2SM: return gemm2_smem_bytes<128>(stages, epi);
         default: return gemm2_smem_bytes<256>(stages, epi);
     }
 }
@@ -132,7 +135,7 @@ int max_stages_for(int tile, int smem_optin, int epi_boxes = 8) {
 }
 
 int ensure_kernel_attrs(int tile, const DeviceInfo& di) {
-    static bool done[6][kMaxDevices] = {};
+    static bool done[7][kMaxDevices] = {};
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
     if (di.device < kMaxDevices && done[tile][di.device]) return B2G_OK;
@@ -273,6 +276,10 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
         case B2G_TILE_256x512_2SM:
             grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
             e = launch_ex(gemm_sm100_2cta<512>, grid, threads, smem, s, tmA, tmB, tmBt, tmD, p);
+            break;
+        case B2G_TILE_256x128_2SM:
+            grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
+            e = launch_ex(gemm_sm100_2cta<128>, grid, threads, smem, s, tmA, tmB, tmBt, tmD, p);
             break;
         default:
             grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
@@ -529,8 +536,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         return fail(B2G_ERR_ARG, "epilogue must be 0 (none) or 1 (bias+ReLU), got %d", epilogue);
     if (tile != B2G_TILE_AUTO && tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 &&
         tile != B2G_TILE_256x256_2SM && tile != B2G_TILE_128x64 &&
-        tile != B2G_TILE_256x512_2SM && tile != B2G_TILE_SWAP_AB)
-        return fail(B2G_ERR_ARG, "tile must be -1 (auto) or 0..5, got %d", tile);
+        tile != B2G_TILE_256x512_2SM && tile != B2G_TILE_SWAP_AB && tile != B2G_TILE_256x128_2SM)
+        return fail(B2G_ERR_ARG, "tile must be -1 (auto) or 0..6, got %d", tile);
     if (stages != 0 && (stages < 2 || stages > kMaxStages))
         return fail(B2G_ERR_ARG, "stages must be 0 (auto) or 2..%d, got %d", kMaxStages, stages);
     if (group < 0) return fail(B2G_ERR_ARG, "group must be >= 0, got %d", group);
@@ -695,7 +702,9 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         const int clusters = max_pair_clusters(di, smem);
         const int rest = p.num_tiles % clusters;
         // K x N B loads 64-column boxes: a slice needs >= 64 columns per CTA
-        const int split = rest ? tail_split_for(rest, clusters, (b_mn && !wide) ? 2 : 4, wide) : 1;
+        // (256 x 128 tiles are not sliced: their 64-column slices would reload A for little)
+        const int max_split = g.bn == 128 ? 1 : b_mn ? std::max(1, g.bn / 128) : 4;
+        const int split = rest ? tail_split_for(rest, clusters, max_split, wide) : 1;
         if (split > 1) {
             p.dp_tiles = p.num_tiles - rest;
             p.tail_split = split;
@@ -764,7 +773,8 @@ B2G_EXPORT int b2g_config_info(int tile, int stages, int* threads, int* regs, in
     clear_error();
     if (tile == B2G_TILE_AUTO) tile = B2G_TILE_256x256_2SM;
     if (tile != B2G_TILE_128x128 && tile != B2G_TILE_128x256 && tile != B2G_TILE_256x256_2SM &&
-        tile != B2G_TILE_128x64 && tile != B2G_TILE_256x512_2SM && tile != B2G_TILE_SWAP_AB)
+        tile != B2G_TILE_128x64 && tile != B2G_TILE_256x512_2SM && tile != B2G_TILE_SWAP_AB &&
+        tile != B2G_TILE_256x128_2SM)
         return fail(B2G_ERR_UNSUPPORTED, "tile %d is not built", tile);
     DeviceInfo di;
     if (int rc = current_device(di)) return rc;

@@ -143,11 +143,12 @@ double frobenius_rows(const std::vector<uint16_t>& A, long long lda, const std::
 
 const char* tile_name(int t) {
     return t == 0 ? "128x128x64" : t == 1 ? "128x256x64" : t == 2 ? "256x256x64"
-         : t == 3 ? "128x64x64" : t == 4 ? "256x512x64" : t == 5 ? "swapAB" : "auto";
+         : t == 3 ? "128x64x64" : t == 4 ? "256x512x64" : t == 5 ? "swapAB"
+         : t == 6 ? "256x128x64" : "auto";
 }
 
 void usage(const char* argv0) {
-    printf("usage: %s [--m M --n N --k K] [--tile 0..5] [--stages 0|2..8]\n"
+    printf("usage: %s [--m M --n N --k K] [--tile 0..6] [--stages 0|2..8]\n"
            "       [--layout 2] [--group G] [--iters N] [--warmup N] [--check] [--cpu S]\n"
            "       [--noref] [--sweep] [--gsweep] [--unfused] [--soak SEC] [--window SEC]\n"
            "       [--acc f32|f16] [--fused] [--b-layout nk|kn] [--init ref|uniform]\n"
@@ -162,6 +163,7 @@ void usage(const char* argv0) {
            "       3 = 128x64x64   1 CTA, UMMA 128x64, TMEM 2x64 cols\n"
            "       4 = 256x512x64  2-CTA pair, two UMMA 256x256 halves, TMEM 512 cols\n"
            "       5 = swapAB      small M: UMMA 128 x MT (MT = 16..64 rows of A), B rows on M\n"
+           "       6 = 256x128x64  2-CTA pair, UMMA 256x128\n"
            "  --splits S split-K factor (0 automatic, 1 none, S >= 2 forced; default: automatic)\n"
            "  --stages   shared-memory ring depth (0 = deepest that fits)\n"
            "  --group G  L2 rasterization: G M-tiles walked column-major (1 = row-major)\n"

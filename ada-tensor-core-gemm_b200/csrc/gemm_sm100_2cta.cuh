@@ -46,7 +46,7 @@ constexpr uint32_t kPairTmemCols = 512;            // 2 x 256 columns: buffers o
 // Per-CTA shared memory of one stage: A half (16 KiB) + this CTA's BNP / 2 rows of B.
 template <int BNP>
 struct PairTraits {
-    static_assert(BNP == 256 || BNP == 512, "pair tile width 256 or 512");
+    static_assert(BNP == 128 || BNP == 256 || BNP == 512, "pair tile width 128, 256 or 512");
     static constexpr uint32_t kBStageBytes = (uint32_t)BNP / 2 * kBK * 2;  // 16 or 32 KiB
     static constexpr uint32_t kStageBytes = kHalfBytes + kBStageBytes;
     static constexpr bool kWide = BNP == 512;
@@ -384,8 +384,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                 const uint32_t tbase = tq + (uint32_t)(buf * kPairBN);
                 if (p.splits > 1) {
                     splitk_epilogue(p, es, &tmD, tbase, t, split, (int)rank, 2, q, warp - 2,
-                                    kPairBN, row0, n_first, c_first, stage0, lane, seq, epi,
-                                    [&] { release(buf); });
+                                    BNP < kPairBN ? BNP : kPairBN, row0, n_first, c_first, stage0,
+                                    lane, seq, epi, [&] { release(buf); });
                 } else {
                     epilogue_rows(p, es, &tmD, tbase, row0, n_first, width, c_first, stage0, lane,
                                   seq, acc16, epi);

@@ -63,6 +63,9 @@ enum { B2G_EPI_NONE = 0, B2G_EPI_BIAS_RELU = 1 }; /* epilogue                   
  *   B2G_TILE_SWAP_AB   : small M (decode): one CTA per 128 columns of D x MT rows, UMMA
  *                        128 x MT x 16 with B's rows on the 128 side (MT = 16, 32 or 64,
  *                        from M and N); B as N x K only, no split-K
+ *   B2G_TILE_256x128_2SM : a 2-CTA cluster, UMMA 256x128x16: per CTA 16 KiB of A + 8 KiB of
+ *                        B per k-block for 128 x 128 outputs (a quarter less than one CTA
+ *                        per 128 x 128 tile)
  *   B2G_TILE_256x256_2SM : a 2-CTA cluster (cta_group::2), UMMA 256x256x16, each CTA loads
  *                        its own 128 rows of A and 128 rows of B (no multicast)
  *   B2G_TILE_AUTO      : chosen from the shape                                           */
@@ -73,6 +76,7 @@ enum {
     B2G_TILE_128x64 = 3,
     B2G_TILE_256x512_2SM = 4,
     B2G_TILE_SWAP_AB = 5,
+    B2G_TILE_256x128_2SM = 6,
     B2G_TILE_AUTO = -1
 };
 

@@ -36,7 +36,8 @@ def test_config1_512_elementwise_vs_fp32_triple_loop(cuda):
 
 
 @pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
-                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM])
+                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM,
+                                  b2g.TILE_256x128_2SM])
 @pytest.mark.parametrize("shape", [(1, 1, 8), (1, 1, 1), (7, 9, 13), (128, 128, 64),
                                    (129, 257, 72), (300, 200, 100), (256, 512, 1000),
                                    (1000, 33, 64), (64, 640, 4096)])
@@ -50,7 +51,8 @@ def test_shapes_small(cuda, tile, shape):
 
 
 @pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
-                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM])
+                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM,
+                                  b2g.TILE_256x128_2SM])
 @pytest.mark.parametrize("stages", [2, 3, 4, 0])
 @pytest.mark.parametrize("group", [1, 2, 8])
 def test_tiles_stages_groups(cuda, tile, stages, group):
@@ -73,7 +75,8 @@ def test_pair_tail_slices(cuda, shape):
 
 
 @pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
-                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM])
+                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM,
+                                  b2g.TILE_256x128_2SM])
 @pytest.mark.parametrize("K,warps", [(1024, 8), (1088, 4), (64, 8)])
 @pytest.mark.parametrize("mode", ["plain", "fused", "f16acc"])
 def test_epilogue_warps_by_k(cuda, tile, K, warps, mode):
@@ -299,7 +302,8 @@ def test_probe_hbm(cuda):
 
 
 @pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
-                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM])
+                                  b2g.TILE_128x64, b2g.TILE_256x512_2SM,
+                                  b2g.TILE_256x128_2SM])
 @pytest.mark.parametrize("shape", [(384, 512, 256), (300, 520, 200), (1000, 64, 1000),
                                    (129, 1000, 72), (2304, 4352, 128)])
 def test_b_kn_layout(cuda, tile, shape):

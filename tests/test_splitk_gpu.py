@@ -15,7 +15,7 @@ ELEM_F32 = 2 * 2.0 ** -11
 
 
 @pytest.mark.parametrize("tile", [b2g.TILE_128x128, b2g.TILE_128x256, b2g.TILE_256x256_2SM,
-                                  b2g.TILE_128x64])
+                                  b2g.TILE_128x64, b2g.TILE_256x128_2SM])
 @pytest.mark.parametrize("splits", [2, 3, 7, 16])
 @pytest.mark.parametrize("fused", [False, True])
 def test_forced_splits(cuda, tile, splits, fused):
