@@ -7,11 +7,11 @@
 //   warp 0 (1 thread)  TMA producer: for every k-block, wait for a free stage, then two
 //                      cp.async.bulk.tensor loads (A 128x64, B BNx64, 128-byte swizzle)
 //                      whose bytes complete the stage's `full` mbarrier.
-//   warp 1 (1 thread)  MMA issuer: allocates TMEM (2 x BN columns: a double-buffered
-//                      accumulator), waits for `full`, issues 4 tcgen05.mma (K = 16 each)
-//                      reading both operands from shared memory, and tcgen05.commit's the
-//                      stage's `empty` barrier; after the last k-block it commits
-//                      `tmem_full[buf]`.
+//   warp 1             MMA issuer (the whole warp runs the loop, one elected lane issues):
+//                      allocates TMEM (2 x BN columns: a double-buffered accumulator), waits
+//                      for `full`, issues 4 tcgen05.mma (K = 16 each) reading both operands
+//                      from shared memory, and tcgen05.commit's the stage's `empty` barrier;
+//                      after the last k-block it commits `tmem_full[buf]`.
 //   warps 2..          epilogue (4 or 8 warps): wait for `tmem_full[buf]`, tcgen05.ld 64
 //                      columns at a time (warp w reads TMEM lanes 32*(w%4)..+31 = tile
 //                      rows; with 8 warps two share a quarter, alternate chunks), apply the

@@ -1,19 +1,22 @@
 // gemm_sm100_2cta.cuh -- persistent FP16 GEMM on 2-CTA clusters (tcgen05 cta_group::2).
 //
-// A cluster of two CTAs on two SMs computes one 256 x 256 output tile with UMMA
-// 256 x 256 x 16 instructions issued by the even ("leader") CTA. Each CTA stages only its
-// own half of the operands in shared memory -- 128 rows of A and 128 rows of B per k-block
-// (32 KiB per stage instead of 48 KiB for a 128 x 256 tile on one SM) -- and the tensor
-// core reads both CTAs' halves. Every CTA keeps its 128 rows of the 256 x 256 accumulator
-// in its own TMEM, double-buffered (2 x 256 columns). No TMA multicast is used: each CTA
-// loads its halves itself (this code also runs on multi-GPU jobs).
+// A cluster of two CTAs on two SMs computes one 256 x BNP output tile (BNP = 128, 256 or
+// 512) with UMMA 256 x N x 16 instructions issued by the even ("leader") CTA. Each CTA stages
+// only its own half of the operands in shared memory -- 128 rows of A and BNP / 2 rows of B
+// per k-block (32 KiB per stage at BNP = 256 instead of 48 KiB for a 128 x 256 tile on one
+// SM) -- and the tensor core reads both CTAs' halves. Every CTA keeps its 128 rows of the
+// accumulator in its own 512 TMEM columns. No TMA multicast is used: each CTA loads its
+// halves itself (this code also runs on multi-GPU jobs).
 //
-// BNP = 512 ("wide" pair tile, 256 x 512): each CTA's 128 x 512 accumulator fills all 512
-// TMEM columns, as two 256-column halves issued as separate UMMA 256 x 256 x 16. Per k-block
-// a CTA then loads 16 KiB of A and 32 KiB of B for twice the work, so the L2 -> SM traffic per
-// FLOP drops by a quarter. There is no second accumulator; instead the halves are released
-// separately: the epilogue drains half 0, frees it, then half 1, while the MMA warp starts
-// the next tile on half 0 and waits for half 1 only before its first half-1 MMA.
+// BNP = 128 and 256: the accumulator is double-buffered (two 256-column buffers), so the
+// epilogue of one tile overlaps the mainloop of the next.
+// BNP = 512 ("wide" pair tile): each CTA's 128 x 512 accumulator fills all 512 columns, as two
+// 256-column halves issued as separate UMMA 256 x 256 x 16. Per k-block a CTA then loads
+// 16 KiB of A and 32 KiB of B for twice the work, so the L2 -> SM traffic per FLOP drops by a
+// quarter. There is no second accumulator; instead the halves are released separately: the
+// epilogue drains half 0, frees it, then half 1, while the MMA warp starts the next tile on
+// half 0 and defers the half-1 MMAs of up to 3 k-blocks (holding their stages) until half 1
+// is free.
 //
 // Work list: whole tiles first, then the tiles of the last, partial wave cut into
 // `tail_split` (2 or 4) column slices (UMMA N = slice width <= 256; B read through a second
@@ -25,7 +28,8 @@
 //     then loads its A half (128 x 64) and B half (width/2 x 64). Both CTAs' loads complete
 //     on the LEADER's `full` barrier, which the leader's producer armed with the pair's
 //     total byte count.
-//   warp 1, one thread, leader only: MMA issuer. Waits for `full` (both halves landed),
+//   warp 1, leader only: MMA issuer (whole warp runs the loop, one elected lane issues).
+//     Waits for `full` (both halves landed),
 //     issues 4 x tcgen05.mma.cta_group::2, then a multicast tcgen05.commit that arrives on
 //     the `empty` barrier of the same stage in both CTAs. After the last k-block, a
 //     multicast commit on `tmem_full[buf]` of both CTAs.

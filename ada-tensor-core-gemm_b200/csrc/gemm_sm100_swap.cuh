@@ -10,7 +10,7 @@
 //
 // Roles as in gemm_sm100_1cta: warp 0 TMA producer (B box 128 rows, A box MT rows per
 // 64-wide k-block), warp 1 MMA issuer (UMMA 128 x MT x 16, double-buffered accumulator of
-// 2 x MT TMEM columns), warps 2-5 epilogue. In TMEM, lane = column n of D and TMEM column j =
+// 2 x MT TMEM columns), warps 2-5 epilogue (4 warps, one per TMEM lane quarter). In TMEM, lane = column n of D and TMEM column j =
 // row m0 + j of D, so each thread holds a column of the output block: it converts its MT
 // values (alpha, bias[n], ReLU, FP16) and stores them row by row -- for every m the 32 lanes
 // of a warp write 32 consecutive columns (64 contiguous bytes). No staging, no TMA store.
