@@ -40,6 +40,7 @@ EXPORTS = (
     "b2g_fill_lcg_f16", "b2g_fill_uniform_f16", "b2g_tile_coord",
     "b2g_selftest_wait_timeout", "b2g_set_wait_timeout_us", "b2g_version",
     "b2g_kernel_clock", "b2g_last_launch", "b2g_gemm_splitk", "b2g_gemm_splitk_noalloc",
+    "b2g_gemm_multi", "b2g_allgather_rows",
 )
 
 
@@ -107,6 +108,11 @@ def lib():
         L.b2g_kernel_clock.argtypes = [C.POINTER(d), C.POINTER(d)]
         L.b2g_last_launch.restype = i
         L.b2g_last_launch.argtypes = [ip, ip, ip, ip, ip, ip]
+        L.b2g_gemm_multi.restype = i
+        L.b2g_gemm_multi.argtypes = [i, ip, vp, vp, vp, vp, i, i, i, ll, ll, ll, i, i, i, f, i,
+                                     i, i, vp, i]
+        L.b2g_allgather_rows.restype = i
+        L.b2g_allgather_rows.argtypes = [i, ip, vp, vp, i, i, ll, vp, i]
         _lib = L
     return _lib
 
@@ -197,6 +203,62 @@ def gemm_noalloc(A, B, D, bias=None, *, b_layout: int = B_NK, acc: int = ACC_F32
                                          A.stride(0), B.stride(0), D.stride(0), b_layout, acc,
                                          epilogue, alpha, tile, stages, group, splits,
                                          _stream_ptr(stream)))
+
+
+def _ptr_array(xs):
+    return (C.c_void_p * len(xs))(*[_ptr(x) for x in xs])
+
+
+def _devices_array(devices):
+    return (C.c_int * len(devices))(*devices)
+
+
+# rows [r0, r1) that device g of ngpu computes in gemm_multi (the C library's split)
+from .shard import panel as panel_rows  # noqa: E402
+
+
+def gemm_multi(A, B, D, bias=None, *, M: int, devices, b_layout: int = B_NK,
+               acc: int = ACC_F32, epilogue: int = EPI_NONE, alpha: float = 1.0,
+               tile: int = TILE_AUTO, stages: int = 0, group: int = 1, streams=None,
+               sync: bool = True) -> None:
+    """b2g_gemm_multi: one M x N x K GEMM split by M-row panels over ``devices``.
+
+    A, D: per-device panels (rows from :func:`panel_rows`), B: per-device full copies, bias:
+    per-device copies or None, streams: per-device streams or None. Row pitches are taken from
+    the first device's tensors and must agree on every device."""
+    ngpu = len(devices)
+    if not (len(A) == len(B) == len(D) == ngpu) or (bias is not None and len(bias) != ngpu):
+        raise B2GError(ERR_ARG, "one A panel, B copy, D panel (and bias) per device")
+    K = A[0].shape[1]
+    N = B[0].shape[0] if b_layout == B_NK else B[0].shape[1]
+    for g in range(ngpu):
+        r0, r1 = panel_rows(M, ngpu, g)
+        if A[g].shape[0] != r1 - r0 or tuple(D[g].shape) != (r1 - r0, N):
+            raise B2GError(ERR_ARG, f"device {g}: panel rows must be {r1 - r0}")
+        if (A[g].stride(0), B[g].stride(0), D[g].stride(0)) != \
+                (A[0].stride(0), B[0].stride(0), D[0].stride(0)):
+            raise B2GError(ERR_ARG, f"device {g}: row pitches differ from device 0")
+    sp = None if streams is None else _ptr_array([_stream_ptr(s) for s in streams])
+    _check(lib().b2g_gemm_multi(ngpu, _devices_array(devices), _ptr_array(A), _ptr_array(B),
+                                _ptr_array(D), None if bias is None else _ptr_array(bias), M, N,
+                                K, A[0].stride(0), B[0].stride(0), D[0].stride(0), b_layout, acc,
+                                epilogue, alpha, tile, stages, group, sp, int(sync)))
+
+
+def allgather_rows(D, D_full, *, devices, streams=None, sync: bool = True) -> None:
+    """b2g_allgather_rows: copy every device's D panel into every device's M x N ``D_full``
+    over peer-to-peer copies."""
+    ngpu = len(devices)
+    if not (len(D) == len(D_full) == ngpu):
+        raise B2GError(ERR_ARG, "one D panel and one D_full per device")
+    M, N = D_full[0].shape
+    ldd = D_full[0].stride(0)
+    for g in range(ngpu):
+        if D[g].stride(0) != ldd or D_full[g].stride(0) != ldd:
+            raise B2GError(ERR_ARG, "D panels and D_full must share one row pitch")
+    sp = None if streams is None else _ptr_array([_stream_ptr(s) for s in streams])
+    _check(lib().b2g_allgather_rows(ngpu, _devices_array(devices), _ptr_array(D),
+                                    _ptr_array(D_full), M, N, ldd, sp, int(sync)))
 
 
 def sync_status(stream=None) -> None:

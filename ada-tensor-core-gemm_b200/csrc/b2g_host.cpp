@@ -195,3 +195,120 @@ B2G_EXPORT int b2g_cublas_gemm(const void* A, const void* B, void* D, int M, int
     if (st != CUBLAS_STATUS_SUCCESS) return fail(B2G_ERR_LIBRARY, "cublasGemmEx: status %d", (int)st);
     return B2G_OK;
 }
+
+// ---------------------------------------------------------------------------------------
+// Multi-GPU: M-row panels from one process (the reference's multi-GPU plan; it has no
+// multi-GPU code of its own). One host thread per device.
+// ---------------------------------------------------------------------------------------
+#include <thread>
+#include <vector>
+
+namespace b2g {
+namespace {
+
+// Rows [r0, r1) of panel g of ngpu: M split as evenly as possible.
+inline void panel_rows(int M, int ngpu, int g, int& r0, int& r1) {
+    r0 = (int)((long long)M * g / ngpu);
+    r1 = (int)((long long)M * (g + 1) / ngpu);
+}
+
+// Runs fn(g) on one host thread per device (device made current on its thread) and folds
+// the results: the first failure (in device order) becomes the caller's error.
+template <class Fn>
+int for_each_device(int ngpu, const int* devices, Fn fn) {
+    std::vector<int> rc((size_t)ngpu, B2G_OK);
+    std::vector<std::string> msg((size_t)ngpu);
+    std::vector<std::thread> th;
+    th.reserve((size_t)ngpu);
+    for (int g = 0; g < ngpu; ++g) {
+        th.emplace_back([&, g] {
+            cudaError_t e = cudaSetDevice(devices[g]);
+            if (e != cudaSuccess) {
+                rc[(size_t)g] = B2G_ERR_CUDA;
+                msg[(size_t)g] = std::string("cudaSetDevice: ") + cudaGetErrorString(e);
+                return;
+            }
+            rc[(size_t)g] = fn(g);
+            if (rc[(size_t)g] != B2G_OK) msg[(size_t)g] = b2g_last_error();
+        });
+    }
+    for (auto& t : th) t.join();
+    for (int g = 0; g < ngpu; ++g)
+        if (rc[(size_t)g] != B2G_OK)
+            return b2g::fail(rc[(size_t)g], "device %d (panel %d of %d): %s", devices[g], g, ngpu,
+                             msg[(size_t)g].c_str());
+    return B2G_OK;
+}
+
+}  // namespace
+}  // namespace b2g
+
+B2G_EXPORT int b2g_gemm_multi(int ngpu, const int* devices, const void* const* A,
+                              const void* const* B, void* const* D, const void* const* bias,
+                              int M, int N, int K, long long lda, long long ldb, long long ldd,
+                              int b_layout, int acc, int epilogue, float alpha, int tile,
+                              int stages, int group, void* const* streams, int sync) {
+    using namespace b2g;
+    clear_error();
+    if (ngpu < 1 || !devices || !A || !B || !D)
+        return fail(B2G_ERR_ARG, "ngpu >= 1 and the devices, A, B, D arrays are required");
+    if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_ARG, "negative shape M=%d N=%d K=%d", M, N, K);
+    return for_each_device(ngpu, devices, [&](int g) -> int {
+        int r0, r1;
+        panel_rows(M, ngpu, g, r0, r1);
+        void* s = streams ? streams[g] : nullptr;
+        int rc = b2g_gemm(A[g], B[g], D[g], bias ? bias[g] : nullptr, r1 - r0, N, K, lda, ldb,
+                          ldd, b_layout, acc, epilogue, alpha, tile, stages, group, s);
+        if (rc == B2G_OK && sync) rc = b2g_sync_status(s);
+        return rc;
+    });
+}
+
+B2G_EXPORT int b2g_allgather_rows(int ngpu, const int* devices, void* const* D,
+                                  void* const* D_full, int M, int N, long long ldd,
+                                  void* const* streams, int sync) {
+    using namespace b2g;
+    clear_error();
+    if (ngpu < 1 || !devices || !D || !D_full)
+        return fail(B2G_ERR_ARG, "ngpu >= 1 and the devices, D, D_full arrays are required");
+    if (M < 0 || N < 0 || ldd < N) return fail(B2G_ERR_ARG, "bad shape M=%d N=%d ldd=%lld", M, N, ldd);
+    // direct peer access between every pair (NVLink / NVSwitch); already-enabled is fine
+    for (int g = 0; g < ngpu; ++g) {
+        if (cudaSetDevice(devices[g]) != cudaSuccess)
+            return fail(B2G_ERR_CUDA, "cudaSetDevice(%d)", devices[g]);
+        for (int h = 0; h < ngpu; ++h) {
+            if (h == g) continue;
+            int ok = 0;
+            cudaDeviceCanAccessPeer(&ok, devices[g], devices[h]);
+            if (ok) {
+                cudaError_t e = cudaDeviceEnablePeerAccess(devices[h], 0);
+                if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+                    return fail(B2G_ERR_CUDA, "peer access %d -> %d: %s", devices[g], devices[h],
+                                cudaGetErrorString(e));
+                cudaGetLastError();
+            }
+        }
+    }
+    return for_each_device(ngpu, devices, [&](int g) -> int {
+        int r0, r1;
+        panel_rows(M, ngpu, g, r0, r1);
+        cudaStream_t s = streams ? (cudaStream_t)streams[g] : nullptr;
+        const size_t pitch = (size_t)ldd * 2;
+        for (int k = 0; k < ngpu; ++k) {
+            const int h = (g + k) % ngpu;  // start at a different peer on every device
+            if (r1 <= r0) break;
+            cudaError_t e = cudaMemcpy2DAsync(static_cast<char*>(D_full[h]) + (size_t)r0 * pitch,
+                                              pitch, D[g], pitch, (size_t)N * 2,
+                                              (size_t)(r1 - r0), cudaMemcpyDefault, s);
+            if (e != cudaSuccess)
+                return fail(B2G_ERR_CUDA, "panel copy to device %d: %s", devices[h],
+                            cudaGetErrorString(e));
+        }
+        if (sync) {
+            cudaError_t e = cudaStreamSynchronize(s);
+            if (e != cudaSuccess)
+                return fail(B2G_ERR_CUDA, "all-gather synchronize: %s", cudaGetErrorString(e));
+        }
+        return B2G_OK;
+    });
+}

@@ -9,14 +9,18 @@
 //
 // Differences, all because the hardware path changed:
 //   --tile    selects B200 tiles: -1 = from the shape (default), 0 = 128x128, 1 = 128x256,
-//             2 = 256x256 2-SM pair, 3 = 128x64
+//             2 = 256x256 2-SM pair, 3 = 128x64, 4 = 256x512 2-SM pair, 5 = swap-AB,
+//             6 = 256x128 2-SM pair
 //   --layout  only 2 (swizzle) exists on sm_100a: TMA writes the 128-byte-swizzled layout
 //             tcgen05.mma reads; 0 / 1 print a SKIP row like an unsupported config
 //   --stages  shared-memory ring depth 2..8 (0 = deepest that fits); --sweep runs 2..8
 //   no K % 32 restriction (TMA zero-fills the K tail); A/B leading dimensions are padded
 //             to a multiple of 8 elements when K is not (16-byte TMA row strides)
 // New flags: --acc f32|f16, --fused, --b-layout nk|kn, --init ref|uniform, --seed S,
-//            --dist LO,HI, --frob ROWS, --json.
+//            --dist LO,HI, --frob ROWS, --json, --splits S, --gpus N, --allgather.
+//   --gpus N  one GEMM split by M-row panels over devices 0..N-1 (b2g_gemm_multi: A and D
+//             by rows, B copied to every device); --allgather then copies every panel to
+//             every device over NVLink (b2g_allgather_rows), timed on its own.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -48,6 +52,8 @@ struct Args {
     int tile = -1, stages = 0, layout = 2, group = 0;  // -1 / 0 = chosen from the shape
     int iters = 50, warmup = 20;
     int splits = -1;    // split-K factor: -1 = b2g_gemm (automatic), else b2g_gemm_splitk
+    int gpus = 1;       // devices for the M-panel multi-GPU run (b2g_gemm_multi)
+    bool allgather = false;
     int cpu = 0;        // output elements verified by the FP64 host spot check
     int frob = 0;       // rows of D checked by an FP64 relative Frobenius norm
     double soak = 0;    // seconds of back-to-back launches (0 = fixed iters)
@@ -152,7 +158,8 @@ void usage(const char* argv0) {
            "       [--layout 2] [--group G] [--iters N] [--warmup N] [--check] [--cpu S]\n"
            "       [--noref] [--sweep] [--gsweep] [--unfused] [--soak SEC] [--window SEC]\n"
            "       [--acc f32|f16] [--fused] [--b-layout nk|kn] [--init ref|uniform]\n"
-           "       [--seed S] [--dist LO,HI] [--frob ROWS] [--json]\n"
+           "       [--seed S] [--dist LO,HI] [--frob ROWS] [--json] [--splits S]\n"
+           "       [--gpus N [--allgather]]\n"
            "  --check    compare against cuBLAS on the device (max |x-y|/max(1,|y|))\n"
            "  --cpu S    verify S output elements against an FP64 host dot product\n"
            "  --frob R   FP64 relative Frobenius error over R rows spread through D\n"
@@ -165,12 +172,201 @@ void usage(const char* argv0) {
            "       5 = swapAB      small M: UMMA 128 x MT (MT = 16..64 rows of A), B rows on M\n"
            "       6 = 256x128x64  2-CTA pair, UMMA 256x128\n"
            "  --splits S split-K factor (0 automatic, 1 none, S >= 2 forced; default: automatic)\n"
+           "  --gpus N   M-row panels over devices 0..N-1 (b2g_gemm_multi), B on every device;\n"
+           "             --allgather then gathers D on every device over NVLink (timed apart)\n"
            "  --stages   shared-memory ring depth (0 = deepest that fits)\n"
            "  --group G  L2 rasterization: G M-tiles walked column-major (1 = row-major)\n"
            "  --sweep    stages 2..8 at fixed tile/group;  --gsweep  group 1,2,4,8,16\n"
            "  --acc      f32 (default) or f16 accumulation; --fused alpha*acc+bias+ReLU\n"
            "  --init     ref = the reference's LCG (default), uniform = seeded U[LO,HI]\n",
            argv0);
+}
+
+// --gpus N: the M-panel plan over devices 0..N-1 through b2g_gemm_multi (and, with
+// --allgather, b2g_allgather_rows). Device time per step is the maximum over the devices of
+// CUDA-event time on each device's stream, as the multi-GPU timing rule asks.
+int run_multi(const Args& a, const std::vector<uint16_t>& hA, const std::vector<uint16_t>& hB,
+              const std::vector<uint16_t>& hBias, long long lda, long long ldb, long long ldd) {
+    int ndev = 0;
+    CUDA_CHECK(cudaGetDeviceCount(&ndev));
+    if (a.gpus < 1 || a.gpus > ndev) {
+        fprintf(stderr, "--gpus %d: %d device(s) visible\n", a.gpus, ndev);
+        return 2;
+    }
+    if (a.soak > 0 || a.sweep || a.gsweep || a.unfused || a.splits >= 0) {
+        fprintf(stderr, "--gpus runs one configuration: no --soak/--sweep/--gsweep/--unfused/--splits\n");
+        return 2;
+    }
+    const int G = a.gpus;
+    const size_t brows = a.b_layout == B2G_B_NK ? (size_t)a.N : (size_t)a.K;
+    const size_t nB = brows * (size_t)ldb, nFull = (size_t)a.M * (size_t)ldd;
+    std::vector<int> devs(G);
+    std::vector<void*> dA(G), dB(G), dD(G), dBias(G), dFull(G, nullptr);
+    std::vector<void*> streams(G);
+    std::vector<cudaEvent_t> t0(G), t1(G);
+    for (int g = 0; g < G; ++g) {
+        devs[g] = g;
+        const int r0 = (int)((long long)a.M * g / G), r1 = (int)((long long)a.M * (g + 1) / G);
+        const size_t rows = (size_t)(r1 - r0);
+        CUDA_CHECK(cudaSetDevice(g));
+        CUDA_CHECK(cudaMalloc(&dA[g], std::max<size_t>(rows * lda, 8) * 2));
+        CUDA_CHECK(cudaMalloc(&dB[g], std::max<size_t>(nB, 8) * 2));
+        CUDA_CHECK(cudaMalloc(&dD[g], std::max<size_t>(rows * ldd, 8) * 2));
+        CUDA_CHECK(cudaMalloc(&dBias[g], hBias.size() * 2));
+        if (a.allgather) CUDA_CHECK(cudaMalloc(&dFull[g], std::max<size_t>(nFull, 8) * 2));
+        if (rows) CUDA_CHECK(cudaMemcpy(dA[g], &hA[(size_t)r0 * lda], rows * lda * 2,
+                                        cudaMemcpyHostToDevice));
+        CUDA_CHECK(cudaMemcpy(dB[g], hB.data(), nB * 2, cudaMemcpyHostToDevice));
+        CUDA_CHECK(cudaMemcpy(dBias[g], hBias.data(), hBias.size() * 2, cudaMemcpyHostToDevice));
+        cudaStream_t s;
+        CUDA_CHECK(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+        streams[g] = s;
+        CUDA_CHECK(cudaEventCreate(&t0[g]));
+        CUDA_CHECK(cudaEventCreate(&t1[g]));
+    }
+    const int epi = a.fused ? B2G_EPI_BIAS_RELU : B2G_EPI_NONE;
+    auto launch = [&](int sync) {
+        return b2g_gemm_multi(G, devs.data(), (const void* const*)dA.data(),
+                              (const void* const*)dB.data(), dD.data(),
+                              a.fused ? (const void* const*)dBias.data() : nullptr, a.M, a.N, a.K,
+                              lda, ldb, ldd, a.b_layout, a.acc, epi, 1.0f, a.tile, a.stages,
+                              a.group, streams.data(), sync);
+    };
+    auto sync_all = [&]() {
+        for (int g = 0; g < G; ++g) {
+            CUDA_CHECK(cudaSetDevice(g));
+            CUDA_CHECK(cudaStreamSynchronize((cudaStream_t)streams[g]));
+        }
+    };
+    // time `body` over `n` repetitions: events on every device's stream, max over devices
+    auto timed = [&](int n, auto&& body) -> double {
+        sync_all();
+        for (int g = 0; g < G; ++g) {
+            CUDA_CHECK(cudaSetDevice(g));
+            CUDA_CHECK(cudaEventRecord(t0[g], (cudaStream_t)streams[g]));
+        }
+        for (int i = 0; i < n; ++i)
+            if (body() != B2G_OK) {
+                fprintf(stderr, "error: %s\n", b2g_last_error());
+                exit(1);
+            }
+        double worst = 0;
+        for (int g = 0; g < G; ++g) {
+            CUDA_CHECK(cudaSetDevice(g));
+            CUDA_CHECK(cudaEventRecord(t1[g], (cudaStream_t)streams[g]));
+        }
+        for (int g = 0; g < G; ++g) {
+            CUDA_CHECK(cudaSetDevice(g));
+            CUDA_CHECK(cudaEventSynchronize(t1[g]));
+            float ms = 0;
+            CUDA_CHECK(cudaEventElapsedTime(&ms, t0[g], t1[g]));
+            worst = std::max(worst, (double)ms);
+        }
+        return worst / std::max(1, n);
+    };
+    for (int i = 0; i < a.warmup; ++i)
+        if (launch(0) != B2G_OK) {
+            fprintf(stderr, "error: %s\n", b2g_last_error());
+            return 1;
+        }
+    if (launch(1) != B2G_OK) {  // one checked launch: every device's status word
+        fprintf(stderr, "error: %s\n", b2g_last_error());
+        return 1;
+    }
+    const double flop = 2.0 * a.M * a.N * a.K;
+    const double ms = timed(a.iters, [&]() { return launch(0); });
+    const double tflops = flop / (ms * 1e-3) / 1e12;
+    if (launch(1) != B2G_OK) {
+        fprintf(stderr, "error: %s\n", b2g_last_error());
+        return 1;
+    }
+    double ag_ms = -1, ag_gbs = -1;
+    if (a.allgather) {
+        auto gather = [&]() {
+            return b2g_allgather_rows(G, devs.data(), dD.data(), dFull.data(), a.M, a.N, ldd,
+                                      streams.data(), 0);
+        };
+        for (int i = 0; i < std::max(1, a.warmup / 4); ++i)
+            if (gather() != B2G_OK) {
+                fprintf(stderr, "error: %s\n", b2g_last_error());
+                return 1;
+            }
+        ag_ms = timed(std::max(1, a.iters / 4), gather);
+        // bytes each device receives from its peers per gather
+        const double recv = (double)a.M * a.N * 2.0 * (G - 1) / G;
+        ag_gbs = recv / (ag_ms * 1e-3) / 1e9;
+    }
+    sync_all();
+
+    // assemble D from the panels; with --allgather, every device's gathered copy must equal it
+    std::vector<uint16_t> hD(nFull);
+    for (int g = 0; g < G; ++g) {
+        const int r0 = (int)((long long)a.M * g / G), r1 = (int)((long long)a.M * (g + 1) / G);
+        CUDA_CHECK(cudaSetDevice(g));
+        if (r1 > r0)
+            CUDA_CHECK(cudaMemcpy(&hD[(size_t)r0 * ldd], dD[g], (size_t)(r1 - r0) * ldd * 2,
+                                  cudaMemcpyDeviceToHost));
+    }
+    int gather_ok = -1;
+    if (a.allgather) {
+        gather_ok = 1;
+        // whole copies up to 256 MiB, else 257 rows spread through D
+        const bool whole = nFull * 2 <= (256u << 20);
+        std::vector<uint16_t> row((size_t)ldd);
+        for (int g = 0; g < G && gather_ok; ++g) {
+            CUDA_CHECK(cudaSetDevice(g));
+            if (whole) {
+                std::vector<uint16_t> hF(nFull);
+                CUDA_CHECK(cudaMemcpy(hF.data(), dFull[g], nFull * 2, cudaMemcpyDeviceToHost));
+                gather_ok = memcmp(hF.data(), hD.data(), nFull * 2) == 0;
+            } else {
+                for (int r = 0; r <= 256 && gather_ok; ++r) {
+                    const size_t m = (size_t)((long long)r * (a.M - 1) / 256);
+                    CUDA_CHECK(cudaMemcpy(row.data(), (const uint16_t*)dFull[g] + m * ldd,
+                                          (size_t)ldd * 2, cudaMemcpyDeviceToHost));
+                    gather_ok = memcmp(row.data(), &hD[m * ldd], (size_t)a.N * 2) == 0;
+                }
+            }
+        }
+    }
+    const bool epi_on = a.fused;
+    double cpurel = -1, frob = -1;
+    int wm = -1, wn = -1;
+    if (a.cpu > 0)
+        cpurel = spot_check(hA, lda, hB, ldb, a.b_layout, hD, ldd, hBias, a.M, a.N, a.K, a.cpu,
+                            epi_on, 1.0f, &wm, &wn);
+    if (a.frob > 0)
+        frob = frobenius_rows(hA, lda, hB, ldb, a.b_layout, hD, ldd, hBias, a.M, a.N, a.K,
+                              a.frob, epi_on, 1.0f);
+
+    printf("# problem       : M=%d N=%d K=%d over %d GPU(s), M-row panels, B on every device\n",
+           a.M, a.N, a.K, G);
+    printf("gpus=%d  tile=%d  ms=%.4f  TFLOP/s=%.2f  per_gpu=%.2f", G, a.tile, ms, tflops,
+           tflops / G);
+    if (ag_ms >= 0)
+        printf("  allgather_ms=%.4f  allgather_GB/s=%.1f  gather=%s", ag_ms, ag_gbs,
+               gather_ok ? "OK" : "FAIL");
+    if (cpurel >= 0)
+        printf("  cpu=%.2e%s(worst m=%d n=%d)", cpurel, cpurel < 3e-2 ? " OK " : " FAIL ", wm, wn);
+    if (frob >= 0) printf("  frob=%.2e", frob);
+    printf("\n");
+    if (a.json)
+        printf("{\"M\": %d, \"N\": %d, \"K\": %d, \"gpus\": %d, \"tile\": %d, \"acc\": \"%s\", "
+               "\"ms\": %.5f, \"tflops\": %.3f, \"tflops_per_gpu\": %.3f, \"allgather_ms\": %.5f, "
+               "\"allgather_gbs\": %.2f, \"gather_ok\": %d, \"cpu_maxrel\": %.3e, "
+               "\"frob_rel\": %.3e}\n",
+               a.M, a.N, a.K, G, a.tile, a.acc == B2G_ACC_F32 ? "f32" : "f16", ms, tflops,
+               tflops / G, ag_ms, ag_gbs, gather_ok, cpurel, frob);
+    fflush(stdout);
+    for (int g = 0; g < G; ++g) {
+        cudaSetDevice(g);
+        cudaFree(dA[g]); cudaFree(dB[g]); cudaFree(dD[g]); cudaFree(dBias[g]);
+        if (dFull[g]) cudaFree(dFull[g]);
+        cudaStreamDestroy((cudaStream_t)streams[g]);
+        cudaEventDestroy(t0[g]);
+        cudaEventDestroy(t1[g]);
+    }
+    return (gather_ok == 0 || (cpurel >= 3e-2) || (frob >= 0 && frob > 1e-2)) ? 1 : 0;
 }
 
 }  // namespace
@@ -192,6 +388,8 @@ int main(int argc, char** argv) {
         else if (eq("--warmup")) a.warmup = val();
         else if (eq("--group")) a.group = val();
         else if (eq("--splits")) a.splits = val();
+        else if (eq("--gpus")) a.gpus = val();
+        else if (eq("--allgather")) a.allgather = true;
         else if (eq("--cpu")) a.cpu = val();
         else if (eq("--frob")) a.frob = val();
         else if (eq("--soak")) a.soak = dval();
@@ -268,6 +466,8 @@ int main(int argc, char** argv) {
                 else hB[(size_t)k * ldb + n] = v;
             }
     }
+    if (a.gpus != 1 || a.allgather) return run_multi(a, hA, hB, hBias, lda, ldb, ldd);
+
     void *dA, *dB, *dD, *dRef, *dBias;
     float* dErr;
     CUDA_CHECK(cudaMalloc(&dA, std::max<size_t>(nA, 8) * 2));

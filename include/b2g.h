@@ -141,6 +141,29 @@ int b2g_gemm_splitk_noalloc(const void* A, const void* B, void* D, const void* b
                             int b_layout, int acc, int epilogue, float alpha, int tile,
                             int stages, int group, int splits, void* stream);
 
+/* One GEMM over `ngpu` devices by M-row panels, from one host process with one host thread
+ * per device: the reference's multi-GPU plan (A split by rows, B replicated, no reduction;
+ * the reference itself has no multi-GPU code). Device devices[g] computes rows
+ * [M*g/ngpu, M*(g+1)/ngpu) of D. Per device, the caller passes pointers on that device:
+ * A[g] = its panel of A (rows x K, lda), B[g] = a full copy of B, D[g] = its panel of D
+ * (rows x N, ldd), bias[g] (bias may be NULL), streams[g] (streams may be NULL: the legacy
+ * stream of each device). The other arguments mean what they mean for b2g_gemm. Returns
+ * after every device's launch is enqueued, or with `sync` = 1 after every device finished
+ * and its status word was checked (b2g_sync_status). A failure names the device. */
+int b2g_gemm_multi(int ngpu, const int* devices, const void* const* A, const void* const* B,
+                   void* const* D, const void* const* bias, int M, int N, int K, long long lda,
+                   long long ldb, long long ldd, int b_layout, int acc, int epilogue, float alpha,
+                   int tile, int stages, int group, void* const* streams, int sync);
+
+/* All-gather of the D panels of b2g_gemm_multi over NVLink / NVSwitch: device g copies its
+ * rows [M*g/ngpu, M*(g+1)/ngpu) (D[g], pitch ldd) into D_full[h] (M x N, pitch ldd, on device
+ * h) for every h, with peer-to-peer copies on streams[g] (peer access is enabled as needed).
+ * Each device's copies are ordered after its own earlier work on streams[g] only: for D_full
+ * to be complete, synchronise every device's stream (or pass `sync` = 1). No counterpart in
+ * the reference (its plan names an NCCL all-gather; this one needs no NCCL). */
+int b2g_allgather_rows(int ngpu, const int* devices, void* const* D, void* const* D_full, int M,
+                       int N, long long ldd, void* const* streams, int sync);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* b2g_last_error(void);
 

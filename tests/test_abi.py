@@ -115,8 +115,8 @@ def test_splitk_argument_validation_without_gpu():
         acc16[11] = b2g.ACC_F16
         assert fn(*acc16, 2, None) == b2g.ERR_UNSUPPORTED    # split-K needs FP32 accumulation
         bad_tile = list(args)
-        bad_tile[14] = 6
-        assert fn(*bad_tile, 0, None) == b2g.ERR_ARG         # tiles are -1 .. 5
+        bad_tile[14] = 7
+        assert fn(*bad_tile, 0, None) == b2g.ERR_ARG         # tiles are -1 .. 6
 
 
 def test_last_launch_before_any_launch():
@@ -136,3 +136,21 @@ def test_last_launch_before_any_launch():
     t.start()
     t.join()
     assert out["rc"] == b2g.ERR_ARG
+
+
+def test_multi_gpu_argument_validation_without_gpu():
+    """b2g_gemm_multi / b2g_allgather_rows reject bad arguments before touching any device."""
+    L = b2g.lib()
+    dev = (C.c_int * 1)(0)
+    ptrs = (C.c_void_p * 1)(None)
+    tail = [64, 64, 64, 64, 64, 64, 0, 0, 0, 1.0, -1, 0, 1, None, 1]
+    assert L.b2g_gemm_multi(0, dev, ptrs, ptrs, ptrs, None, *tail) == b2g.ERR_ARG
+    assert "ngpu" in b2g.last_error()
+    assert L.b2g_gemm_multi(1, None, ptrs, ptrs, ptrs, None, *tail) == b2g.ERR_ARG
+    neg = [-1] + tail[1:]
+    assert L.b2g_gemm_multi(1, dev, ptrs, ptrs, ptrs, None, *neg) == b2g.ERR_ARG
+    assert L.b2g_allgather_rows(0, dev, ptrs, ptrs, 64, 64, 64, None, 1) == b2g.ERR_ARG
+    assert L.b2g_allgather_rows(1, dev, ptrs, None, 64, 64, 64, None, 1) == b2g.ERR_ARG
+    assert L.b2g_allgather_rows(1, dev, ptrs, ptrs, 64, 64, 32, None, 1) == b2g.ERR_ARG
+    assert "ldd" in b2g.last_error()
+
