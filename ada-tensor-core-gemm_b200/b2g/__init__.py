@@ -40,7 +40,7 @@ EXPORTS = (
     "b2g_fill_lcg_f16", "b2g_fill_uniform_f16", "b2g_tile_coord",
     "b2g_selftest_wait_timeout", "b2g_set_wait_timeout_us", "b2g_version",
     "b2g_kernel_clock", "b2g_last_launch", "b2g_gemm_splitk", "b2g_gemm_splitk_noalloc",
-    "b2g_gemm_multi", "b2g_allgather_rows",
+    "b2g_gemm_multi", "b2g_allgather_rows", "b2g_gemm_multi_allgather",
 )
 
 
@@ -113,6 +113,8 @@ def lib():
                                      i, i, vp, i]
         L.b2g_allgather_rows.restype = i
         L.b2g_allgather_rows.argtypes = [i, ip, vp, vp, i, i, ll, vp, i]
+        L.b2g_gemm_multi_allgather.restype = i
+        L.b2g_gemm_multi_allgather.argtypes = L.b2g_gemm_multi.argtypes
         _lib = L
     return _lib
 
@@ -259,6 +261,33 @@ def allgather_rows(D, D_full, *, devices, streams=None, sync: bool = True) -> No
     sp = None if streams is None else _ptr_array([_stream_ptr(s) for s in streams])
     _check(lib().b2g_allgather_rows(ngpu, _devices_array(devices), _ptr_array(D),
                                     _ptr_array(D_full), M, N, ldd, sp, int(sync)))
+
+
+def gemm_multi_allgather(A, B, D_full, bias=None, *, devices, b_layout: int = B_NK,
+                         acc: int = ACC_F32, epilogue: int = EPI_NONE, alpha: float = 1.0,
+                         tile: int = TILE_AUTO, stages: int = 0, group: int = 1, streams=None,
+                         sync: bool = True) -> None:
+    """b2g_gemm_multi_allgather: the M-panel GEMM with the all-gather fused into its epilogue.
+
+    A: per-device panels (rows from :func:`panel_rows`), B: per-device full copies, D_full:
+    one M x N matrix per device, each receiving every device's rows."""
+    ngpu = len(devices)
+    if not (len(A) == len(B) == len(D_full) == ngpu) or (bias is not None and len(bias) != ngpu):
+        raise B2GError(ERR_ARG, "one A panel, B copy, D_full (and bias) per device")
+    M, N = D_full[0].shape
+    K = A[0].shape[1]
+    for g in range(ngpu):
+        r0, r1 = panel_rows(M, ngpu, g)
+        if A[g].shape[0] != r1 - r0 or tuple(D_full[g].shape) != (M, N):
+            raise B2GError(ERR_ARG, f"device {g}: A panel rows {r1 - r0}, D_full {M} x {N}")
+        if (A[g].stride(0), B[g].stride(0), D_full[g].stride(0)) != \
+                (A[0].stride(0), B[0].stride(0), D_full[0].stride(0)):
+            raise B2GError(ERR_ARG, f"device {g}: row pitches differ from device 0")
+    sp = None if streams is None else _ptr_array([_stream_ptr(s) for s in streams])
+    _check(lib().b2g_gemm_multi_allgather(
+        ngpu, _devices_array(devices), _ptr_array(A), _ptr_array(B), _ptr_array(D_full),
+        None if bias is None else _ptr_array(bias), M, N, K, A[0].stride(0), B[0].stride(0),
+        D_full[0].stride(0), b_layout, acc, epilogue, alpha, tile, stages, group, sp, int(sync)))
 
 
 def sync_status(stream=None) -> None:

@@ -212,6 +212,33 @@ inline void panel_rows(int M, int ngpu, int g, int& r0, int& r1) {
     r1 = (int)((long long)M * (g + 1) / ngpu);
 }
 
+// Direct peer access between every pair of distinct devices in the list (NVLink / NVSwitch);
+// already-enabled pairs are fine. `required`: a pair without peer access is an error (kernels
+// store into peer memory), else copies between such a pair go through the host.
+int enable_peers(int ngpu, const int* devices, bool required) {
+    for (int g = 0; g < ngpu; ++g) {
+        if (cudaSetDevice(devices[g]) != cudaSuccess)
+            return fail(B2G_ERR_CUDA, "cudaSetDevice(%d)", devices[g]);
+        for (int h = 0; h < ngpu; ++h) {
+            if (devices[h] == devices[g]) continue;
+            int ok = 0;
+            cudaDeviceCanAccessPeer(&ok, devices[g], devices[h]);
+            if (!ok) {
+                if (required)
+                    return fail(B2G_ERR_UNSUPPORTED, "device %d cannot access device %d's memory",
+                                devices[g], devices[h]);
+                continue;
+            }
+            cudaError_t e = cudaDeviceEnablePeerAccess(devices[h], 0);
+            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+                return fail(B2G_ERR_CUDA, "peer access %d -> %d: %s", devices[g], devices[h],
+                            cudaGetErrorString(e));
+            cudaGetLastError();  // clears cudaErrorPeerAccessAlreadyEnabled
+        }
+    }
+    return B2G_OK;
+}
+
 // Runs fn(g) on one host thread per device (device made current on its thread) and folds
 // the results: the first failure (in device order) becomes the caller's error.
 template <class Fn>
@@ -272,23 +299,7 @@ B2G_EXPORT int b2g_allgather_rows(int ngpu, const int* devices, void* const* D,
     if (ngpu < 1 || !devices || !D || !D_full)
         return fail(B2G_ERR_ARG, "ngpu >= 1 and the devices, D, D_full arrays are required");
     if (M < 0 || N < 0 || ldd < N) return fail(B2G_ERR_ARG, "bad shape M=%d N=%d ldd=%lld", M, N, ldd);
-    // direct peer access between every pair (NVLink / NVSwitch); already-enabled is fine
-    for (int g = 0; g < ngpu; ++g) {
-        if (cudaSetDevice(devices[g]) != cudaSuccess)
-            return fail(B2G_ERR_CUDA, "cudaSetDevice(%d)", devices[g]);
-        for (int h = 0; h < ngpu; ++h) {
-            if (h == g) continue;
-            int ok = 0;
-            cudaDeviceCanAccessPeer(&ok, devices[g], devices[h]);
-            if (ok) {
-                cudaError_t e = cudaDeviceEnablePeerAccess(devices[h], 0);
-                if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
-                    return fail(B2G_ERR_CUDA, "peer access %d -> %d: %s", devices[g], devices[h],
-                                cudaGetErrorString(e));
-                cudaGetLastError();
-            }
-        }
-    }
+    if (int rc = enable_peers(ngpu, devices, false)) return rc;
     return for_each_device(ngpu, devices, [&](int g) -> int {
         int r0, r1;
         panel_rows(M, ngpu, g, r0, r1);
@@ -310,5 +321,37 @@ B2G_EXPORT int b2g_allgather_rows(int ngpu, const int* devices, void* const* D,
                 return fail(B2G_ERR_CUDA, "all-gather synchronize: %s", cudaGetErrorString(e));
         }
         return B2G_OK;
+    });
+}
+
+B2G_EXPORT int b2g_gemm_multi_allgather(int ngpu, const int* devices, const void* const* A,
+                                        const void* const* B, void* const* D_full,
+                                        const void* const* bias, int M, int N, int K,
+                                        long long lda, long long ldb, long long ldd, int b_layout,
+                                        int acc, int epilogue, float alpha, int tile, int stages,
+                                        int group, void* const* streams, int sync) {
+    using namespace b2g;
+    clear_error();
+    if (ngpu < 1 || ngpu > kMaxPeerDst + 1 || !devices || !A || !B || !D_full)
+        return fail(B2G_ERR_ARG, "ngpu in 1..%d and the devices, A, B, D_full arrays are required",
+                    kMaxPeerDst + 1);
+    if (M < 0 || N < 0 || K < 0) return fail(B2G_ERR_ARG, "negative shape M=%d N=%d K=%d", M, N, K);
+    if (ldd < N) return fail(B2G_ERR_ARG, "ldd (%lld) < N (%d)", ldd, N);
+    for (int g = 0; g < ngpu; ++g)
+        if (!D_full[g]) return fail(B2G_ERR_ARG, "D_full[%d] is NULL", g);
+    if (int rc = enable_peers(ngpu, devices, true)) return rc;
+    return for_each_device(ngpu, devices, [&](int g) -> int {
+        int r0, r1;
+        panel_rows(M, ngpu, g, r0, r1);
+        const size_t off = (size_t)r0 * (size_t)ldd * 2;  // this panel's first row, in bytes
+        PeerDst peers;
+        for (int h = 0; h < ngpu; ++h)
+            if (h != g) peers.ptr[peers.n++] = static_cast<char*>(D_full[h]) + off;
+        void* s = streams ? streams[g] : nullptr;
+        int rc = gemm_to_peers(A[g], B[g], static_cast<char*>(D_full[g]) + off,
+                               bias ? bias[g] : nullptr, r1 - r0, N, K, lda, ldb, ldd, b_layout,
+                               acc, epilogue, alpha, tile, stages, group, s, peers);
+        if (rc == B2G_OK && sync) rc = b2g_sync_status(s);
+        return rc;
     });
 }

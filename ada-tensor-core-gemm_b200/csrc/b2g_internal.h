@@ -27,4 +27,19 @@ struct DeviceInfo {
 // Facts about the current device, cached. Returns B2G_OK or an error (with message).
 int current_device(DeviceInfo& out);
 
+// Extra copies of a GEMM's D for a fused all-gather: ptr[i] addresses D's first row in a
+// copy on another device (peer access enabled), with D's ldd.
+constexpr int kMaxPeerDst = 7;
+struct PeerDst {
+    int n = 0;
+    void* ptr[kMaxPeerDst] = {};
+};
+
+// b2g_gemm on the current device whose epilogue also writes every D element into each
+// peers.ptr[i] (requires N % 8 == 0, ldd % 8 == 0, D and the copies 16-byte aligned).
+int gemm_to_peers(const void* A, const void* B, void* D, const void* bias, int M, int N, int K,
+                  long long lda, long long ldb, long long ldd, int b_layout, int acc,
+                  int epilogue, float alpha, int tile, int stages, int group, void* stream,
+                  const PeerDst& peers);
+
 }  // namespace b2g

@@ -89,15 +89,22 @@ TileGeom geom(int tile) {
     }
 }
 
-const void* kernel_ptr(int tile) {
+// `peers`: the fused all-gather instantiation (the swapped-operand kernel has none).
+const void* kernel_ptr(int tile, bool peers = false) {
     switch (tile) {
-        case B2G_TILE_128x128: return (const void*)gemm_sm100_1cta<128>;
-        case B2G_TILE_128x256: return (const void*)gemm_sm100_1cta<256>;
-        case B2G_TILE_128x64: return (const void*)gemm_sm100_1cta<64>;
-        case B2G_TILE_256x512_2SM: return (const void*)gemm_sm100_2cta<512>;
+        case B2G_TILE_128x128:
+            return peers ? (const void*)gemm_sm100_1cta<128, true> : (const void*)gemm_sm100_1cta<128>;
+        case B2G_TILE_128x256:
+            return peers ? (const void*)gemm_sm100_1cta<256, true> : (const void*)gemm_sm100_1cta<256>;
+        case B2G_TILE_128x64:
+            return peers ? (const void*)gemm_sm100_1cta<64, true> : (const void*)gemm_sm100_1cta<64>;
+        case B2G_TILE_256x512_2SM:
+            return peers ? (const void*)gemm_sm100_2cta<512, true> : (const void*)gemm_sm100_2cta<512>;
         case B2G_TILE_SWAP_AB: return (const void*)gemm_sm100_swap<64>;
-        case B2G_TILE_256x128_2SM: return (const void*)gemm_sm100_2cta<128>;
-        default: return (const void*)gemm_sm100_2cta<256>;
+        case B2G_TILE_256x128_2SM:
+            return peers ? (const void*)gemm_sm100_2cta<128, true> : (const void*)gemm_sm100_2cta<128>;
+        default:
+            return peers ? (const void*)gemm_sm100_2cta<256, true> : (const void*)gemm_sm100_2cta<256>;
     }
 }
 
@@ -134,18 +141,18 @@ int max_stages_for(int tile, int smem_optin, int epi_boxes = 8) {
     return s;
 }
 
-int ensure_kernel_attrs(int tile, const DeviceInfo& di) {
-    static bool done[7][kMaxDevices] = {};
+int ensure_kernel_attrs(int tile, const DeviceInfo& di, bool peers = false) {
+    static bool done[2][7][kMaxDevices] = {};
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
-    if (di.device < kMaxDevices && done[tile][di.device]) return B2G_OK;
-    cudaError_t e = cudaFuncSetAttribute(kernel_ptr(tile),
+    if (di.device < kMaxDevices && done[peers][tile][di.device]) return B2G_OK;
+    cudaError_t e = cudaFuncSetAttribute(kernel_ptr(tile, peers),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          di.smem_optin);
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "cudaFuncSetAttribute(tile %d, max dynamic smem %d): %s", tile,
                     di.smem_optin, cudaGetErrorString(e));
-    if (di.device < kMaxDevices) done[tile][di.device] = true;
+    if (di.device < kMaxDevices) done[peers][tile][di.device] = true;
     return B2G_OK;
 }
 
@@ -253,39 +260,47 @@ cudaError_t launch_ex(Kern kern, int grid, int threads, size_t smem, cudaStream_
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
-                const CUtensorMap& tmBt, const CUtensorMap& tmD, const GemmParams& p,
-                const DeviceInfo& di, size_t smem, cudaStream_t s, int epi_warps) {
-    if (int rc = ensure_kernel_attrs(tile, di)) return rc;
-    int grid = 0;
-    const int threads = gemm_threads(epi_warps);
-    cudaError_t e = cudaSuccess;
+template <bool PEERS>
+cudaError_t launch_gemm_t(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                          const CUtensorMap& tmBt, const CUtensorMap& tmD, const GemmParams& p,
+                          const DeviceInfo& di, size_t smem, cudaStream_t s, int threads,
+                          int& grid) {
     switch (tile) {
         case B2G_TILE_128x128:
             grid = std::min(p.num_units, di.sm_count);
-            e = launch_ex(gemm_sm100_1cta<128>, grid, threads, smem, s, tmA, tmB, tmD, p);
-            break;
+            return launch_ex(gemm_sm100_1cta<128, PEERS>, grid, threads, smem, s, tmA, tmB, tmD, p);
         case B2G_TILE_128x256:
             grid = std::min(p.num_units, di.sm_count);
-            e = launch_ex(gemm_sm100_1cta<256>, grid, threads, smem, s, tmA, tmB, tmD, p);
-            break;
+            return launch_ex(gemm_sm100_1cta<256, PEERS>, grid, threads, smem, s, tmA, tmB, tmD, p);
         case B2G_TILE_128x64:
             grid = std::min(p.num_units, di.sm_count);
-            e = launch_ex(gemm_sm100_1cta<64>, grid, threads, smem, s, tmA, tmB, tmD, p);
-            break;
+            return launch_ex(gemm_sm100_1cta<64, PEERS>, grid, threads, smem, s, tmA, tmB, tmD, p);
         case B2G_TILE_256x512_2SM:
             grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
-            e = launch_ex(gemm_sm100_2cta<512>, grid, threads, smem, s, tmA, tmB, tmBt, tmD, p);
-            break;
+            return launch_ex(gemm_sm100_2cta<512, PEERS>, grid, threads, smem, s, tmA, tmB, tmBt,
+                             tmD, p);
         case B2G_TILE_256x128_2SM:
             grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
-            e = launch_ex(gemm_sm100_2cta<128>, grid, threads, smem, s, tmA, tmB, tmBt, tmD, p);
-            break;
+            return launch_ex(gemm_sm100_2cta<128, PEERS>, grid, threads, smem, s, tmA, tmB, tmBt,
+                             tmD, p);
         default:
             grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
-            e = launch_ex(gemm_sm100_2cta<256>, grid, threads, smem, s, tmA, tmB, tmBt, tmD, p);
-            break;
+            return launch_ex(gemm_sm100_2cta<256, PEERS>, grid, threads, smem, s, tmA, tmB, tmBt,
+                             tmD, p);
     }
+}
+
+int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
+                const CUtensorMap& tmBt, const CUtensorMap& tmD, const GemmParams& p,
+                const DeviceInfo& di, size_t smem, cudaStream_t s, int epi_warps) {
+    const bool peers = p.peers.n > 0;
+    if (int rc = ensure_kernel_attrs(tile, di, peers)) return rc;
+    int grid = 0;
+    const int threads = gemm_threads(epi_warps);
+    cudaError_t e = peers ? launch_gemm_t<true>(tile, tmA, tmB, tmBt, tmD, p, di, smem, s,
+                                                threads, grid)
+                          : launch_gemm_t<false>(tile, tmA, tmB, tmBt, tmD, p, di, smem, s,
+                                                 threads, grid);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "GEMM launch (tile %d, grid %d, smem %zu): %s", tile, grid, smem,
@@ -525,7 +540,8 @@ namespace {
 int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, int N, int K,
               long long lda, long long ldb, long long ldd, int b_layout, int acc, int epilogue,
               float alpha, int tile, int stages, int group, int splits, cudaStream_t s,
-              bool noalloc = false) {
+              bool noalloc = false, const PeerDst* peers = nullptr) {
+    static_assert(kMaxPeerDst == kMaxPeers, "peer table sizes");
     if (M < 0 || N < 0 || K < 0)
         return fail(B2G_ERR_ARG, "negative shape M=%d N=%d K=%d", M, N, K);
     if (b_layout != B2G_B_NK && b_layout != B2G_B_KN)
@@ -546,10 +562,25 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         return fail(B2G_ERR_UNSUPPORTED,
                     "split-K sums FP32 partials: it needs FP32 accumulation (acc 0), got acc %d",
                     acc);
+    const int npeer = peers ? peers->n : 0;
+    if (npeer < 0 || npeer > kMaxPeers)
+        return fail(B2G_ERR_ARG, "peer copies of D: 0..%d, got %d", kMaxPeers, npeer);
     if (M == 0 || N == 0) return B2G_OK;
     if (!D) return fail(B2G_ERR_ARG, "D is NULL");
     if (ldd < N) return fail(B2G_ERR_ARG, "ldd (%lld) < N (%d)", ldd, N);
     if (epilogue == B2G_EPI_NONE) bias = nullptr;
+    if (npeer > 0) {
+        if (N % 8 || ldd % 8 || ((uintptr_t)D & 15))
+            return fail(B2G_ERR_ALIGN,
+                        "fused all-gather needs N %% 8 == 0, ldd %% 8 == 0 and a 16-byte "
+                        "aligned D (N=%d, ldd=%lld)", N, ldd);
+        for (int i = 0; i < npeer; ++i)
+            if (!peers->ptr[i] || ((uintptr_t)peers->ptr[i] & 15))
+                return fail(B2G_ERR_ALIGN, "peer copy %d of D is NULL or not 16-byte aligned", i);
+        if (tile == B2G_TILE_SWAP_AB)
+            return fail(B2G_ERR_UNSUPPORTED,
+                        "the swapped-operand kernel (tile 5) has no fused all-gather");
+    }
 
     DeviceInfo di;
     if (int rc = current_device(di)) return rc;
@@ -558,8 +589,9 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
 
     if (K == 0) {  // zero accumulator: only the epilogue remains
         const size_t n = (size_t)M * N;
-        zero_k_fill_kernel<<<elementwise_grid(n, di.sm_count), 256, 0, s>>>(
-            (__half*)D, (const __half*)bias, M, N, ldd, epilogue);
+        for (int i = -1; i < npeer; ++i)
+            zero_k_fill_kernel<<<elementwise_grid(n, di.sm_count), 256, 0, s>>>(
+                (__half*)(i < 0 ? D : peers->ptr[i]), (const __half*)bias, M, N, ldd, epilogue);
         cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? B2G_OK
                                 : fail(B2G_ERR_CUDA, "K == 0 fill launch: %s", cudaGetErrorString(e));
@@ -598,7 +630,7 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         // (measured on B200: 16 x 16384 x 4096 77.8 -> 84.7 TFLOP/s; with N = 4096 its 32
         // CTAs are slower than 128 x 128 tiles with split-K, so it is not used there).
         const long long n_blocks = (N + 127) / 128;
-        if (M <= 32 && b_layout == B2G_B_NK && requested_splits <= 1 &&
+        if (M <= 32 && b_layout == B2G_B_NK && requested_splits <= 1 && npeer == 0 &&
             2 * n_blocks > di.sm_count && 3 * n_blocks >= 2LL * di.sm_count)
             tile = B2G_TILE_SWAP_AB;
     }
@@ -662,6 +694,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     p.D = (__half*)D;
     p.ldd = ldd;
     p.d_tma = (((uintptr_t)D & 15) == 0) && (ldd % 8 == 0);
+    p.peers.n = npeer;
+    for (int i = 0; i < npeer; ++i) p.peers.d[i] = (__half*)peers->ptr[i];
     p.b_mn_major = b_mn ? 1 : 0;
     p.dp_tiles = p.num_tiles;
     p.tail_split = 1;
@@ -683,7 +717,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     if (auto_tile && requested_splits == 0 && splits == 1 && tile == B2G_TILE_128x128 &&
         2LL * p.num_tiles <= di.sm_count)
         return gemm_impl(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc, epilogue, alpha,
-                         B2G_TILE_128x64, stages_arg, group_arg, requested_splits, s, noalloc);
+                         B2G_TILE_128x64, stages_arg, group_arg, requested_splits, s, noalloc,
+                         peers);
     p.splits = splits;
     p.num_units = p.num_tiles * splits;
     if (splits > 1) {
@@ -738,6 +773,16 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
 }
 
 }  // namespace
+}  // namespace b2g
+
+namespace b2g {
+int gemm_to_peers(const void* A, const void* B, void* D, const void* bias, int M, int N, int K,
+                  long long lda, long long ldb, long long ldd, int b_layout, int acc,
+                  int epilogue, float alpha, int tile, int stages, int group, void* stream,
+                  const PeerDst& peers) {
+    return gemm_impl(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc, epilogue, alpha, tile,
+                     stages, group, 0, (cudaStream_t)stream, false, &peers);
+}
 }  // namespace b2g
 
 B2G_EXPORT int b2g_gemm(const void* A, const void* B, void* D, const void* bias, int M, int N,

@@ -20,7 +20,9 @@
 //            --dist LO,HI, --frob ROWS, --json, --splits S, --gpus N, --allgather.
 //   --gpus N  one GEMM split by M-row panels over devices 0..N-1 (b2g_gemm_multi: A and D
 //             by rows, B copied to every device); --allgather then copies every panel to
-//             every device over NVLink (b2g_allgather_rows), timed on its own.
+//             every device over NVLink (b2g_allgather_rows), timed on its own, and then
+//             times the GEMM with the all-gather fused into its epilogue
+//             (b2g_gemm_multi_allgather).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -174,6 +176,7 @@ void usage(const char* argv0) {
            "  --splits S split-K factor (0 automatic, 1 none, S >= 2 forced; default: automatic)\n"
            "  --gpus N   M-row panels over devices 0..N-1 (b2g_gemm_multi), B on every device;\n"
            "             --allgather then gathers D on every device over NVLink (timed apart)\n"
+           "             and times the GEMM with the gather fused into its epilogue\n"
            "  --stages   shared-memory ring depth (0 = deepest that fits)\n"
            "  --group G  L2 rasterization: G M-tiles walked column-major (1 = row-major)\n"
            "  --sweep    stages 2..8 at fixed tile/group;  --gsweep  group 1,2,4,8,16\n"
@@ -307,26 +310,62 @@ int run_multi(const Args& a, const std::vector<uint16_t>& hA, const std::vector<
             CUDA_CHECK(cudaMemcpy(&hD[(size_t)r0 * ldd], dD[g], (size_t)(r1 - r0) * ldd * 2,
                                   cudaMemcpyDeviceToHost));
     }
-    int gather_ok = -1;
-    if (a.allgather) {
-        gather_ok = 1;
-        // whole copies up to 256 MiB, else 257 rows spread through D
+    // every device's D_full must equal the assembled panels: whole copies up to 256 MiB,
+    // else 257 rows spread through D
+    auto full_matches = [&]() -> int {
         const bool whole = nFull * 2 <= (256u << 20);
         std::vector<uint16_t> row((size_t)ldd);
-        for (int g = 0; g < G && gather_ok; ++g) {
+        for (int g = 0; g < G; ++g) {
             CUDA_CHECK(cudaSetDevice(g));
             if (whole) {
                 std::vector<uint16_t> hF(nFull);
                 CUDA_CHECK(cudaMemcpy(hF.data(), dFull[g], nFull * 2, cudaMemcpyDeviceToHost));
-                gather_ok = memcmp(hF.data(), hD.data(), nFull * 2) == 0;
+                if (memcmp(hF.data(), hD.data(), nFull * 2) != 0) return 0;
             } else {
-                for (int r = 0; r <= 256 && gather_ok; ++r) {
+                for (int r = 0; r <= 256; ++r) {
                     const size_t m = (size_t)((long long)r * (a.M - 1) / 256);
                     CUDA_CHECK(cudaMemcpy(row.data(), (const uint16_t*)dFull[g] + m * ldd,
                                           (size_t)ldd * 2, cudaMemcpyDeviceToHost));
-                    gather_ok = memcmp(row.data(), &hD[m * ldd], (size_t)a.N * 2) == 0;
+                    if (memcmp(row.data(), &hD[m * ldd], (size_t)a.N * 2) != 0) return 0;
                 }
             }
+        }
+        return 1;
+    };
+    int gather_ok = -1, fused_ok = -1;
+    double fz_ms = -1, fz_tflops = -1;
+    if (a.allgather) {
+        gather_ok = full_matches();
+        // the same GEMM with the all-gather fused into the epilogue (b2g_gemm_multi_allgather)
+        if (a.N % 8 == 0 && ldd % 8 == 0) {
+            for (int g = 0; g < G; ++g) {  // clear the copies the separate gather wrote
+                CUDA_CHECK(cudaSetDevice(g));
+                CUDA_CHECK(cudaMemset(dFull[g], 0xFF, std::max<size_t>(nFull, 8) * 2));
+            }
+            sync_all();
+            auto fused = [&]() {
+                return b2g_gemm_multi_allgather(
+                    G, devs.data(), (const void* const*)dA.data(), (const void* const*)dB.data(),
+                    dFull.data(), a.fused ? (const void* const*)dBias.data() : nullptr, a.M, a.N,
+                    a.K, lda, ldb, ldd, a.b_layout, a.acc, epi, 1.0f, a.tile, a.stages, a.group,
+                    streams.data(), 0);
+            };
+            for (int i = 0; i < a.warmup; ++i)
+                if (fused() != B2G_OK) {
+                    fprintf(stderr, "error: %s\n", b2g_last_error());
+                    return 1;
+                }
+            fz_ms = timed(a.iters, fused);
+            fz_tflops = flop / (fz_ms * 1e-3) / 1e12;
+            sync_all();
+            for (int g = 0; g < G; ++g) {
+                CUDA_CHECK(cudaSetDevice(g));
+                if (b2g_sync_status(streams[g]) != B2G_OK) {
+                    fprintf(stderr, "error: %s\n", b2g_last_error());
+                    return 1;
+                }
+            }
+            fused_ok = full_matches();
         }
     }
     const bool epi_on = a.fused;
@@ -346,6 +385,9 @@ int run_multi(const Args& a, const std::vector<uint16_t>& hA, const std::vector<
     if (ag_ms >= 0)
         printf("  allgather_ms=%.4f  allgather_GB/s=%.1f  gather=%s", ag_ms, ag_gbs,
                gather_ok ? "OK" : "FAIL");
+    if (fz_ms >= 0)
+        printf("  fused_ms=%.4f  fused_TFLOP/s=%.2f  fused=%s", fz_ms, fz_tflops,
+               fused_ok ? "OK" : "FAIL");
     if (cpurel >= 0)
         printf("  cpu=%.2e%s(worst m=%d n=%d)", cpurel, cpurel < 3e-2 ? " OK " : " FAIL ", wm, wn);
     if (frob >= 0) printf("  frob=%.2e", frob);
@@ -353,10 +395,11 @@ int run_multi(const Args& a, const std::vector<uint16_t>& hA, const std::vector<
     if (a.json)
         printf("{\"M\": %d, \"N\": %d, \"K\": %d, \"gpus\": %d, \"tile\": %d, \"acc\": \"%s\", "
                "\"ms\": %.5f, \"tflops\": %.3f, \"tflops_per_gpu\": %.3f, \"allgather_ms\": %.5f, "
-               "\"allgather_gbs\": %.2f, \"gather_ok\": %d, \"cpu_maxrel\": %.3e, "
+               "\"allgather_gbs\": %.2f, \"gather_ok\": %d, \"fused_ms\": %.5f, "
+               "\"fused_tflops\": %.3f, \"fused_ok\": %d, \"cpu_maxrel\": %.3e, "
                "\"frob_rel\": %.3e}\n",
                a.M, a.N, a.K, G, a.tile, a.acc == B2G_ACC_F32 ? "f32" : "f16", ms, tflops,
-               tflops / G, ag_ms, ag_gbs, gather_ok, cpurel, frob);
+               tflops / G, ag_ms, ag_gbs, gather_ok, fz_ms, fz_tflops, fused_ok, cpurel, frob);
     fflush(stdout);
     for (int g = 0; g < G; ++g) {
         cudaSetDevice(g);
@@ -366,7 +409,8 @@ int run_multi(const Args& a, const std::vector<uint16_t>& hA, const std::vector<
         cudaEventDestroy(t0[g]);
         cudaEventDestroy(t1[g]);
     }
-    return (gather_ok == 0 || (cpurel >= 3e-2) || (frob >= 0 && frob > 1e-2)) ? 1 : 0;
+    return (gather_ok == 0 || fused_ok == 0 || (cpurel >= 3e-2) || (frob >= 0 && frob > 1e-2))
+               ? 1 : 0;
 }
 
 }  // namespace

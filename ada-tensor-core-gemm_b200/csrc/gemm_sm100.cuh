@@ -34,6 +34,13 @@
 
 namespace b2g {
 
+// Most peer copies of D a fused all-gather writes (eight devices: seven peers).
+constexpr int kMaxPeers = 7;
+struct PeerCopies {
+    int n;                     // copies in use (0: no fused all-gather)
+    __half* d[kMaxPeers];      // D's first row in each copy
+};
+
 struct GemmParams {
     int M, N, K;
     int tiles_m, tiles_n, num_tiles, num_kb;
@@ -67,6 +74,10 @@ struct GemmParams {
     // Epilogue staging: boxes of 4 KiB per epilogue warp (1..4), used in turn; the staging
     // area is epilogue warps x epi_bufs x 4 KiB, after the operand ring.
     int epi_bufs;
+    // Fused all-gather: every staged box of D is also written, with 16-byte stores, to the
+    // same rows and columns of npeer other copies of D (same ldd; peer devices' memory over
+    // NVLink). The host guarantees N % 8 == 0, ldd % 8 == 0 and 16-byte aligned copies.
+    PeerCopies peers;
 };
 
 // k-blocks [kb0, kb1) of split s: an even share of the tile's num_kb k-blocks.
@@ -258,13 +269,52 @@ __device__ __forceinline__ void epi_box_store_rows(const GemmParams& p, const Ep
     __syncwarp();  // the box may be refilled
 }
 
+// Fused all-gather: copy a filled staging box (32 rows x 64 columns, 128-byte swizzle) to the
+// same rows and columns of each peer copy of D. Lane l reads 16-byte group (l & 7) of rows
+// (l >> 3) + 4i, i = 0..7, so each store instruction of the warp writes four whole 128-byte
+// row segments. N % 8 == 0, so a group lies wholly inside or outside D. The stores are
+// posted (nothing waits for them here); kernel completion makes them visible. Only the
+// PEERS instantiations of the kernels contain this code.
+template <bool PEERS>
+__device__ __forceinline__ void epi_box_push(const GemmParams& p, const EpiScalars& e,
+                                             uint32_t box, int col, int row0, int lane) {
+    if constexpr (PEERS) {
+        const int npeer = p.peers.n;
+        __syncwarp();  // every lane's part of the box is written
+        const int j = lane & 7, rq = lane >> 3;
+        const int cg = col + j * 8;
+        uint4 v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int r = rq + 4 * i;
+            v[i] = ld_shared_v4(box + (uint32_t)r * 128u +
+                                (((uint32_t)j ^ (uint32_t)(r & 7)) << 4));
+        }
+        const size_t ldd = (size_t)p.ldd;
+        const size_t off = (size_t)(row0 + rq) * ldd + (size_t)cg;
+        const int rows_left = e.M - row0 - rq;  // rows rq + 4i, 4i < rows_left, are inside D
+        if (cg < e.N) {
+#pragma unroll
+            for (int q = 0; q < kMaxPeers; ++q) {  // constant indices into the parameters
+                if (q < npeer) {
+                    __half* dst = p.peers.d[q] + off;
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        if (4 * i < rows_left) st_global_cs_v4(dst + (size_t)(4 * i) * ldd, v[i]);
+                }
+            }
+        }
+        __syncwarp();  // the box may be refilled
+    }
+}
+
 // Chunks c_first, c_first + e.c_step, ... (< nchunks) of 64 columns of this warp's 32 rows:
 // TMEM -> registers 32 columns at a time -> convert -> swizzled staging box -> TMA store
 // (d_tma), or coalesced plain stores of the box's rows. With two or more boxes per warp the
 // chunks go in pairs: both boxes filled, then one generic->async proxy fence for the pair and
 // two TMA stores (the per-chunk fence showed up as the epilogue's top "membar" stall; pairing
 // measured +1.3% at 2048^3, +3% at 16384^2 x 256).
-template <bool ACC16, bool EPI>
+template <bool ACC16, bool EPI, bool PEERS>
 __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiScalars& e,
                                                 const CUtensorMap* tmD, uint32_t trow, int row0,
                                                 int n_first, int nchunks, int c_first,
@@ -297,6 +347,9 @@ __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiSc
                                       n_first + (c + i * e.c_step) * 64, row0, e.store_pol);
                 bulk_commit();
             }
+            for (int i = 0; i < cn; ++i)  // the TMA stores and these read the boxes together
+                epi_box_push<PEERS>(p, e, stage0 + (uint32_t)i * kEpiBoxBytes,
+                                    n_first + (c + i * e.c_step) * 64, row0, lane);
             seq += (uint32_t)cn;
         }
         return;
@@ -318,6 +371,7 @@ __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiSc
             epi_box_store(e, tmD, box, col, row0, lane, seq);
         else
             epi_box_store_rows(p, e, box, col, row0, lane);
+        epi_box_push<PEERS>(p, e, box, col, row0, lane);
     }
 }
 
@@ -326,6 +380,7 @@ __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiSc
 // applied), 64 columns at a time: chunks c_first, c_first + e.c_step, ... (with 8 epilogue
 // warps the other warp of the lane quarter takes the rest). `seq` counts this warp's issued
 // TMA stores.
+template <bool PEERS>
 __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiScalars& e,
                                               const CUtensorMap* tmD, uint32_t trow, int row0,
                                               int n_first, int width, int c_first,
@@ -338,17 +393,17 @@ __device__ __forceinline__ void epilogue_rows(const GemmParams& p, const EpiScal
     if (nchunks <= c_first) return;
     if (acc16) {
         if (epi)
-            epilogue_rows_t<true, true>(p, e, tmD, trow, row0, n_first, nchunks, c_first, stage0,
+            epilogue_rows_t<true, true, PEERS>(p, e, tmD, trow, row0, n_first, nchunks, c_first, stage0,
                                         lane, seq);
         else
-            epilogue_rows_t<true, false>(p, e, tmD, trow, row0, n_first, nchunks, c_first, stage0,
+            epilogue_rows_t<true, false, PEERS>(p, e, tmD, trow, row0, n_first, nchunks, c_first, stage0,
                                          lane, seq);
     } else {
         if (epi)
-            epilogue_rows_t<false, true>(p, e, tmD, trow, row0, n_first, nchunks, c_first, stage0,
+            epilogue_rows_t<false, true, PEERS>(p, e, tmD, trow, row0, n_first, nchunks, c_first, stage0,
                                          lane, seq);
         else
-            epilogue_rows_t<false, false>(p, e, tmD, trow, row0, n_first, nchunks, c_first,
+            epilogue_rows_t<false, false, PEERS>(p, e, tmD, trow, row0, n_first, nchunks, c_first,
                                           stage0, lane, seq);
     }
 }
@@ -425,7 +480,7 @@ __device__ __forceinline__ bool splitk_arrive(unsigned long long* cnt, unsigned 
 // Last split: sum the partials of every split in split order 0..S-1, 16 columns at a time
 // (the loads of four splits in flight together), and hand the sums to the
 // normal epilogue (alpha, bias, ReLU, FP16, TMA store of each 64-column chunk).
-template <bool EPI>
+template <bool EPI, bool PEERS>
 __device__ __forceinline__ void splitk_reduce_t(const GemmParams& p, const EpiScalars& e,
                                                 const CUtensorMap* tmD, int t, int rank,
                                                 int ctas, int q, int bn, int row0, int n_first,
@@ -487,12 +542,13 @@ __device__ __forceinline__ void splitk_reduce_t(const GemmParams& p, const EpiSc
             epi_box_store(e, tmD, box, col, row0, lane, seq);
         else
             epi_box_store_rows(p, e, box, col, row0, lane);
+        epi_box_push<PEERS>(p, e, box, col, row0, lane);
     }
 }
 
 // Split-K epilogue of one warp for one unit: partial out, TMEM released through `release`
 // (called once the accumulator has been read), then the reduction if this split was last.
-template <class Release>
+template <bool PEERS, class Release>
 __device__ __forceinline__ void splitk_epilogue(const GemmParams& p, const EpiScalars& e,
                                                 const CUtensorMap* tmD, uint32_t trow, int t,
                                                 int s, int rank, int ctas, int q, int wslot,
@@ -518,15 +574,16 @@ __device__ __forceinline__ void splitk_epilogue(const GemmParams& p, const EpiSc
     B2G_TIC(t_red);
     B2G_COUNT(15, threadIdx.x == 64 ? 1 : 0);
     if (epi)
-        splitk_reduce_t<true>(p, e, tmD, t, rank, ctas, q, bn, row0, n_first, nchunks, c_first,
+        splitk_reduce_t<true, PEERS>(p, e, tmD, t, rank, ctas, q, bn, row0, n_first, nchunks, c_first,
                               stage0, lane, seq);
     else
-        splitk_reduce_t<false>(p, e, tmD, t, rank, ctas, q, bn, row0, n_first, nchunks, c_first,
+        splitk_reduce_t<false, PEERS>(p, e, tmD, t, rank, ctas, q, bn, row0, n_first, nchunks, c_first,
                                stage0, lane, seq);
     B2G_TOC64(12, t_red);
 }
 
-template <int BN>
+// PEERS: the fused all-gather instantiation (every staged box of D also goes to p.peers).
+template <int BN, bool PEERS = false>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_1cta(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
@@ -734,12 +791,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
             };
             if (p.splits > 1) {
-                splitk_epilogue(p, es, &tmD, tbase, t, u - t * p.splits, 0, 1, q, warp - 2, BN,
+                splitk_epilogue<PEERS>(p, es, &tmD, tbase, t, u - t * p.splits, 0, 1, q, warp - 2, BN,
                                 tm * kBM + q * 32, tn * BN, c_first, stage0, lane, seq, epi,
                                 release);
             } else {
-                epilogue_rows(p, es, &tmD, tbase, tm * kBM + q * 32, tn * BN, BN, c_first, stage0,
-                              lane, seq, acc16, epi);
+                epilogue_rows<PEERS>(p, es, &tmD, tbase, tm * kBM + q * 32, tn * BN, BN, c_first,
+                                     stage0, lane, seq, acc16, epi);
                 release();
             }
             if (warp == 2 && lane == 0) B2G_TOC(4, t_epi);

@@ -96,7 +96,8 @@ __device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& t, in
     n_first = tn * BNP + sub * width;
 }
 
-template <int BNP>
+// PEERS: the fused all-gather instantiation (every staged box of D also goes to p.peers).
+template <int BNP, bool PEERS = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_2cta(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
@@ -379,20 +380,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                 for (int h = 0; h < 2; ++h) {
                     const int hw = width - h * kPairBN;
                     if (hw > 0)
-                        epilogue_rows(p, es, &tmD, tq + (uint32_t)(h * kPairBN), row0,
-                                      n_first + h * kPairBN, hw < kPairBN ? hw : kPairBN, c_first,
-                                      stage0, lane, seq, acc16, epi);
+                        epilogue_rows<PEERS>(p, es, &tmD, tq + (uint32_t)(h * kPairBN), row0,
+                                             n_first + h * kPairBN, hw < kPairBN ? hw : kPairBN,
+                                             c_first, stage0, lane, seq, acc16, epi);
                     release(h);
                 }
             } else {
                 const uint32_t tbase = tq + (uint32_t)(buf * kPairBN);
                 if (p.splits > 1) {
-                    splitk_epilogue(p, es, &tmD, tbase, t, split, (int)rank, 2, q, warp - 2,
-                                    BNP < kPairBN ? BNP : kPairBN, row0, n_first, c_first, stage0,
-                                    lane, seq, epi, [&] { release(buf); });
+                    splitk_epilogue<PEERS>(p, es, &tmD, tbase, t, split, (int)rank, 2, q,
+                                           warp - 2, BNP < kPairBN ? BNP : kPairBN, row0, n_first,
+                                           c_first, stage0, lane, seq, epi,
+                                           [&] { release(buf); });
                 } else {
-                    epilogue_rows(p, es, &tmD, tbase, row0, n_first, width, c_first, stage0, lane,
-                                  seq, acc16, epi);
+                    epilogue_rows<PEERS>(p, es, &tmD, tbase, row0, n_first, width, c_first,
+                                         stage0, lane, seq, acc16, epi);
                     release(buf);
                 }
             }

@@ -338,6 +338,23 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
                  : "memory");
 }
 
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+// 16-byte store with the streaming (evict-first) hint; `ptr` may be a peer device's memory
+// (peer access enabled), in which case the store crosses NVLink.
+__device__ __forceinline__ void st_global_cs_v4(void* ptr, uint4 v) {
+    asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
 // ---------------------------------------------------------------------------------------
 // Tensor memory and tcgen05
 // ---------------------------------------------------------------------------------------

@@ -164,6 +164,22 @@ int b2g_gemm_multi(int ngpu, const int* devices, const void* const* A, const voi
 int b2g_allgather_rows(int ngpu, const int* devices, void* const* D, void* const* D_full, int M,
                        int N, long long ldd, void* const* streams, int sync);
 
+/* b2g_gemm_multi and the all-gather in one kernel per device: device g computes its rows
+ * [M*g/ngpu, M*(g+1)/ngpu) from its A panel A[g] and a full copy of B, B[g], and its epilogue
+ * writes every staged 32 x 64 box of the result both into its own D_full[g] (TMA stores) and,
+ * with 16-byte stores over NVLink, into the same rows of every other device's D_full[h], so
+ * the transfer overlaps the next tile's MMAs. D_full[g] is an M x N matrix (pitch ldd) on
+ * device devices[g]. Needs 1 <= ngpu <= 8, peer access between every pair of devices, N % 8
+ * == 0, ldd % 8 == 0 and 16-byte aligned D_full; tile 5 (swapped operands) is not offered.
+ * With `sync` = 0 D_full[h] is complete once every device's stream has finished (kernel
+ * completion makes the remote stores visible). No counterpart in the reference (its plan
+ * names an NCCL all-gather after the GEMM). */
+int b2g_gemm_multi_allgather(int ngpu, const int* devices, const void* const* A,
+                             const void* const* B, void* const* D_full, const void* const* bias,
+                             int M, int N, int K, long long lda, long long ldb, long long ldd,
+                             int b_layout, int acc, int epilogue, float alpha, int tile,
+                             int stages, int group, void* const* streams, int sync);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* b2g_last_error(void);
 

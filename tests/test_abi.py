@@ -149,6 +149,14 @@ def test_multi_gpu_argument_validation_without_gpu():
     assert L.b2g_gemm_multi(1, None, ptrs, ptrs, ptrs, None, *tail) == b2g.ERR_ARG
     neg = [-1] + tail[1:]
     assert L.b2g_gemm_multi(1, dev, ptrs, ptrs, ptrs, None, *neg) == b2g.ERR_ARG
+    fused = L.b2g_gemm_multi_allgather
+    assert fused(0, dev, ptrs, ptrs, ptrs, None, *tail) == b2g.ERR_ARG
+    devs9 = (C.c_int * 9)(*range(9))
+    ptrs9 = (C.c_void_p * 9)()
+    assert fused(9, devs9, ptrs9, ptrs9, ptrs9, None, *tail) == b2g.ERR_ARG  # 8 devices at most
+    assert fused(1, dev, ptrs, ptrs, ptrs, None, *neg) == b2g.ERR_ARG
+    assert fused(1, dev, ptrs, ptrs, ptrs, None, *tail) == b2g.ERR_ARG      # D_full[0] NULL
+    assert "D_full" in b2g.last_error()
     assert L.b2g_allgather_rows(0, dev, ptrs, ptrs, 64, 64, 64, None, 1) == b2g.ERR_ARG
     assert L.b2g_allgather_rows(1, dev, ptrs, None, 64, 64, 64, None, 1) == b2g.ERR_ARG
     assert L.b2g_allgather_rows(1, dev, ptrs, ptrs, 64, 64, 32, None, 1) == b2g.ERR_ARG

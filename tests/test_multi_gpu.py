@@ -1,5 +1,6 @@
 """GPU tests of the one-process multi-device entry points b2g_gemm_multi (M-row panels, one
-host thread per device) and b2g_allgather_rows (peer-to-peer copies of the D panels).
+host thread per device), b2g_allgather_rows (peer-to-peer copies of the D panels) and
+b2g_gemm_multi_allgather (the all-gather fused into the GEMM epilogue).
 
 On a single-GPU box the "devices" list names device 0 more than once: every panel then runs
 on device 0 from its own host thread and stream, which exercises the panel split, the threads
@@ -129,3 +130,112 @@ def test_cli_gpus_allgather():
     assert out.returncode == 0, out.stdout + out.stderr
     assert "gather=OK" in out.stdout
     assert f"gpus={n}" in out.stdout
+
+
+def _fused(A, B, bias, devices, *, D_pitch=None, **kw):
+    """Run b2g_gemm_multi_allgather; returns the per-device D_full tensors."""
+    M, N = A.shape[0], B.shape[0]
+    dA, dB, dBias, _ = _panels(A, B, bias, devices)
+    ld = D_pitch or N
+    full = [torch.full((M, ld), float("nan"), dtype=torch.float16, device=f"cuda:{d}")[:, :N]
+            for d in devices]
+    b2g.gemm_multi_allgather(dA, dB, full, dBias if kw.get("epilogue") else None,
+                             devices=devices, **kw)
+    return full
+
+
+def _separate(A, B, bias, devices, **kw):
+    """The same product through b2g_gemm_multi (panels stacked on the host)."""
+    dA, dB, dBias, dD = _panels(A, B, bias, devices)
+    b2g.gemm_multi(dA, dB, dD, dBias if kw.get("epilogue") else None, M=A.shape[0],
+                   devices=devices, **kw)
+    return _assemble(dD)
+
+
+@pytest.mark.parametrize("devices", [[0], [0, 0], [0, 0, 0, 0]])
+@pytest.mark.parametrize("M,N,K", [(1024, 512, 512), (1000, 520, 200), (4096, 4096, 256),
+                                   (520, 1024, 4096), (300, 136, 64)])
+def test_fused_allgather_equals_separate(devices, M, N, K):
+    """Every device's D_full from the fused kernel equals the separately computed panels bit
+    for bit (same tiles, same k order), and agrees with the FP64 oracle."""
+    A, B, bias = inputs(M, N, K, seed=M + 2 * N + K)
+    full = _fused(A, B, bias, devices)
+    ref = _separate(A, B, bias, devices)
+    for f in full:
+        assert np.array_equal(to_host(f), ref)
+    frob, _ = check_rows(A, B, ref, sample_rows(M, 32))
+    assert frob <= 1e-3
+
+
+@pytest.mark.parametrize("kw", [dict(epilogue=b2g.EPI_BIAS_RELU, alpha=0.75),
+                                dict(acc=b2g.ACC_F16), dict(tile=b2g.TILE_128x128),
+                                dict(tile=b2g.TILE_256x512_2SM), dict(tile=b2g.TILE_128x64),
+                                dict(tile=b2g.TILE_256x128_2SM), dict(b_layout=b2g.B_KN)])
+def test_fused_allgather_modes(kw):
+    devices = [0, 0]
+    M, N, K = 1536, 1024, 576
+    A, B, bias = inputs(M, N, K, seed=5, lo=-0.5, hi=0.5)
+    if kw.get("b_layout") == b2g.B_KN:
+        Bt = np.ascontiguousarray(B.T)
+        dA, _, _, dD = _panels(A, B, bias, devices)
+        dB = [to_dev(torch, Bt) for _ in devices]
+        full = [torch.empty((M, N), dtype=torch.float16, device="cuda") for _ in devices]
+        b2g.gemm_multi_allgather(dA, dB, full, devices=devices, **kw)
+        b2g.gemm_multi(dA, dB, dD, M=M, devices=devices, **kw)
+        ref = _assemble(dD)
+    else:
+        full = _fused(A, B, bias, devices, **kw)
+        ref = _separate(A, B, bias, devices, **kw)
+    for f in full:
+        assert np.array_equal(to_host(f), ref)
+
+
+def test_fused_allgather_split_k_and_padded_pitch():
+    """Small M per device with long K (split-K, the last split's reduction pushes the boxes)
+    and D_full rows padded to a wider pitch."""
+    devices = [0, 0]
+    M, N, K = 256, 1024, 4096
+    A, B, bias = inputs(M, N, K, seed=9)
+    run(torch, A[:M // 2], B)  # one panel on this thread: the automatic choice splits K
+    assert b2g.last_launch()["splits"] > 1
+    full = _fused(A, B, bias, devices, D_pitch=N + 64)
+    ref = _separate(A, B, bias, devices)
+    for f in full:
+        assert np.array_equal(to_host(f), ref)
+
+
+def test_fused_allgather_k0_and_rejections():
+    devices = [0, 0]
+    M, N = 96, 64
+    A = np.zeros((M, 0), np.uint16)
+    B = np.zeros((N, 0), np.uint16)
+    _, _, bias = inputs(M, N, 8)
+    full = _fused(A, B, bias, devices, epilogue=b2g.EPI_BIAS_RELU)
+    expect = b2g_f16(bias)
+    for f in full:
+        assert np.array_equal(to_host(f), np.broadcast_to(expect, (M, N)))
+    A, B, bias = inputs(64, 60, 64)
+    with pytest.raises(b2g.B2GError) as e:          # N % 8 != 0
+        _fused(A, B, bias, devices)
+    assert e.value.code == b2g.ERR_ALIGN
+    A, B, bias = inputs(64, 64, 64)
+    with pytest.raises(b2g.B2GError) as e:          # the swapped-operand kernel
+        _fused(A, B, bias, devices, tile=b2g.TILE_SWAP_AB)
+    assert e.value.code == b2g.ERR_UNSUPPORTED
+
+
+def b2g_f16(bits):
+    """FP16 bit patterns -> the same bit patterns after max(x, 0) in FP16 (as uint16)."""
+    x = bits.view(np.float16).astype(np.float32)
+    return np.maximum(x, 0).astype(np.float16).view(np.uint16)
+
+
+@pytest.mark.skipif(_ndev() < 2, reason="needs two devices")
+def test_two_devices_fused_allgather():
+    devices = [0, 1]
+    M, N, K = 4096, 2048, 1024
+    A, B, bias = inputs(M, N, K, seed=13)
+    full = _fused(A, B, bias, devices)
+    ref = _separate(A, B, bias, devices)
+    for f in full:
+        assert np.array_equal(to_host(f), ref)
