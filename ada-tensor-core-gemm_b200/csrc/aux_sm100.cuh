@@ -1,11 +1,12 @@
 // aux_sm100.cuh -- small kernels around the GEMM: the device-side max relative difference,
-// the unfused bias+ReLU epilogue, the K == 0 epilogue fill, the HBM stream probe and the
-// bounded-wait self-test. All are bandwidth-bound elementwise kernels with grid-stride
+// the unfused bias+ReLU epilogue, the K == 0 epilogue fill, the HBM stream probe, the
+// all-gather push of D panels to peer devices and the bounded-wait self-test. All are bandwidth-bound elementwise kernels with grid-stride
 // loops over 16-byte (or 2-byte at ragged edges) accesses.
 #pragma once
 
 #include <cuda_fp16.h>
 
+#include "b2g_internal.h"
 #include "sm100_ptx.cuh"
 
 namespace b2g {
@@ -88,6 +89,42 @@ __global__ void __launch_bounds__(512) hbm_copy_kernel(const uint4* __restrict__
 
 // Failure-detection self-test: wait on an mbarrier that nothing arrives at, bounded by
 // `timeout_ns`; the wait records kErrWaitSelftest in the status word and returns.
+// Destinations of one device's all-gather push: its own full D and the peers' (same rows);
+// kMaxGatherDst (8) comes from b2g_internal.h.
+struct GatherDst {
+    int n;
+    __half* d[kMaxGatherDst];
+};
+
+// Copy `rows` x `n8` 16-byte groups of a D panel (pitch ldd elements) to every destination
+// with the same pitch: each group is read once from HBM and stored to all n destinations
+// (peer ones over NVLink), four groups per thread in flight. Blocks stride over rows,
+// threads over a row's groups.
+__global__ void __launch_bounds__(256) allgather_push_kernel(const __half* __restrict__ src,
+                                                             int rows, int n8, long long ldd,
+                                                             GatherDst dst) {
+    const int bs = blockDim.x;
+    for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+        const size_t row = (size_t)r * (size_t)ldd;
+        const uint4* srow = reinterpret_cast<const uint4*>(src + row);
+        for (int c0 = threadIdx.x; c0 < n8; c0 += 4 * bs) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (c0 + u * bs < n8) v[u] = __ldcs(srow + c0 + u * bs);
+#pragma unroll
+            for (int q = 0; q < kMaxGatherDst; ++q) {  // constant indices into the parameters
+                if (q < dst.n) {
+                    uint4* drow = reinterpret_cast<uint4*>(dst.d[q] + row);
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        if (c0 + u * bs < n8) st_global_cs_v4(drow + c0 + u * bs, v[u]);
+                }
+            }
+        }
+    }
+}
+
 __global__ void selftest_wait_kernel(unsigned long long timeout_ns) {
     __shared__ __align__(8) uint64_t bar;
     __shared__ int abort_flag;

@@ -299,21 +299,37 @@ B2G_EXPORT int b2g_allgather_rows(int ngpu, const int* devices, void* const* D,
     if (ngpu < 1 || !devices || !D || !D_full)
         return fail(B2G_ERR_ARG, "ngpu >= 1 and the devices, D, D_full arrays are required");
     if (M < 0 || N < 0 || ldd < N) return fail(B2G_ERR_ARG, "bad shape M=%d N=%d ldd=%lld", M, N, ldd);
-    if (int rc = enable_peers(ngpu, devices, false)) return rc;
+    // SM-driven push (one HBM read, ngpu stores of every 16 bytes) when the rows are 16-byte
+    // groups and every pair of devices has peer access; else copy-engine 2D copies.
+    bool push = ngpu <= kMaxGatherDst && N % 8 == 0 && ldd % 8 == 0;
+    for (int g = 0; g < ngpu && push; ++g)
+        push = !(((uintptr_t)D[g] | (uintptr_t)D_full[g]) & 15);
+    if (push && enable_peers(ngpu, devices, true) != B2G_OK) {
+        clear_error();
+        push = false;
+    }
+    if (!push)
+        if (int rc = enable_peers(ngpu, devices, false)) return rc;
     return for_each_device(ngpu, devices, [&](int g) -> int {
         int r0, r1;
         panel_rows(M, ngpu, g, r0, r1);
         cudaStream_t s = streams ? (cudaStream_t)streams[g] : nullptr;
         const size_t pitch = (size_t)ldd * 2;
-        for (int k = 0; k < ngpu; ++k) {
-            const int h = (g + k) % ngpu;  // start at a different peer on every device
-            if (r1 <= r0) break;
-            cudaError_t e = cudaMemcpy2DAsync(static_cast<char*>(D_full[h]) + (size_t)r0 * pitch,
-                                              pitch, D[g], pitch, (size_t)N * 2,
-                                              (size_t)(r1 - r0), cudaMemcpyDefault, s);
-            if (e != cudaSuccess)
-                return fail(B2G_ERR_CUDA, "panel copy to device %d: %s", devices[h],
-                            cudaGetErrorString(e));
+        if (push) {
+            void* dst[kMaxGatherDst];
+            for (int k = 0; k < ngpu; ++k)  // start at a different peer on every device
+                dst[k] = static_cast<char*>(D_full[(g + k) % ngpu]) + (size_t)r0 * pitch;
+            if (int rc = allgather_push(D[g], r1 - r0, N, ldd, dst, ngpu, s)) return rc;
+        } else {
+            for (int k = 0; k < ngpu && r1 > r0; ++k) {
+                const int h = (g + k) % ngpu;
+                cudaError_t e = cudaMemcpy2DAsync(static_cast<char*>(D_full[h]) + (size_t)r0 * pitch,
+                                                  pitch, D[g], pitch, (size_t)N * 2,
+                                                  (size_t)(r1 - r0), cudaMemcpyDefault, s);
+                if (e != cudaSuccess)
+                    return fail(B2G_ERR_CUDA, "panel copy to device %d: %s", devices[h],
+                                cudaGetErrorString(e));
+            }
         }
         if (sync) {
             cudaError_t e = cudaStreamSynchronize(s);

@@ -42,4 +42,11 @@ int gemm_to_peers(const void* A, const void* B, void* D, const void* bias, int M
                   int epilogue, float alpha, int tile, int stages, int group, void* stream,
                   const PeerDst& peers);
 
+// Copies `rows` x N of a D panel (pitch ldd) into each dst[i] (same pitch) with 16-byte
+// loads and stores on the current device (peer destinations over NVLink). Requires N % 8 ==
+// 0, ldd % 8 == 0 and 16-byte aligned pointers; 1..8 destinations.
+constexpr int kMaxGatherDst = 8;
+int allgather_push(const void* src, int rows, int N, long long ldd, void* const* dst, int ndst,
+                   void* stream);
+
 }  // namespace b2g

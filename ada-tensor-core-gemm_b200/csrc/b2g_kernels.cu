@@ -776,6 +776,24 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
 }  // namespace b2g
 
 namespace b2g {
+int allgather_push(const void* src, int rows, int N, long long ldd, void* const* dst, int ndst,
+                   void* stream) {
+    if (ndst < 1 || ndst > kMaxGatherDst)
+        return fail(B2G_ERR_ARG, "all-gather destinations: 1..%d, got %d", kMaxGatherDst, ndst);
+    if (rows <= 0 || N <= 0) return B2G_OK;
+    GatherDst d{};
+    d.n = ndst;
+    for (int i = 0; i < ndst; ++i) d.d[i] = (__half*)dst[i];
+    DeviceInfo di;
+    if (int rc = current_device(di)) return rc;
+    const int grid = std::min(rows, 4 * di.sm_count);
+    allgather_push_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>((const __half*)src, rows, N / 8,
+                                                                   ldd, d);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? B2G_OK
+                            : fail(B2G_ERR_CUDA, "all-gather push launch: %s", cudaGetErrorString(e));
+}
+
 int gemm_to_peers(const void* A, const void* B, void* D, const void* bias, int M, int N, int K,
                   long long lda, long long ldb, long long ldd, int b_layout, int acc,
                   int epilogue, float alpha, int tile, int stages, int group, void* stream,

@@ -90,9 +90,11 @@ def test_multi_names_the_failing_device():
 
 
 @pytest.mark.parametrize("devices", [[0], [0, 0], [0, 0, 0, 0]])
-def test_allgather_rows(devices):
-    """Every device's gathered copy equals the stacked panels, bit for bit."""
-    M, N, K = 515, 200, 128
+@pytest.mark.parametrize("N", [200, 203])
+def test_allgather_rows(devices, N):
+    """Every device's gathered copy equals the stacked panels, bit for bit (N % 8 == 0: the
+    SM push kernel; else copy-engine 2D copies)."""
+    M, K = 515, 128
     A, B, bias = inputs(M, N, K, seed=3)
     dA, dB, _, dD = _panels(A, B, bias, devices)
     b2g.gemm_multi(dA, dB, dD, M=M, devices=devices)
