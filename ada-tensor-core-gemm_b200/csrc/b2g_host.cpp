@@ -198,8 +198,15 @@ B2G_EXPORT int b2g_cublas_gemm(const void* A, const void* B, void* D, int M, int
 
 // ---------------------------------------------------------------------------------------
 // Multi-GPU: M-row panels from one process (the reference's multi-GPU plan; it has no
-// multi-GPU code of its own). One host thread per device.
+// multi-GPU code of its own). One persistent host thread per device.
 // ---------------------------------------------------------------------------------------
+#include <pthread.h>
+
+#include <atomic>
+#include <condition_variable>
+#include <deque>
+#include <functional>
+#include <memory>
 #include <thread>
 #include <vector>
 
@@ -212,54 +219,176 @@ inline void panel_rows(int M, int ngpu, int g, int& r0, int& r1) {
     r1 = (int)((long long)M * (g + 1) / ngpu);
 }
 
-// Direct peer access between every pair of distinct devices in the list (NVLink / NVSwitch);
-// already-enabled pairs are fine. `required`: a pair without peer access is an error (kernels
-// store into peer memory), else copies between such a pair go through the host.
-int enable_peers(int ngpu, const int* devices, bool required) {
-    for (int g = 0; g < ngpu; ++g) {
-        if (cudaSetDevice(devices[g]) != cudaSuccess)
-            return fail(B2G_ERR_CUDA, "cudaSetDevice(%d)", devices[g]);
+// One persistent host thread per device ordinal, started on first use. A call hands each of
+// its devices' workers a task and waits for all of them: spawning a thread per device per
+// call measured ~250 us for 8 devices on an 8-core host (more than an 8192^3 GEMM's share of
+// one GPU), a hand-off to a waiting thread a few us. Tasks for one device (a device listed
+// twice) run one after the other on its worker. The pool is never destroyed (idle workers end
+// with the process); a forked child starts a fresh, empty pool. A task must not wait for
+// another task.
+class DeviceWorkers {
+  public:
+    static DeviceWorkers& get() {
+        static const bool hooked = [] {
+            pthread_atfork(nullptr, nullptr, [] { current().store(new DeviceWorkers()); });
+            return true;
+        }();
+        (void)hooked;
+        DeviceWorkers* w = current().load();
+        if (!w) {
+            DeviceWorkers* fresh = new DeviceWorkers();
+            if (current().compare_exchange_strong(w, fresh)) return *fresh;
+            delete fresh;  // another thread installed one first
+        }
+        return *w;
+    }
+
+    // Queues `task` on the worker of `device`; false if the worker thread could not start.
+    bool post(int device, std::function<void()> task) {
+        Worker* w = worker(device);
+        if (!w) return false;
+        {
+            std::lock_guard<std::mutex> lock(w->mu);
+            w->q.push_back(std::move(task));
+        }
+        w->cv.notify_one();
+        return true;
+    }
+
+  private:
+    struct Worker {
+        std::mutex mu;
+        std::condition_variable cv;
+        std::deque<std::function<void()>> q;
+    };
+
+    static std::atomic<DeviceWorkers*>& current() {
+        static std::atomic<DeviceWorkers*> p{nullptr};
+        return p;
+    }
+
+    Worker* worker(int device) {
+        std::lock_guard<std::mutex> lock(mu_);
+        if ((int)workers_.size() <= device) workers_.resize((size_t)device + 1);
+        if (!workers_[(size_t)device]) {
+            std::unique_ptr<Worker> w(new Worker());
+            try {
+                std::thread([p = w.get()] { loop(p); }).detach();
+            } catch (...) {
+                return nullptr;
+            }
+            workers_[(size_t)device] = std::move(w);
+        }
+        return workers_[(size_t)device].get();
+    }
+
+    static void loop(Worker* w) {
+        for (;;) {
+            std::function<void()> task;
+            {
+                std::unique_lock<std::mutex> lock(w->mu);
+                w->cv.wait(lock, [w] { return !w->q.empty(); });
+                task = std::move(w->q.front());
+                w->q.pop_front();
+            }
+            task();
+        }
+    }
+
+    std::mutex mu_;
+    std::vector<std::unique_ptr<Worker>> workers_;  // by device ordinal; Workers never move
+};
+
+// Every listed device must be a visible CUDA device.
+int check_devices(int ngpu, const int* devices) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        return fail(B2G_ERR_NO_DEVICE, "no CUDA device: %s",
+                    e != cudaSuccess ? cudaGetErrorString(e) : "count is 0");
+    }
+    for (int g = 0; g < ngpu; ++g)
+        if (devices[g] < 0 || devices[g] >= n)
+            return fail(B2G_ERR_ARG, "devices[%d] = %d: %d device(s) visible", g, devices[g], n);
+    return B2G_OK;
+}
+
+// True if every pair of distinct listed devices has direct peer access (NVLink / NVSwitch).
+bool all_peers_reachable(int ngpu, const int* devices) {
+    for (int g = 0; g < ngpu; ++g)
         for (int h = 0; h < ngpu; ++h) {
             if (devices[h] == devices[g]) continue;
             int ok = 0;
-            cudaDeviceCanAccessPeer(&ok, devices[g], devices[h]);
-            if (!ok) {
-                if (required)
-                    return fail(B2G_ERR_UNSUPPORTED, "device %d cannot access device %d's memory",
-                                devices[g], devices[h]);
-                continue;
-            }
-            cudaError_t e = cudaDeviceEnablePeerAccess(devices[h], 0);
-            if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
-                return fail(B2G_ERR_CUDA, "peer access %d -> %d: %s", devices[g], devices[h],
-                            cudaGetErrorString(e));
-            cudaGetLastError();  // clears cudaErrorPeerAccessAlreadyEnabled
+            if (cudaDeviceCanAccessPeer(&ok, devices[g], devices[h]) != cudaSuccess || !ok)
+                return false;
+        }
+    return true;
+}
+
+// On the current device (a worker's): enable direct access to every other listed device that
+// it can reach; already-enabled pairs are remembered and skipped.
+int enable_peers_from(int self, int ngpu, const int* devices) {
+    static std::mutex mu;
+    static bool on[64][64] = {};
+    for (int h = 0; h < ngpu; ++h) {
+        const int peer = devices[h];
+        if (peer == self) continue;
+        if (self < 64 && peer < 64) {
+            std::lock_guard<std::mutex> lock(mu);
+            if (on[self][peer]) continue;
+        }
+        int ok = 0;
+        if (cudaDeviceCanAccessPeer(&ok, self, peer) != cudaSuccess || !ok) continue;
+        cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+        if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
+            return fail(B2G_ERR_CUDA, "peer access %d -> %d: %s", self, peer, cudaGetErrorString(e));
+        cudaGetLastError();  // clears cudaErrorPeerAccessAlreadyEnabled
+        if (self < 64 && peer < 64) {
+            std::lock_guard<std::mutex> lock(mu);
+            on[self][peer] = true;
         }
     }
     return B2G_OK;
 }
 
-// Runs fn(g) on one host thread per device (device made current on its thread) and folds
-// the results: the first failure (in device order) becomes the caller's error.
+// Runs fn(g) for every listed device on that device's worker (device current) and waits for
+// all of them; the first failure (in list order) becomes the caller's error, naming the device.
+// The caller's own current device is left as it was.
 template <class Fn>
 int for_each_device(int ngpu, const int* devices, Fn fn) {
+    if (int rc = check_devices(ngpu, devices)) return rc;
     std::vector<int> rc((size_t)ngpu, B2G_OK);
     std::vector<std::string> msg((size_t)ngpu);
-    std::vector<std::thread> th;
-    th.reserve((size_t)ngpu);
+    std::mutex mu;
+    std::condition_variable cv;
+    int left = ngpu;
+    auto done = [&] {
+        std::lock_guard<std::mutex> lock(mu);
+        if (--left == 0) cv.notify_all();
+    };
     for (int g = 0; g < ngpu; ++g) {
-        th.emplace_back([&, g] {
+        const bool posted = DeviceWorkers::get().post(devices[g], [&, g] {
             cudaError_t e = cudaSetDevice(devices[g]);
             if (e != cudaSuccess) {
                 rc[(size_t)g] = B2G_ERR_CUDA;
                 msg[(size_t)g] = std::string("cudaSetDevice: ") + cudaGetErrorString(e);
-                return;
+            } else {
+                rc[(size_t)g] = fn(g);
+                if (rc[(size_t)g] != B2G_OK) msg[(size_t)g] = b2g_last_error();
             }
-            rc[(size_t)g] = fn(g);
-            if (rc[(size_t)g] != B2G_OK) msg[(size_t)g] = b2g_last_error();
+            done();
         });
+        if (!posted) {
+            rc[(size_t)g] = B2G_ERR_CUDA;
+            msg[(size_t)g] = "could not start the device's host worker thread";
+            done();
+        }
     }
-    for (auto& t : th) t.join();
+    {
+        std::unique_lock<std::mutex> lock(mu);
+        cv.wait(lock, [&] { return left == 0; });
+    }
     for (int g = 0; g < ngpu; ++g)
         if (rc[(size_t)g] != B2G_OK)
             return b2g::fail(rc[(size_t)g], "device %d (panel %d of %d): %s", devices[g], g, ngpu,
@@ -301,16 +430,13 @@ B2G_EXPORT int b2g_allgather_rows(int ngpu, const int* devices, void* const* D,
     if (M < 0 || N < 0 || ldd < N) return fail(B2G_ERR_ARG, "bad shape M=%d N=%d ldd=%lld", M, N, ldd);
     // SM-driven push (one HBM read, ngpu stores of every 16 bytes) when the rows are 16-byte
     // groups and every pair of devices has peer access; else copy-engine 2D copies.
-    bool push = ngpu <= kMaxGatherDst && N % 8 == 0 && ldd % 8 == 0;
+    if (int rc = check_devices(ngpu, devices)) return rc;
+    bool push = ngpu <= kMaxGatherDst && N % 8 == 0 && ldd % 8 == 0 &&
+                all_peers_reachable(ngpu, devices);
     for (int g = 0; g < ngpu && push; ++g)
         push = !(((uintptr_t)D[g] | (uintptr_t)D_full[g]) & 15);
-    if (push && enable_peers(ngpu, devices, true) != B2G_OK) {
-        clear_error();
-        push = false;
-    }
-    if (!push)
-        if (int rc = enable_peers(ngpu, devices, false)) return rc;
     return for_each_device(ngpu, devices, [&](int g) -> int {
+        if (int rc = enable_peers_from(devices[g], ngpu, devices)) return rc;
         int r0, r1;
         panel_rows(M, ngpu, g, r0, r1);
         cudaStream_t s = streams ? (cudaStream_t)streams[g] : nullptr;
@@ -355,8 +481,12 @@ B2G_EXPORT int b2g_gemm_multi_allgather(int ngpu, const int* devices, const void
     if (ldd < N) return fail(B2G_ERR_ARG, "ldd (%lld) < N (%d)", ldd, N);
     for (int g = 0; g < ngpu; ++g)
         if (!D_full[g]) return fail(B2G_ERR_ARG, "D_full[%d] is NULL", g);
-    if (int rc = enable_peers(ngpu, devices, true)) return rc;
+    if (int rc = check_devices(ngpu, devices)) return rc;
+    if (!all_peers_reachable(ngpu, devices))
+        return fail(B2G_ERR_UNSUPPORTED,
+                    "the fused all-gather needs direct peer access between every pair of devices");
     return for_each_device(ngpu, devices, [&](int g) -> int {
+        if (int rc = enable_peers_from(devices[g], ngpu, devices)) return rc;
         int r0, r1;
         panel_rows(M, ngpu, g, r0, r1);
         const size_t off = (size_t)r0 * (size_t)ldd * 2;  // this panel's first row, in bytes

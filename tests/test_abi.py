@@ -7,7 +7,6 @@ import re
 import subprocess
 
 import numpy as np
-import pytest
 
 import b2g
 import oracle as O
@@ -162,3 +161,16 @@ def test_multi_gpu_argument_validation_without_gpu():
     assert L.b2g_allgather_rows(1, dev, ptrs, ptrs, 64, 64, 32, None, 1) == b2g.ERR_ARG
     assert "ldd" in b2g.last_error()
 
+
+
+def test_multi_gpu_without_a_device():
+    """With well-formed arguments the multi-device entry points ask the runtime for devices
+    first; here (no GPU) that is B2G_ERR_NO_DEVICE, returned without starting any work."""
+    L = b2g.lib()
+    dev = (C.c_int * 1)(0)
+    fake = (C.c_void_p * 1)(0x1000)
+    tail = [64, 64, 64, 64, 64, 64, 0, 0, 0, 1.0, -1, 0, 1, None, 1]
+    assert L.b2g_gemm_multi(1, dev, fake, fake, fake, None, *tail) == b2g.ERR_NO_DEVICE
+    assert L.b2g_gemm_multi_allgather(1, dev, fake, fake, fake, None, *tail) == b2g.ERR_NO_DEVICE
+    assert L.b2g_allgather_rows(1, dev, fake, fake, 64, 64, 64, None, 1) == b2g.ERR_NO_DEVICE
+    assert "no CUDA device" in b2g.last_error()
