@@ -40,7 +40,8 @@ EXPORTS = (
     "b2g_fill_lcg_f16", "b2g_fill_uniform_f16", "b2g_tile_coord",
     "b2g_selftest_wait_timeout", "b2g_set_wait_timeout_us", "b2g_version",
     "b2g_kernel_clock", "b2g_last_launch", "b2g_gemm_splitk", "b2g_gemm_splitk_noalloc",
-    "b2g_gemm_multi", "b2g_allgather_rows", "b2g_gemm_multi_allgather",
+    "b2g_gemm_multi", "b2g_allgather_rows", "b2g_gemm_multi_allgather", "b2g_gemm_peers",
+    "b2g_ipc_handle", "b2g_ipc_open", "b2g_ipc_close",
 )
 
 
@@ -115,6 +116,15 @@ def lib():
         L.b2g_allgather_rows.argtypes = [i, ip, vp, vp, i, i, ll, vp, i]
         L.b2g_gemm_multi_allgather.restype = i
         L.b2g_gemm_multi_allgather.argtypes = L.b2g_gemm_multi.argtypes
+        L.b2g_gemm_peers.restype = i
+        L.b2g_gemm_peers.argtypes = [vp, vp, vp, vp, i, i, i, ll, ll, ll, i, i, i, f, i, i, i,
+                                     vp, i, vp]
+        L.b2g_ipc_handle.restype = i
+        L.b2g_ipc_handle.argtypes = [vp, vp, C.POINTER(C.c_ulonglong)]
+        L.b2g_ipc_open.restype = i
+        L.b2g_ipc_open.argtypes = [vp, C.POINTER(vp)]
+        L.b2g_ipc_close.restype = i
+        L.b2g_ipc_close.argtypes = [vp]
         _lib = L
     return _lib
 
@@ -288,6 +298,41 @@ def gemm_multi_allgather(A, B, D_full, bias=None, *, devices, b_layout: int = B_
         ngpu, _devices_array(devices), _ptr_array(A), _ptr_array(B), _ptr_array(D_full),
         None if bias is None else _ptr_array(bias), M, N, K, A[0].stride(0), B[0].stride(0),
         D_full[0].stride(0), b_layout, acc, epilogue, alpha, tile, stages, group, sp, int(sync)))
+
+
+def gemm_peers(A, B, D, peers, bias=None, *, b_layout: int = B_NK, acc: int = ACC_F32,
+               epilogue: int = EPI_NONE, alpha: float = 1.0, tile: int = TILE_AUTO,
+               stages: int = 0, group: int = 1, stream=None) -> None:
+    """b2g_gemm_peers: D = A * B on this device, every element of D also stored into each of
+    ``peers`` (raw device addresses of D's first row in other copies with D's row pitch,
+    e.g. from :func:`ipc_open`)."""
+    M, K = A.shape
+    N = B.shape[0] if b_layout == B_NK else B.shape[1]
+    if tuple(D.shape) != (M, N):
+        raise B2GError(ERR_ARG, f"D shape {tuple(D.shape)} != ({M}, {N})")
+    arr = (C.c_void_p * max(1, len(peers)))(*peers)
+    _check(lib().b2g_gemm_peers(_ptr(A), _ptr(B), _ptr(D), _ptr(bias), M, N, K, A.stride(0),
+                                B.stride(0), D.stride(0), b_layout, acc, epilogue, alpha, tile,
+                                stages, group, arr, len(peers), _stream_ptr(stream)))
+
+
+def ipc_handle(t) -> tuple[bytes, int]:
+    """(64-byte CUDA IPC handle of the allocation holding tensor/pointer t, t's byte offset)."""
+    h = C.create_string_buffer(64)
+    off = C.c_ulonglong()
+    _check(lib().b2g_ipc_handle(_ptr(t), h, C.byref(off)))
+    return h.raw, off.value
+
+
+def ipc_open(handle: bytes) -> int:
+    """Map another process's allocation; returns its base address in this process."""
+    base = C.c_void_p()
+    _check(lib().b2g_ipc_open(C.create_string_buffer(handle, 64), C.byref(base)))
+    return base.value
+
+
+def ipc_close(base: int) -> None:
+    _check(lib().b2g_ipc_close(base))
 
 
 def sync_status(stream=None) -> None:

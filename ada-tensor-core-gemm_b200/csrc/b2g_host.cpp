@@ -1,6 +1,9 @@
 // b2g_host.cpp -- host-only part of libb200gemm.so: error reporting, device facts, the
-// cuBLAS comparison column, the host input generators and the tile-scheduler mapping.
+// cuBLAS comparison column, the host input generators, the tile-scheduler mapping, the
+// multi-GPU entry points and CUDA IPC sharing of D buffers between processes.
 #include <cublas_v2.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <omp.h>
 
@@ -500,4 +503,79 @@ B2G_EXPORT int b2g_gemm_multi_allgather(int ngpu, const int* devices, const void
         if (rc == B2G_OK && sync) rc = b2g_sync_status(s);
         return rc;
     });
+}
+
+B2G_EXPORT int b2g_gemm_peers(const void* A, const void* B, void* D, const void* bias, int M,
+                              int N, int K, long long lda, long long ldb, long long ldd,
+                              int b_layout, int acc, int epilogue, float alpha, int tile,
+                              int stages, int group, const void* const* peer_D, int npeer,
+                              void* stream) {
+    using namespace b2g;
+    clear_error();
+    if (npeer < 0 || npeer > kMaxPeerDst)
+        return fail(B2G_ERR_ARG, "npeer must be 0..%d, got %d", kMaxPeerDst, npeer);
+    if (npeer > 0 && !peer_D) return fail(B2G_ERR_ARG, "peer_D is NULL with npeer = %d", npeer);
+    PeerDst peers;
+    peers.n = npeer;
+    for (int i = 0; i < npeer; ++i) peers.ptr[i] = const_cast<void*>(peer_D[i]);
+    return gemm_to_peers(A, B, D, bias, M, N, K, lda, ldb, ldd, b_layout, acc, epilogue, alpha,
+                         tile, stages, group, stream, peers);
+}
+
+// ---------------------------------------------------------------------------------------
+// CUDA IPC: one process per GPU shares its D buffer with the others (fused all-gather).
+// ---------------------------------------------------------------------------------------
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+
+B2G_EXPORT int b2g_ipc_handle(const void* ptr, void* handle, unsigned long long* offset) {
+    using namespace b2g;
+    clear_error();
+    if (!ptr || !handle || !offset) return fail(B2G_ERR_ARG, "ptr, handle and offset are required");
+    static PFN_cuMemGetAddressRange_v3020 range = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            range = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+    });
+    if (!range) return fail(B2G_ERR_CUDA, "cuMemGetAddressRange is not available from the driver");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    CUresult r = range(&base, &size, (CUdeviceptr)(uintptr_t)ptr);
+    if (r != CUDA_SUCCESS)
+        return fail(B2G_ERR_ARG, "pointer %p is not device memory (cuMemGetAddressRange: %d)",
+                    ptr, (int)r);
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, (void*)(uintptr_t)base);
+    if (e != cudaSuccess)
+        return fail(B2G_ERR_CUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+    memcpy(handle, &h, sizeof h);
+    *offset = (unsigned long long)((uintptr_t)ptr - (uintptr_t)base);
+    return B2G_OK;
+}
+
+B2G_EXPORT int b2g_ipc_open(const void* handle, void** base) {
+    using namespace b2g;
+    clear_error();
+    if (!handle || !base) return fail(B2G_ERR_ARG, "handle and base are required");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    cudaError_t e = cudaIpcOpenMemHandle(base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        *base = nullptr;
+        return fail(B2G_ERR_CUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+    }
+    return B2G_OK;
+}
+
+B2G_EXPORT int b2g_ipc_close(void* base) {
+    using namespace b2g;
+    clear_error();
+    if (!base) return fail(B2G_ERR_ARG, "base is NULL");
+    cudaError_t e = cudaIpcCloseMemHandle(base);
+    return e == cudaSuccess ? B2G_OK
+                            : fail(B2G_ERR_CUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
 }

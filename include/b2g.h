@@ -180,6 +180,27 @@ int b2g_gemm_multi_allgather(int ngpu, const int* devices, const void* const* A,
                              int b_layout, int acc, int epilogue, float alpha, int tile,
                              int stages, int group, void* const* streams, int sync);
 
+/* b2g_gemm on the current device whose epilogue also writes every element of D into each of
+ * npeer (0..7) other copies of D: peer_D[i] addresses D's first row in a copy with the same
+ * ldd, normally another device's memory (peer access enabled, or a CUDA IPC mapping from
+ * b2g_ipc_open), reached with 16-byte stores over NVLink. The building block of the fused
+ * all-gather for callers with one process per GPU: rank r passes its M-row panel of A and, as
+ * D and peer_D, its rows in its own and every other rank's full D. Needs N % 8 == 0, ldd % 8
+ * == 0 and 16-byte aligned D and copies; tile 5 is not offered. The copies are complete when
+ * this launch has finished. No counterpart in the reference. */
+int b2g_gemm_peers(const void* A, const void* B, void* D, const void* bias, int M, int N, int K,
+                   long long lda, long long ldb, long long ldd, int b_layout, int acc,
+                   int epilogue, float alpha, int tile, int stages, int group,
+                   const void* const* peer_D, int npeer, void* stream);
+
+/* CUDA IPC for the fused all-gather across processes. b2g_ipc_handle writes the 64-byte IPC
+ * handle of the device allocation containing `ptr` and ptr's byte offset inside it;
+ * another process maps that allocation with b2g_ipc_open (*base = its address there; add the
+ * offset) and unmaps it with b2g_ipc_close(base). A process cannot open its own handles. */
+int b2g_ipc_handle(const void* ptr, void* handle, unsigned long long* offset);
+int b2g_ipc_open(const void* handle, void** base);
+int b2g_ipc_close(void* base);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* b2g_last_error(void);
 

@@ -174,3 +174,17 @@ def test_multi_gpu_without_a_device():
     assert L.b2g_gemm_multi_allgather(1, dev, fake, fake, fake, None, *tail) == b2g.ERR_NO_DEVICE
     assert L.b2g_allgather_rows(1, dev, fake, fake, 64, 64, 64, None, 1) == b2g.ERR_NO_DEVICE
     assert "no CUDA device" in b2g.last_error()
+
+
+def test_peers_and_ipc_argument_validation_without_gpu():
+    L = b2g.lib()
+    args = [None, None, None, None, 64, 64, 64, 64, 64, 64, 0, 0, 0, 1.0, -1, 0, 1]
+    assert L.b2g_gemm_peers(*args, None, -1, None) == b2g.ERR_ARG
+    assert L.b2g_gemm_peers(*args, None, 8, None) == b2g.ERR_ARG       # 7 copies at most
+    assert L.b2g_gemm_peers(*args, None, 2, None) == b2g.ERR_ARG       # peer_D NULL
+    off = C.c_ulonglong()
+    buf = C.create_string_buffer(64)
+    assert L.b2g_ipc_handle(None, buf, C.byref(off)) == b2g.ERR_ARG
+    base = C.c_void_p()
+    assert L.b2g_ipc_open(None, C.byref(base)) == b2g.ERR_ARG
+    assert L.b2g_ipc_close(None) == b2g.ERR_ARG
