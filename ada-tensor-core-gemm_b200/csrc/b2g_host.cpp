@@ -330,27 +330,19 @@ bool all_peers_reachable(int ngpu, const int* devices) {
 }
 
 // On the current device (a worker's): enable direct access to every other listed device that
-// it can reach; already-enabled pairs are remembered and skipped.
+// it can reach. Asked on every call rather than remembered, so that access the application
+// disabled in between is back before a kernel stores into a peer (an already-enabled pair
+// costs one quick runtime call).
 int enable_peers_from(int self, int ngpu, const int* devices) {
-    static std::mutex mu;
-    static bool on[64][64] = {};
     for (int h = 0; h < ngpu; ++h) {
         const int peer = devices[h];
         if (peer == self) continue;
-        if (self < 64 && peer < 64) {
-            std::lock_guard<std::mutex> lock(mu);
-            if (on[self][peer]) continue;
-        }
         int ok = 0;
         if (cudaDeviceCanAccessPeer(&ok, self, peer) != cudaSuccess || !ok) continue;
         cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
         if (e != cudaSuccess && e != cudaErrorPeerAccessAlreadyEnabled)
             return fail(B2G_ERR_CUDA, "peer access %d -> %d: %s", self, peer, cudaGetErrorString(e));
         cudaGetLastError();  // clears cudaErrorPeerAccessAlreadyEnabled
-        if (self < 64 && peer < 64) {
-            std::lock_guard<std::mutex> lock(mu);
-            on[self][peer] = true;
-        }
     }
     return B2G_OK;
 }

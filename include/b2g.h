@@ -196,7 +196,8 @@ int b2g_gemm_peers(const void* A, const void* B, void* D, const void* bias, int 
 /* CUDA IPC for the fused all-gather across processes. b2g_ipc_handle writes the 64-byte IPC
  * handle of the device allocation containing `ptr` and ptr's byte offset inside it;
  * another process maps that allocation with b2g_ipc_open (*base = its address there; add the
- * offset) and unmaps it with b2g_ipc_close(base). A process cannot open its own handles. */
+ * offset) and unmaps it with b2g_ipc_close(base). The allocation must come from cudaMalloc
+ * (PyTorch's default caching allocator uses it); a process cannot open its own handles. */
 int b2g_ipc_handle(const void* ptr, void* handle, unsigned long long* offset);
 int b2g_ipc_open(const void* handle, void** base);
 int b2g_ipc_close(void* base);
