@@ -7,6 +7,7 @@ import re
 import subprocess
 
 import numpy as np
+import pytest
 
 import b2g
 import oracle as O
@@ -188,3 +189,36 @@ def test_peers_and_ipc_argument_validation_without_gpu():
     base = C.c_void_p()
     assert L.b2g_ipc_open(None, C.byref(base)) == b2g.ERR_ARG
     assert L.b2g_ipc_close(None) == b2g.ERR_ARG
+
+
+def test_multi_gpu_python_wrappers_validate_on_the_host():
+    """The Python wrappers check panel shapes and pitches before calling the library; with
+    consistent CPU tensors the call reaches the library, which finds no device here."""
+    import torch
+
+    M, N, K = 10, 16, 8
+    devs = [0, 0]
+    A = [torch.zeros(5, K, dtype=torch.float16), torch.zeros(5, K, dtype=torch.float16)]
+    B = [torch.zeros(N, K, dtype=torch.float16)] * 2
+    D = [torch.zeros(5, N, dtype=torch.float16), torch.zeros(5, N, dtype=torch.float16)]
+    full = [torch.zeros(M, N, dtype=torch.float16)] * 2
+    with pytest.raises(b2g.B2GError, match="panel rows"):
+        b2g.gemm_multi([A[0], torch.zeros(4, K, dtype=torch.float16)], B, D, M=M, devices=devs)
+    with pytest.raises(b2g.B2GError, match="per device"):
+        b2g.gemm_multi(A[:1], B, D, M=M, devices=devs)
+    with pytest.raises(b2g.B2GError, match="pitches"):
+        wide = torch.zeros(5, K + 8, dtype=torch.float16)[:, :K]
+        b2g.gemm_multi([A[0], wide], B, D, M=M, devices=devs)
+    with pytest.raises(b2g.B2GError) as e:
+        b2g.gemm_multi(A, B, D, M=M, devices=devs)
+    assert e.value.code == b2g.ERR_NO_DEVICE
+    with pytest.raises(b2g.B2GError, match="A panel rows"):
+        b2g.gemm_multi_allgather([A[0], A[0][:4]], B, full, devices=devs)
+    with pytest.raises(b2g.B2GError) as e:
+        b2g.gemm_multi_allgather(A, B, full, devices=devs)
+    assert e.value.code == b2g.ERR_NO_DEVICE
+    with pytest.raises(b2g.B2GError, match="one row pitch"):
+        b2g.allgather_rows([torch.zeros(5, N + 8, dtype=torch.float16)[:, :N], D[1]], full,
+                           devices=devs)
+    with pytest.raises(b2g.B2GError, match="D shape"):
+        b2g.gemm_peers(A[0], B[0], D[0][:4], [])
