@@ -41,7 +41,7 @@ EXPORTS = (
     "b2g_selftest_wait_timeout", "b2g_set_wait_timeout_us", "b2g_version",
     "b2g_kernel_clock", "b2g_last_launch", "b2g_gemm_splitk", "b2g_gemm_splitk_noalloc",
     "b2g_gemm_multi", "b2g_allgather_rows", "b2g_gemm_multi_allgather", "b2g_gemm_peers",
-    "b2g_ipc_handle", "b2g_ipc_open", "b2g_ipc_close",
+    "b2g_ipc_handle", "b2g_ipc_open", "b2g_ipc_close", "b2g_last_launch_cluster",
 )
 
 
@@ -109,6 +109,8 @@ def lib():
         L.b2g_kernel_clock.argtypes = [C.POINTER(d), C.POINTER(d)]
         L.b2g_last_launch.restype = i
         L.b2g_last_launch.argtypes = [ip, ip, ip, ip, ip, ip]
+        L.b2g_last_launch_cluster.restype = i
+        L.b2g_last_launch_cluster.argtypes = [ip]
         L.b2g_gemm_multi.restype = i
         L.b2g_gemm_multi.argtypes = [i, ip, vp, vp, vp, vp, i, i, i, ll, ll, ll, i, i, i, f, i,
                                      i, i, vp, i]
@@ -353,7 +355,11 @@ def last_launch() -> dict:
     vals = [C.c_int() for _ in range(6)]
     _check(lib().b2g_last_launch(*[C.byref(v) for v in vals]))
     keys = ("grid", "threads", "tile", "stages", "units", "splits")
-    return {k: v.value for k, v in zip(keys, vals)}
+    out = {k: v.value for k, v in zip(keys, vals)}
+    cl = C.c_int()
+    _check(lib().b2g_last_launch_cluster(C.byref(cl)))
+    out["cluster"] = cl.value  # CTAs per thread-block cluster (split-K clusters: the splits)
+    return out
 
 
 def cublas_gemm(A, B, D, stream=None) -> None:

@@ -35,11 +35,25 @@ _QUERY = ("clocks.sm,clocks.mem,power.draw,temperature.gpu,utilization.gpu,"
 _REASONS = ("swPowerCap", "hwSlowdown", "hwThermal", "swThermal", "hwPowerBrake")
 
 
-def sample(index: int = 0):
-    """One telemetry sample (values in TELEMETRY_COLUMNS order after `t`), or None."""
+def device_uuid(cuda_index: int):
+    """UUID ("GPU-...") of CUDA device `cuda_index` of this process's visible devices, or
+    None. nvidia-smi numbers GPUs its own way (PCI order), which need not be CUDA's order
+    (CUDA_DEVICE_ORDER, CUDA_VISIBLE_DEVICES), so the soaked GPU is named by its UUID."""
+    try:
+        import torch
+
+        u = str(torch.cuda.get_device_properties(cuda_index).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:  # noqa: BLE001 -- no torch / no device
+        return None
+
+
+def sample(ident="0"):
+    """One telemetry sample (values in TELEMETRY_COLUMNS order after `t`) of the GPU that
+    nvidia-smi's -i names `ident` (a UUID, or an nvidia-smi index), or None."""
     try:
         out = subprocess.run(["nvidia-smi", f"--query-gpu={_QUERY}",
-                              "--format=csv,noheader,nounits", "-i", str(index)],
+                              "--format=csv,noheader,nounits", "-i", str(ident)],
                              capture_output=True, text=True, timeout=20)
         f = [v.strip() for v in out.stdout.strip().splitlines()[0].split(",")]
         if out.returncode != 0 or len(f) != 10:
@@ -110,13 +124,19 @@ def run(seconds, window, M, N, K, tile, stages, layout, group, acc, tag, out_dir
     args = [exe, "--m", str(M), "--n", str(N), "--k", str(K), "--tile", str(tile), "--stages",
             str(stages), "--layout", str(layout), "--group", str(group), "--acc", acc, "--noref",
             "--warmup", "20", "--soak", str(seconds), "--window", str(window)]
-    log(f"soaking {seconds} s: {' '.join(args)}")
+    # the CLI runs on its CUDA device 0: make that the soaked GPU, and sample the same GPU
+    uuid = device_uuid(gpu)
+    env = dict(os.environ)
+    if uuid:
+        env["CUDA_VISIBLE_DEVICES"] = uuid
+    ident = uuid or str(gpu)
+    log(f"soaking {seconds} s on {ident}: {' '.join(args)}")
     t0 = time.monotonic()
     samples = []
     with open(stdout_path, "w") as fh:
-        proc = subprocess.Popen(args, stdout=fh, stderr=subprocess.STDOUT)
+        proc = subprocess.Popen(args, stdout=fh, stderr=subprocess.STDOUT, env=env)
         while proc.poll() is None:
-            s = sample(gpu)
+            s = sample(ident)
             if s is not None:
                 samples.append({"t": round(time.monotonic() - t0, 2), **s})
             time.sleep(sample_ms / 1000.0)
@@ -151,7 +171,8 @@ def main(argv=None):
     p.add_argument("--out-dir", default="data")
     p.add_argument("--sample-ms", type=int, default=250)
     p.add_argument("--exe", default=DEFAULT_EXE)
-    p.add_argument("--gpu", type=int, default=0)
+    p.add_argument("--gpu", type=int, default=0,
+                   help="CUDA ordinal (of the visible devices) to soak and sample")
     a = p.parse_args(argv)
     s = run(a.seconds, a.window, a.m, a.n, a.k, a.tile, a.stages, a.layout, a.group, a.acc,
             a.tag, a.out_dir, a.sample_ms, a.exe, a.gpu)

@@ -46,7 +46,9 @@ __global__ void __launch_bounds__(256) bias_relu_kernel(__half* D, const __half*
         const size_t m = i / (size_t)N, n = i - m * (size_t)N;
         __half* d = D + m * (size_t)ldd + n;
         float v = __half2float(*d);
-        v = bias ? fmaf(v, alpha, __half2float(bias[n])) : v * alpha;
+        // multiply, then add (two roundings), as src/gemm_bench.cu:405-406 compiles
+        v = __fmul_rn(v, alpha);
+        if (bias) v = __fadd_rn(v, __half2float(bias[n]));
         *d = __float2half_rn(v > 0.f ? v : 0.f);
     }
 }

@@ -14,6 +14,7 @@
 #include <cstdlib>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 #include "b2g.h"
@@ -63,6 +64,40 @@ int make_tmap(CUtensorMap* tm, const void* ptr, uint64_t inner, uint64_t outer, 
                     what, (unsigned long long)outer, (unsigned long long)inner,
                     (unsigned long long)ld, (int)r);
     return B2G_OK;
+}
+
+// B stored K x N as a 3D tensor: (64 columns, K rows, N / 64 column groups), strides ldb * 2
+// bytes between rows and 128 bytes between groups, read in boxes of 64 columns x 64 k-rows x
+// `groups` groups. TMA writes a box group after group, each group 64 rows of 128 bytes with
+// 128-byte swizzle: exactly the MN-major operand layout of `groups` separate 2D boxes placed
+// back to back, in one load. N must be a multiple of 64 so the groups tile N exactly (no load
+// reads past the end of a row); groups past N / 64 read as zeros.
+int make_tmap_kn3d(CUtensorMap* tm, const void* ptr, uint64_t N, uint64_t K, uint64_t ldb,
+                   uint32_t groups) {
+    auto enc = encode_fn();
+    if (!enc) return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[3] = {64, K, N / 64};
+    const cuuint64_t strides[2] = {ldb * 2, 128};
+    const cuuint32_t box[3] = {64, (cuuint32_t)kBK, groups};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled(B K x N in 3D, %llu x %llu, %u groups): %d",
+                    (unsigned long long)K, (unsigned long long)N, groups, (int)r);
+    return B2G_OK;
+}
+
+// One 3D load per stage for B stored K x N (default; B2G_KN3D=0 in the environment, read
+// once per process, keeps the per-64-column 2D loads).
+bool kn3d_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("B2G_KN3D");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -238,26 +273,91 @@ int epi_warps_for(int num_kb, int splits, bool wide) {
     return (num_kb <= 16 || splits > 1 || wide) ? 8 : 4;
 }
 
-// The most recent GEMM launch of this host thread (b2g_last_launch).
+// The most recent GEMM launch of this host thread (b2g_last_launch, b2g_last_launch_cluster).
 struct LaunchRecord {
-    int grid, threads, tile, stages, units, splits;
+    int grid, threads, tile, stages, units, splits, cluster;
 };
 thread_local LaunchRecord g_last_launch = {};
 
+// Launch with programmatic dependent launch (when enabled) and, for cluster > 1, a runtime
+// cluster shape of `cluster` CTAs along x (kernels without __cluster_dims__).
 template <class Kern, class... Args>
-cudaError_t launch_ex(Kern kern, int grid, int threads, size_t smem, cudaStream_t s,
-                      const Args&... args) {
+cudaError_t launch_exc(Kern kern, int grid, int threads, size_t smem, cudaStream_t s,
+                       int cluster, const Args&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid, 1, 1);
     cfg.blockDim = dim3((unsigned)threads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (cluster > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)cluster;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cfg.numAttrs = (unsigned)na;
     return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+template <class Kern, class... Args>
+cudaError_t launch_ex(Kern kern, int grid, int threads, size_t smem, cudaStream_t s,
+                      const Args&... args) {
+    return launch_exc(kern, grid, threads, smem, s, 1, args...);
+}
+
+// Split-K reduced through distributed shared memory (csplit) unless B2G_SPLITK_CLUSTER=0 in
+// the environment (read once per process), which keeps every split on the workspace path.
+bool csplit_enabled() {
+    static const bool on = [] {
+        const char* e = std::getenv("B2G_SPLITK_CLUSTER");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+// Largest receive area a cluster split-K launch may take from the shared-memory ring.
+constexpr uint32_t kCsMaxRecvBytes = 64 * 1024;
+
+// Whether clusters of `ctas` CTAs of the 1-CTA kernel `tile` (one per SM at this shared-
+// memory size) can be resident on this device at all; cached per (device, tile, ctas, smem).
+bool cluster_fits(const DeviceInfo& di, int tile, int ctas, int threads, size_t smem,
+                  bool peers) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int, size_t, bool>, bool> cache;
+    const auto key = std::make_tuple(di.device, tile, ctas, smem, peers);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ctas, 1, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)ctas;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    const bool ok = cudaOccupancyMaxActiveClusters(&n, kernel_ptr(tile, peers), &cfg) ==
+                        cudaSuccess &&
+                    n > 0;
+    if (!ok) cudaGetLastError();
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = ok;
+    return ok;
 }
 
 template <bool PEERS>
@@ -267,14 +367,17 @@ cudaError_t launch_gemm_t(int tile, const CUtensorMap& tmA, const CUtensorMap& t
                           int& grid) {
     switch (tile) {
         case B2G_TILE_128x128:
-            grid = std::min(p.num_units, di.sm_count);
-            return launch_ex(gemm_sm100_1cta<128, PEERS>, grid, threads, smem, s, tmA, tmB, tmD, p);
+            grid = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
+            return launch_exc(gemm_sm100_1cta<128, PEERS>, grid, threads, smem, s,
+                              p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
         case B2G_TILE_128x256:
-            grid = std::min(p.num_units, di.sm_count);
-            return launch_ex(gemm_sm100_1cta<256, PEERS>, grid, threads, smem, s, tmA, tmB, tmD, p);
+            grid = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
+            return launch_exc(gemm_sm100_1cta<256, PEERS>, grid, threads, smem, s,
+                              p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
         case B2G_TILE_128x64:
-            grid = std::min(p.num_units, di.sm_count);
-            return launch_ex(gemm_sm100_1cta<64, PEERS>, grid, threads, smem, s, tmA, tmB, tmD, p);
+            grid = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
+            return launch_exc(gemm_sm100_1cta<64, PEERS>, grid, threads, smem, s,
+                              p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
         case B2G_TILE_256x512_2SM:
             grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
             return launch_ex(gemm_sm100_2cta<512, PEERS>, grid, threads, smem, s, tmA, tmB, tmBt,
@@ -305,7 +408,8 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "GEMM launch (tile %d, grid %d, smem %zu): %s", tile, grid, smem,
                     cudaGetErrorString(e));
-    g_last_launch = LaunchRecord{grid, threads, tile, p.stages, p.num_units, p.splits};
+    const int cluster = p.csplit ? p.splits : geom(tile).ctas;
+    g_last_launch = LaunchRecord{grid, threads, tile, p.stages, p.num_units, p.splits, cluster};
     return B2G_OK;
 }
 
@@ -371,7 +475,7 @@ int launch_swap(const void* A, const void* B, int M, int N, int K, long long lda
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "swap GEMM launch (MT %d, grid %d): %s", MT, grid,
                     cudaGetErrorString(e));
-    g_last_launch = LaunchRecord{grid, threads, B2G_TILE_SWAP_AB, p.stages, p.num_units, 1};
+    g_last_launch = LaunchRecord{grid, threads, B2G_TILE_SWAP_AB, p.stages, p.num_units, 1, 1};
     return B2G_OK;
 }
 
@@ -665,7 +769,7 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     if (smem_needed(tile, stages, epi_boxes) > (size_t)di.smem_optin)
         return fail(B2G_ERR_SMEM, "smem over per-block opt-in limit: %zu > %d (tile %d, %d stages)",
                     smem_needed(tile, stages, epi_boxes), di.smem_optin, tile, stages);
-    const size_t smem = smem_request(tile, stages, di, epi_boxes);
+    size_t smem = smem_request(tile, stages, di, epi_boxes);
 
     GemmParams p{};
     p.M = M;
@@ -721,7 +825,30 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
                          peers);
     p.splits = splits;
     p.num_units = p.num_tiles * splits;
-    if (splits > 1) {
+    // Split-K of 1-CTA tiles is reduced inside clusters of `splits` CTAs through distributed
+    // shared memory when the receive slots fit beside a ring of at least two stages (measured
+    // on B200: the workspace's partial stores, release-ordered arrival and L2 re-reads cost
+    // more than the split mainloop they serve at decode shapes). b2g_gemm_splitk_noalloc
+    // keeps the workspace path on its static scratch; both reductions give the same bits.
+    if (splits > 1 && g.ctas == 1 && !noalloc && splits <= 8 && csplit_enabled()) {
+        const uint32_t recv = csplit_recv_bytes(g.bn, splits);
+        int st = stages;
+        if (stages_arg == 0)
+            while (st > 2 && smem_needed(tile, st, epi_boxes) + recv > (size_t)di.smem_optin) --st;
+        const size_t need = smem_needed(tile, st, epi_boxes) + recv;
+        const size_t req = std::max(need, (size_t)di.smem_per_sm / 2 + 1024);
+        if (recv <= kCsMaxRecvBytes && need <= (size_t)di.smem_optin) {
+            if (int rc = ensure_kernel_attrs(tile, di, npeer > 0)) return rc;
+            if (cluster_fits(di, tile, splits, gemm_threads(8), req, npeer > 0)) {
+                p.csplit = 1;
+                p.recv_bytes = recv;
+                stages = st;
+                p.stages = st;
+                smem = req;
+            }
+        }
+    }
+    if (splits > 1 && !p.csplit) {
         const size_t part = (size_t)p.num_tiles * splits * g.ctas * 128 * g.bn * sizeof(float);
         const size_t counters = (size_t)p.num_tiles * g.ctas * kMaxEpiWarps;
         SplitScratch sc{};
@@ -753,16 +880,34 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     CUtensorMap tmA, tmB;
     if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK, a_rows, "A"))
         return rc;
-    // B: N x K in 128-row x 64-k boxes, or K x N in 64-column x 64-k-row boxes (MN-major)
-    if (int rc = b_mn ? make_tmap(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, kBK, "B")
-                      : make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, g.box_b,
-                                  "B"))
-        return rc;
+    // B: N x K in 128-row x 64-k boxes, or K x N (MN-major) either in one 3D box of all the
+    // 64-column groups a CTA loads per stage (N % 64 == 0) or in 64-column x 64-k-row boxes
+    // (columns per CTA and stage: BN on one CTA, min(tile width, 256) / 2 per CTA of a pair)
+    const auto kn_groups = [&](int width) {
+        return (uint32_t)((g.ctas == 2 ? std::min(width, kPairBN) / 2 : width) / 64);
+    };
+    if (b_mn && N % 64 == 0 && kn3d_enabled()) {
+        if (make_tmap_kn3d(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, kn_groups(g.bn)) ==
+            B2G_OK)
+            p.b_kn3d = 1;
+        else
+            clear_error();  // not encodable here: the 2D boxes below
+    }
+    if (!p.b_kn3d)
+        if (int rc = b_mn ? make_tmap(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, kBK, "B")
+                          : make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK,
+                                      g.box_b, "B"))
+            return rc;
     CUtensorMap tmBt = tmB;  // B boxes of the tail slices (min(width, 256) / 2 rows per CTA)
-    if (p.tail_split > 1 && !b_mn)
+    if (p.tail_split > 1 && p.b_kn3d) {
+        if (int rc = make_tmap_kn3d(&tmBt, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb,
+                                    kn_groups(g.bn / p.tail_split)))
+            return rc;
+    } else if (p.tail_split > 1 && !b_mn) {
         if (int rc = make_tmap(&tmBt, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK,
                                (uint32_t)(std::min(g.bn / p.tail_split, kPairBN) / 2), "B tail"))
             return rc;
+    }
     CUtensorMap tmD = tmA;  // D in 32-row x 64-column boxes (unused without d_tma)
     if (p.d_tma)
         if (int rc = make_tmap(&tmD, D, (uint64_t)N, (uint64_t)M, (uint64_t)ldd, 64, 32, "D"))
@@ -879,6 +1024,14 @@ B2G_EXPORT int b2g_last_launch(int* grid, int* threads, int* tile, int* stages, 
     if (stages) *stages = r.stages;
     if (units) *units = r.units;
     if (splits) *splits = r.splits;
+    return B2G_OK;
+}
+
+B2G_EXPORT int b2g_last_launch_cluster(int* cluster_ctas) {
+    clear_error();
+    const LaunchRecord r = g_last_launch;
+    if (r.grid == 0) return fail(B2G_ERR_ARG, "no GEMM kernel launched on this host thread yet");
+    if (cluster_ctas) *cluster_ctas = r.cluster;
     return B2G_OK;
 }
 
@@ -1017,37 +1170,50 @@ B2G_EXPORT int b2g_probe_tcgen05(int kind, int cta_group, int n, int iters,
                                  double* flop_per_clk_sm, long long* cycles_out) {
     clear_error();
     if (kind < 0 || kind > 3) return fail(B2G_ERR_ARG, "kind must be 0..3, got %d", kind);
-    if (cta_group != 1)
-        return fail(B2G_ERR_UNSUPPORTED, "cta_group %d probe is not built yet", cta_group);
+    if (cta_group != 1 && cta_group != 2)
+        return fail(B2G_ERR_ARG, "cta_group must be 1 or 2, got %d", cta_group);
     if (n < 16 || n > 256 || n % 16) return fail(B2G_ERR_ARG, "n must be 16..256, step 16");
     if (iters < 1 || iters > (1 << 24)) return fail(B2G_ERR_ARG, "iters must be 1..2^24");
     DeviceInfo di;
     if (int rc = current_device(di)) return rc;
-    const int blocks = di.sm_count;
+    // one CTA per SM (cta_group 1) or one 2-CTA cluster per pair of SMs (cta_group 2)
+    const int blocks = cta_group == 1 ? di.sm_count : 2 * (di.sm_count / 2);
+    const int timed = cta_group == 1 ? blocks : blocks / 2;
     long long* dcyc = nullptr;
-    cudaError_t e = cudaMalloc(&dcyc, sizeof(long long) * blocks);
+    cudaError_t e = cudaMalloc(&dcyc, sizeof(long long) * timed);
     if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "probe cudaMalloc: %s", cudaGetErrorString(e));
-    const uint32_t idesc = idesc_probe(kind, 128, n);
+    e = cudaMemset(dcyc, 0, sizeof(long long) * timed);
+    const uint32_t idesc = idesc_probe(kind, cta_group == 1 ? 128 : 256, n);
     const unsigned long long tmo = wait_timeout_ns();
     auto run = [&](auto kern) -> cudaError_t {
         cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)kProbeSmem);
         if (r != cudaSuccess) return r;
-        for (int w = 0; w < 3; ++w) kern<<<blocks, kProbeThreads, kProbeSmem>>>(idesc, iters, dcyc, tmo);
-        kern<<<blocks, kProbeThreads, kProbeSmem>>>(idesc, iters, dcyc, tmo);
+        for (int w = 0; w < 4; ++w) kern<<<blocks, kProbeThreads, kProbeSmem>>>(idesc, iters, dcyc, tmo);
         return cudaDeviceSynchronize();
     };
-    switch (kind) {
-        case kProbeF16F32: e = run(probe_tcgen05_kernel<kProbeF16F32>); break;
-        case kProbeF16F16: e = run(probe_tcgen05_kernel<kProbeF16F16>); break;
-        case kProbeI8: e = run(probe_tcgen05_kernel<kProbeI8>); break;
-        default: e = run(probe_tcgen05_kernel<kProbeE4M3>); break;
+    if (e == cudaSuccess) {
+        if (cta_group == 1) {
+            switch (kind) {
+                case kProbeF16F32: e = run(probe_tcgen05_kernel<kProbeF16F32>); break;
+                case kProbeF16F16: e = run(probe_tcgen05_kernel<kProbeF16F16>); break;
+                case kProbeI8: e = run(probe_tcgen05_kernel<kProbeI8>); break;
+                default: e = run(probe_tcgen05_kernel<kProbeE4M3>); break;
+            }
+        } else {
+            switch (kind) {
+                case kProbeF16F32: e = run(probe_tcgen05_pair_kernel<kProbeF16F32>); break;
+                case kProbeF16F16: e = run(probe_tcgen05_pair_kernel<kProbeF16F16>); break;
+                case kProbeI8: e = run(probe_tcgen05_pair_kernel<kProbeI8>); break;
+                default: e = run(probe_tcgen05_pair_kernel<kProbeE4M3>); break;
+            }
+        }
     }
     long long best = -1;
     if (e == cudaSuccess) {
-        long long* h = new long long[blocks];
-        e = cudaMemcpy(h, dcyc, sizeof(long long) * blocks, cudaMemcpyDeviceToHost);
-        for (int b = 0; b < blocks && e == cudaSuccess; ++b)
+        long long* h = new long long[timed];
+        e = cudaMemcpy(h, dcyc, sizeof(long long) * timed, cudaMemcpyDeviceToHost);
+        for (int b = 0; b < timed && e == cudaSuccess; ++b)
             if (h[b] > 0 && (best < 0 || h[b] < best)) best = h[b];  // least-perturbed SM
         delete[] h;
     }
@@ -1055,6 +1221,7 @@ B2G_EXPORT int b2g_probe_tcgen05(int kind, int cta_group, int n, int iters,
     if (e != cudaSuccess) return fail(B2G_ERR_CUDA, "probe: %s", cudaGetErrorString(e));
     if (int rc = b2g_sync_status(nullptr)) return rc;
     if (best <= 0) return fail(B2G_ERR_TIMEOUT, "probe produced no timing");
+    // FLOP of one MMA: 2 x M x N x K, M = 128 per SM (the pair's M = 256 spans two SMs)
     const double flop = 2.0 * 128.0 * n * probe_mma_k(kind) * (double)iters;
     if (flop_per_clk_sm) *flop_per_clk_sm = flop / (double)best;
     if (cycles_out) *cycles_out = best;

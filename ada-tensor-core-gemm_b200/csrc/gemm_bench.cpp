@@ -470,7 +470,7 @@ int main(int argc, char** argv) {
             usage(argv[0]);
             return 0;
         } else {
-            // silently ignoring an unrecognised flag once cost the reference a soak run
+            // a typo'd flag must stop the run: otherwise a long measurement runs with defaults
             fprintf(stderr, "unknown option '%s' (try --help)\n", argv[i]);
             return 2;
         }

@@ -55,6 +55,8 @@ struct GemmParams {
     int d_tma;       // D written by TMA stores (D 16-byte aligned and ldd % 8 == 0), else by
                      // coalesced plain stores from the same staging box
     int b_mn_major;  // B is K x N (MN-major) in global memory
+    int b_kn3d;      // ... and read through a 3D tensor map (64 columns, K, N / 64): one load
+                     // per CTA per stage brings all of its 64-column boxes (N % 64 == 0)
     unsigned long long timeout_ns;
     // 2-CTA kernel work list: tiles [0, dp_tiles) run whole; each remaining tile (the last,
     // partial wave) is cut into tail_split column slices of kPairBN / tail_split columns,
@@ -67,6 +69,12 @@ struct GemmParams {
     float* ws_part;                // FP32 partial accumulators, splitk_slot() layout
     unsigned long long* ws_count;  // arrival counters: (launch epoch << 32) | arrivals
     unsigned int epoch;            // this launch's epoch, never 0 and never repeated
+    // 1-CTA kernels, splits > 1: csplit = 1 reduces the splits of a tile inside a cluster of
+    // `splits` CTAs through distributed shared memory (see csplit_epilogue) instead of the
+    // workspace; the grid is then one CTA per unit (not persistent) and recv_bytes of shared
+    // memory after the epilogue staging hold the receive slots.
+    int csplit;
+    uint32_t recv_bytes;
     // 1-CTA kernels: bytes one stage's two TMA loads deliver. When all of M fits one tile the
     // A box is only round_up(M, 8) rows high; the stale shared-memory rows below it feed
     // accumulator rows >= M, which the epilogue never stores.
@@ -130,18 +138,25 @@ struct TileTraits {
     static constexpr uint32_t kTmemCols = 2 * BN;  // power of two for BN in {128, 256}
 };
 
+// Cluster split-K: most pieces (32 accumulator rows x 64 columns) one CTA owns and reduces,
+// and the bytes of one FP32 piece.
+constexpr int kCsMaxPieces = 8;
+constexpr uint32_t kCsPieceBytes = 32 * 64 * 4;
+
 struct SmemCtl {
     uint64_t full[kMaxStages];
     uint64_t empty[kMaxStages];
     uint64_t tmem_full[2];
     uint64_t tmem_empty[2];
+    uint64_t recv[kCsMaxPieces];  // cluster split-K: one receive barrier per owned piece
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
     int never;  // stays 0: lets teardown waits ignore `abort` and use only their time limit
 };
 
-// Dynamic shared memory: [align slack][stages x (A, B)][epilogue staging][SmemCtl]
+// Dynamic shared memory: [align slack][stages x (A, B)][epilogue staging][cluster split-K
+// receive slots, if any][SmemCtl]
 template <int BN>
 constexpr size_t gemm_smem_bytes(int stages, uint32_t epi) {
     return 1024 /* alignment slack */ + (size_t)stages * TileTraits<BN>::kStageBytes + epi +
@@ -180,14 +195,15 @@ __device__ __forceinline__ uint32_t epi_pack2(const EpiScalars& e, int col, uint
         v1 = __uint_as_float(r1);
     }
     if constexpr (EPI) {
+        // multiply, then add: two roundings, as the reference's fused kernel computes them
+        // (src/gemm_bench.cu:380-383; checked bit for bit against it on exact accumulators)
+        v0 = __fmul_rn(v0, e.alpha);
+        v1 = __fmul_rn(v1, e.alpha);
         if (e.bias != nullptr) {
             const int n0 = col < e.N ? col : e.N - 1;
             const int n1 = col + 1 < e.N ? col + 1 : e.N - 1;
-            v0 = fmaf(v0, e.alpha, __half2float(e.bias[n0]));
-            v1 = fmaf(v1, e.alpha, __half2float(e.bias[n1]));
-        } else {
-            v0 *= e.alpha;
-            v1 *= e.alpha;
+            v0 = __fadd_rn(v0, __half2float(e.bias[n0]));
+            v1 = __fadd_rn(v1, __half2float(e.bias[n1]));
         }
         v0 = v0 > 0.f ? v0 : 0.f;
         v1 = v1 > 0.f ? v1 : 0.f;
@@ -582,6 +598,140 @@ __device__ __forceinline__ void splitk_epilogue(const GemmParams& p, const EpiSc
     B2G_TOC64(12, t_red);
 }
 
+// ------------------------------------------------------------------------------------------
+// Split-K reduced inside a cluster (1-CTA tiles, csplit). The grid has one CTA per unit and
+// clusters of S = splits CTAs along x, so CTA rank s of a cluster computes split s of the
+// cluster's tile; no workspace and no counters. The tile is cut into pieces of 32
+// accumulator rows (one TMEM lane quarter q) x 64 columns (chunk c); piece i = q * chunks + c
+// belongs to CTA i mod S of the cluster, as its (i / S)-th owned piece. The warp of every
+// other split that holds the piece writes its FP32 values straight into the owner's shared
+// memory with st.async, whose bytes complete the owner's receive barrier of that piece; the
+// owner's warp sums the S partials in split order 0..S-1 (its own read from TMEM) -- the
+// operations and order of the workspace reduction, so both give the same bits -- and runs the
+// normal epilogue of the piece. Every receive slot is written once per launch, so no slot is
+// ever reused and nothing waits for a free slot; senders never wait at all.
+// ------------------------------------------------------------------------------------------
+
+// Receive slots of one CTA: [owned piece k][sender slot j (senders in split order, the owner
+// skipped)][float4 g 0..15][lane], so every warp-wide st.async / ld.shared is one contiguous
+// 512-byte run.
+__host__ __device__ constexpr uint32_t csplit_recv_bytes(int bn, int splits) {
+    return (uint32_t)((4 * (bn / 64) + splits - 1) / splits) * (uint32_t)(splits - 1) *
+           kCsPieceBytes;
+}
+
+// Send chunk c of this warp's 32 TMEM lanes to the owner: `dst` = the slot and `bar` = the
+// owner's receive barrier, both as shared::cluster addresses.
+__device__ __forceinline__ void csplit_send(uint32_t trow, int c, uint32_t dst, uint32_t bar,
+                                            int lane) {
+    uint32_t r[32];
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+        tmem_ld_32x32b_x32(trow + (uint32_t)(c * 64 + h * 32), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+            st_async_v4(dst + (uint32_t)(((h * 8 + g) * 32 + lane) * 16), r[4 * g], r[4 * g + 1],
+                        r[4 * g + 2], r[4 * g + 3], bar);
+    }
+}
+
+// Owner: sum the S partials of chunk c in split order (own partial, split s, from TMEM; the
+// others from the receive slots starting at `slots`) and store the piece like any epilogue.
+template <bool EPI, bool PEERS>
+__device__ __forceinline__ void csplit_reduce(const GemmParams& p, const EpiScalars& e,
+                                              const CUtensorMap* tmD, uint32_t trow, int c,
+                                              int s, uint32_t slots, int row0, int n_first,
+                                              uint32_t stage0, int lane, uint32_t& seq) {
+    const int S = p.splits;
+    const int col = n_first + c * 64;
+    const uint32_t box = e.d_tma ? epi_box_acquire(e, stage0, seq, lane) : stage0;
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(trow + (uint32_t)(c * 64 + h * 32), r);
+        tmem_ld_wait();
+        float acc[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+#pragma unroll 1
+        for (int t = 0; t < S; ++t) {
+            if (t == s) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc[j] += __uint_as_float(r[j]);
+            } else {
+                const uint32_t slot = slots + (uint32_t)(t < s ? t : t - 1) * kCsPieceBytes;
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                    const uint4 v = ld_shared_v4(slot + (uint32_t)(((h * 8 + g) * 32 + lane) * 16));
+                    acc[4 * g] += __uint_as_float(v.x);
+                    acc[4 * g + 1] += __uint_as_float(v.y);
+                    acc[4 * g + 2] += __uint_as_float(v.z);
+                    acc[4 * g + 3] += __uint_as_float(v.w);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(acc[j]);
+        epi_box_put32<false, EPI>(e, box, col, h, r, lane);
+    }
+    if (e.d_tma)
+        epi_box_store(e, tmD, box, col, row0, lane, seq);
+    else
+        epi_box_store_rows(p, e, box, col, row0, lane);
+    epi_box_push<PEERS>(p, e, box, col, row0, lane);
+}
+
+// Cluster split-K epilogue of one warp (lane quarter q, chunks c_first, c_first + c_step, ...)
+// for this CTA's split s: first every piece another CTA owns is sent, then every owned piece
+// is received (bounded wait) and reduced; TMEM is released last. Pieces outside D (rows >= M
+// or chunks starting at or beyond N) are skipped by every split alike.
+template <bool PEERS, class Release>
+__device__ __forceinline__ void csplit_epilogue(const GemmParams& p, const EpiScalars& e,
+                                                const CUtensorMap* tmD, uint32_t trow, int q,
+                                                int bn, int row0, int n_first, int c_first,
+                                                uint32_t stage0, int lane, uint32_t& seq,
+                                                bool epi, uint32_t recv0, uint32_t rbar0,
+                                                const WaitCtx& w, Release release) {
+    const int S = p.splits;
+    const int s = (int)cluster_ctarank();
+    const int nch = bn / 64;
+    int nchunks = nch;
+    const int in_n = (e.N - n_first + 63) / 64;
+    if (in_n < nchunks) nchunks = in_n;
+    if (row0 < e.M) {
+#pragma unroll 1
+        for (int c = c_first; c < nchunks; c += e.c_step) {
+            const int i = q * nch + c, owner = i % S, k = i / S;
+            if (owner == s) continue;
+            const int j = s < owner ? s : s - 1;
+            csplit_send(trow, c,
+                        mapa_shared(recv0 + (uint32_t)(k * (S - 1) + j) * kCsPieceBytes,
+                                    (uint32_t)owner),
+                        mapa_shared(rbar0 + 8u * (uint32_t)k, (uint32_t)owner), lane);
+        }
+#pragma unroll 1
+        for (int c = c_first; c < nchunks; c += e.c_step) {
+            const int i = q * nch + c, owner = i % S, k = i / S;
+            if (owner != s) continue;
+            const uint32_t rb = rbar0 + 8u * (uint32_t)k;
+            if (lane == 0) mbar_arrive_expect_tx(rb, (uint32_t)(S - 1) * kCsPieceBytes);
+            __syncwarp();
+            B2G_TIC(t_rv);
+            if (!mbar_wait_warp<true>(rb, 0, w)) break;
+            B2G_TOC64(14, t_rv);
+            const uint32_t slots = recv0 + (uint32_t)(k * (S - 1)) * kCsPieceBytes;
+            if (epi)
+                csplit_reduce<true, PEERS>(p, e, tmD, trow, c, s, slots, row0, n_first, stage0,
+                                           lane, seq);
+            else
+                csplit_reduce<false, PEERS>(p, e, tmD, trow, c, s, slots, row0, n_first, stage0,
+                                            lane, seq);
+        }
+    }
+    release();
+}
+
 // PEERS: the fused all-gather instantiation (every staged box of D also goes to p.peers).
 template <int BN, bool PEERS = false>
 __global__ void __launch_bounds__(kMaxThreads, 1)
@@ -599,14 +749,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const uint32_t sB = sA + (uint32_t)p.stages * kAStageBytes;
     const uint32_t sEpi = raw + pad + (uint32_t)p.stages * TT::kStageBytes;
     const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
+    const uint32_t sRecv = sEpi + epi_bytes(epi_warps, p.epi_bufs);
     SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * TT::kStageBytes +
-                                              epi_bytes(epi_warps, p.epi_bufs));
+                                              epi_bytes(epi_warps, p.epi_bufs) + p.recv_bytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t full0 = smem_u32(&ctl->full[0]);
     const uint32_t empty0 = smem_u32(&ctl->empty[0]);
     const uint32_t tfull0 = smem_u32(&ctl->tmem_full[0]);
     const uint32_t tempty0 = smem_u32(&ctl->tmem_empty[0]);
+    const uint32_t rbar0 = smem_u32(&ctl->recv[0]);
     const uint32_t drain = smem_u32(&ctl->drain);
 
     if (threadIdx.x == 0) {
@@ -618,6 +770,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             mbar_init(tfull0 + 8 * b, 1);
             mbar_init(tempty0 + 8 * b, (uint32_t)epi_warps);  // one arrive per epilogue warp
         }
+        for (int k = 0; k < kCsMaxPieces; ++k) mbar_init(rbar0 + 8 * k, 1);  // owner's arm
         mbar_init(drain, 1);
         ctl->abort = 0;
         ctl->never = 0;
@@ -634,6 +787,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
+    // cluster split-K: every CTA's receive barriers exist before any peer stores into them
+    if (p.csplit) cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = ctl->tmem_base;
     volatile int* abort_flag = &ctl->abort;
@@ -667,7 +822,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     mbar_arrive_expect_tx(fb, p.stage_tx);
                     tma_load_2d(sA + stage * kAStageBytes, &tmA, fb, kb * kBK, m0);
                     const uint32_t sBs = sB + stage * TT::kBStageBytes;
-                    if (p.b_mn_major) {
+                    if (p.b_kn3d) {
+                        // B is K x N: the BN / 64 boxes of 64 columns x 64 k-rows in one load
+                        tma_load_3d(sBs, &tmB, fb, 0, kb * kBK, n0 >> 6);
+                    } else if (p.b_mn_major) {
                         // B is K x N: BN / 64 boxes of 64 columns x 64 k-rows (8 KiB each)
 #pragma unroll
                         for (int j = 0; j < BN / 64; ++j)
@@ -790,7 +948,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
             };
-            if (p.splits > 1) {
+            if (p.splits > 1 && p.csplit) {
+                csplit_epilogue<PEERS>(p, es, &tmD, tbase, q, BN, tm * kBM + q * 32, tn * BN,
+                                       c_first, stage0, lane, seq, epi, sRecv, rbar0, w, release);
+            } else if (p.splits > 1) {
                 splitk_epilogue<PEERS>(p, es, &tmD, tbase, t, u - t * p.splits, 0, 1, q, warp - 2, BN,
                                 tm * kBM + q * 32, tn * BN, c_first, stage0, lane, seq, epi,
                                 release);
@@ -806,6 +967,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     }
 
     __syncthreads();
+    // cluster split-K: no CTA leaves while a peer may still store into its receive slots
+    if (p.csplit) cluster_sync();
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();

@@ -201,7 +201,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                     for (int h = 0; h < nh; ++h) {
                         const int n0 = n_first + h * kPairBN + (int)rank * hw;
                         const uint32_t dst = sB + stage * PT::kBStageBytes + (uint32_t)h * kHalfBytes;
-                        if (p.b_mn_major) {
+                        if (p.b_kn3d) {
+                            // B is K x N: the hw / 64 boxes of 64 columns x 64 k-rows at once
+                            tma_load_3d_pair(dst, mapB, fb, 0, kb * kBK, n0 >> 6);
+                        } else if (p.b_mn_major) {
                             // B is K x N: hw / 64 boxes of 64 columns x 64 k-rows
                             for (int j = 0; j < (hw >> 6); ++j)
                                 tma_load_2d_pair(dst + (uint32_t)j * kMnBoxBytes, mapB, fb,

@@ -58,7 +58,7 @@ __device__ __forceinline__ void swap_epilogue_t(const GemmParams& p, uint32_t tr
             float v = ACC16 ? __half2float(__ushort_as_half((unsigned short)(r[jj] & 0xFFFFu)))
                             : __uint_as_float(r[jj]);
             if constexpr (EPI) {
-                v = fmaf(v, alpha, badd);
+                v = __fadd_rn(__fmul_rn(v, alpha), badd);  // two roundings, as the reference
                 v = v > 0.f ? v : 0.f;
             }
             if (in_n && m < M) col[(size_t)m * ldd] = __float2half_rn(v);

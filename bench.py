@@ -15,6 +15,12 @@ BASELINE.json configs). Workloads:
             all-gather of the D panels and the same gather fused into the GEMM
             (b2g_gemm_peers over CUDA IPC mappings), reported separately (any workload).
 
+Unless --no-sharded, the bench line also carries a `sharded` object: configs[4] with its M
+rows split over the ranks (strong scaling), the same run's 1-GPU time of the whole problem,
+an NCCL all-gather of the D panels and the fused GEMM + all-gather (b2g_gemm_peers), each
+device-timed as the max over ranks. Under torchrun NCCL's init log goes to a per-process
+file and rank 0 quotes its `Init COMPLETE` line (`nccl_comm`).
+
 `value` is whole-job TFLOP/s with inputs resident in HBM, timed with CUDA events on the
 launching stream, max over ranks. Between timed iterations the inputs rotate over enough
 buffer sets that the working set exceeds the 126 MB L2. `e2e` is the same metric through
@@ -86,6 +92,8 @@ def parse():
                    help="target CPU time of the bounded cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--allgather", action="store_true")
+    p.add_argument("--no-sharded", action="store_true",
+                   help="skip the configs[4] strong-scaling object (`sharded`) of the bench line")
     p.add_argument("--sweep", choices=tuple(SWEEPS), default=None,
                    help="per-shape table (one JSON line per shape, then a markdown table) "
                         "instead of the single bench line")
@@ -202,19 +210,20 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------------------
-def fused_allgather(full, rows, N, acc, inputs, stream, sptr, dev, rank, world, args,
-                    sequential_ms, barrier):
+def fused_allgather(full, rows, N, acc, dA, dB, stream, sptr, dev, rank, world,
+                    sequential_ms, barrier, tile=-1, stages=0, group=0, reps=5):
     """GEMM and all-gather in one kernel per rank: every rank maps every other rank's full D
     through CUDA IPC and runs b2g_gemm_peers, whose epilogue stores each D box into its own
     rows of every rank's full D over NVLink. Timed like the rest (CUDA events, max over ranks)
-    and checked bit for bit against an NCCL all-gather of the same GEMM's panels."""
+    and checked bit for bit against an NCCL all-gather of the same GEMM's panels. `full` is
+    filled with NaN on every rank before the timed steps and again before the checked step,
+    so every compared byte was written by that step's TMA stores or peer stores."""
     import torch
     import torch.distributed as dist
 
     import b2g
     from b2g.shard import max_over_ranks
 
-    dA, dB, _ = inputs
     handles = [None] * world
     dist.all_gather_object(handles, b2g.ipc_handle(full))
     bases, peers = [], []
@@ -226,15 +235,20 @@ def fused_allgather(full, rows, N, acc, inputs, stream, sptr, dev, rank, world, 
     own = full[rank * rows:(rank + 1) * rows]
 
     def step():
-        b2g.gemm_peers(dA, dB, own, peers, acc=acc, tile=args.tile, stages=args.stages,
-                       group=args.group, stream=sptr)
+        b2g.gemm_peers(dA, dB, own, peers, acc=acc, tile=tile, stages=stages, group=group,
+                       stream=sptr)
 
+    def nan_everywhere():
+        full.fill_(float("nan"))
+        torch.cuda.synchronize()
+        barrier()  # no rank pushes into a `full` that is still being filled
+
+    nan_everywhere()
     for _ in range(2):
         step()
     b2g.sync_status(sptr)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    reps = 5
     e0.record(stream)
     for _ in range(reps):
         step()
@@ -243,9 +257,12 @@ def fused_allgather(full, rows, N, acc, inputs, stream, sptr, dev, rank, world, 
     b2g.sync_status(sptr)
     barrier()  # every rank's pushes into `full` have completed
     fused_ms = max_over_ranks(e0.elapsed_time(e1) / reps, dev)
+    nan_everywhere()
+    step()
+    b2g.sync_status(sptr)
+    barrier()  # the checked step's pushes have landed everywhere
     panel = torch.empty_like(own)
-    b2g.gemm(dA, dB, panel, acc=acc, tile=args.tile, stages=args.stages, group=args.group,
-             stream=sptr)
+    b2g.gemm(dA, dB, panel, acc=acc, tile=tile, stages=stages, group=group, stream=sptr)
     b2g.sync_status(sptr)
     ref = torch.empty_like(full)
     dist.all_gather_into_tensor(ref, panel)
@@ -255,9 +272,147 @@ def fused_allgather(full, rows, N, acc, inputs, stream, sptr, dev, rank, world, 
     barrier()  # no rank still writes through a mapping
     for base in bases:
         b2g.ipc_close(base)
+    del ref
     return {"ms": fused_ms, "vs_gemm_then_allgather": round(fused_ms / sequential_ms, 4),
             "equal_to_nccl_gather": bool(same.item()),
+            "check": "full D NaN-filled on every rank before the checked step",
             "how": "b2g_gemm_peers: epilogue stores each D box into every rank's D (CUDA IPC)"}
+
+
+NCCL_LOG = "/tmp/b2g_nccl_{pid}.log"
+
+
+def nccl_log_setup():
+    """NCCL's communicator-init log goes to a per-process file (not stdout, which carries
+    the JSON line); rank 0 quotes its `Init COMPLETE` line (rank, nranks) in the output."""
+    if "NCCL_DEBUG" not in os.environ:
+        os.environ["NCCL_DEBUG"] = "INFO"
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", NCCL_LOG.format(pid=os.getpid()))
+
+
+def nccl_log_summary():
+    path = os.environ.get("NCCL_DEBUG_FILE", "")
+    if not path or not os.path.exists(path):
+        return None
+    with open(path, errors="replace") as fh:
+        lines = fh.read().splitlines()
+    done = [ln.split("NCCL INFO", 1)[-1].strip() for ln in lines if "Init COMPLETE" in ln]
+    ver = [ln.split("NCCL INFO", 1)[-1].strip() for ln in lines if "NCCL version" in ln]
+    return {"version": ver[0] if ver else None, "init_complete": done[:4]}
+
+
+def sharded_leg(args, world, rank, dev, stream, sptr, barrier):
+    """BASELINE configs[4] strong scaling: the 32768 x 32768 x 8192 GEMM with its M rows split
+    over the ranks (B replicated), device-timed as the max over ranks; the same run's 1-GPU
+    figure (rank 0 alone with the whole problem, the other ranks waiting); an NCCL
+    all-gather of the D panels; and the all-gather fused into the GEMM (b2g_gemm_peers).
+    No cuBLAS or end-to-end legs here, so every N fits the driver's per-run limit."""
+    import torch
+    import torch.distributed as dist
+
+    import b2g
+    from b2g.shard import max_over_ranks, mean_over_ranks, panel, strong_scaling
+
+    wl = WORKLOADS["sharded"]
+    M, N, K = wl["M"], wl["N"], wl["K"]
+    r0, r1 = panel(M, world, rank)
+    rows = r1 - r0
+    f16 = torch.float16
+    flop = 2.0 * M * N * K
+    host = torch.empty((max(M, N), K), dtype=f16, pin_memory=True)
+    dB = torch.empty((N, K), dtype=f16, device=dev)
+    if rank == 0:  # B is generated once and broadcast (set-up, outside any timed region)
+        b2g.fill_uniform(N * K, wl["seed"], 1, wl["lo"], wl["hi"], out=host.data_ptr())
+        dB.copy_(host[:N])
+    if world > 1:
+        dist.broadcast(dB, src=0)
+    solo = rank == 0 and world > 1
+    if solo:  # rank 0 keeps all of A for the 1-GPU run; its panel is the first rows
+        b2g.fill_uniform(M * K, wl["seed"], 0, wl["lo"], wl["hi"], out=host.data_ptr())
+        dA_full = torch.empty((M, K), dtype=f16, device=dev)
+        dA_full.copy_(host[:M])
+        dA = dA_full[:rows]
+    else:
+        b2g.fill_uniform(rows * K, wl["seed"], 0, wl["lo"], wl["hi"], out=host.data_ptr(),
+                         first=r0 * K)
+        dA = torch.empty((rows, K), dtype=f16, device=dev)
+        dA.copy_(host[:rows])
+    del host
+    dD = torch.empty((rows, N), dtype=f16, device=dev)
+    torch.cuda.synchronize()
+    steps, warm = max(3, min(args.steps, 10)), 2
+
+    def time_gemm(a, d, m):
+        def go():
+            b2g.gemm_raw(a.data_ptr(), dB.data_ptr(), d.data_ptr(), None, m, N, K, K, K, N,
+                         b2g.B_NK, b2g.ACC_F32, b2g.EPI_NONE, 1.0, b2g.TILE_AUTO, 0, 0, sptr)
+        for _ in range(warm):
+            go()
+        b2g.sync_status(sptr)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            go()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        b2g.sync_status(sptr)
+        return e0.elapsed_time(e1) / steps, b2g.kernel_clock()[0], b2g.last_launch()
+
+    ms1 = mhz1 = None
+    if solo:
+        dD_full = torch.empty((M, N), dtype=f16, device=dev)
+        ms1, mhz1, _ = time_gemm(dA_full, dD_full, M)
+        del dD_full, dA_full
+        torch.cuda.empty_cache()
+    barrier()
+    ms_local, mhz_local, launch = time_gemm(dA, dD, rows)
+    barrier()
+    ms_n = max_over_ranks(ms_local, dev)
+    mhz_n = mean_over_ranks(mhz_local, dev)
+    if world == 1:
+        ms1, mhz1 = ms_n, mhz_n
+    peaks, _ = measured_peaks()
+    out = {"workload": wl["name"], "M": M, "N": N, "K": K, "rows_per_gpu": rows,
+           "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": round(ms_n, 4),
+           "kernel_sm_mhz_mean": round(mhz_n, 1), "launch_rank0": launch,
+           "one_gpu_same_run": {"ms_per_step": round(ms1, 4) if ms1 else None,
+                                "tflops": round(flop / (ms1 * 1e-3) / 1e12, 2) if ms1 else None,
+                                "kernel_sm_mhz": round(mhz1, 1) if mhz1 else None},
+           "timing": "CUDA events per rank around back-to-back launches, max over ranks; "
+                     "inputs > L2 (B alone is 512 MiB)"}
+    recv = (world - 1) * rows * N * 2
+    scal = strong_scaling(flop, ms_n, world, ms1, mhz_n, mhz1,
+                          recv if world > 1 else None, 770.0, peaks["bf16_tflops_sustained"])
+    out.update({k: (round(v, 4) if isinstance(v, float) else v) for k, v in scal.items()})
+    if world > 1:
+        full = torch.empty((M, N), dtype=f16, device=dev)
+        for _ in range(2):
+            dist.all_gather_into_tensor(full, dD)
+        torch.cuda.synchronize()
+        barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 3
+        a0.record(stream)
+        for _ in range(reps):
+            dist.all_gather_into_tensor(full, dD)
+        a1.record(stream)
+        torch.cuda.synchronize()
+        ag = max_over_ranks(a0.elapsed_time(a1) / reps, dev)
+        out["allgather_nccl"] = {"ms": round(ag, 4), "bytes_received_per_gpu": recv,
+                                 "gbs_per_gpu": round(recv / (ag * 1e-3) / 1e9, 1),
+                                 "gemm_then_allgather_ms": round(ms_n + ag, 4)}
+        out["fused_gemm_allgather"] = fused_allgather(full, rows, N, b2g.ACC_F32, dA, dB,
+                                                      stream, sptr, dev, rank, world, ms_n + ag,
+                                                      barrier, reps=3)
+        fb = out.get("fused_step_bound")
+        if fb:
+            out["fused_gemm_allgather"]["frac_of_roofline"] = round(
+                fb["roofline_ms"] / out["fused_gemm_allgather"]["ms"], 4)
+        del full
+    del dA, dB, dD
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_ours(args):
@@ -274,6 +429,7 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
+        nccl_log_setup()
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
 
     wl = WORKLOADS[args.workload]
@@ -339,7 +495,9 @@ def run_ours(args):
         return max_over_ranks(e0.elapsed_time(e1), dev)
 
     # tcgen05 issue-rate probe (FLOP/clk/SM), for the %-of-peak column
-    probe_fpc, _ = b2g.probe_tcgen05(1 if acc == b2g.ACC_F16 else 0, 1, 256, 4096)
+    probe_kind = 1 if acc == b2g.ACC_F16 else 0
+    probe_fpc1, _ = b2g.probe_tcgen05(probe_kind, 1, 256, 4096)
+    probe_fpc2, _ = b2g.probe_tcgen05(probe_kind, 2, 256, 4096)
 
     sampler = ClockSampler(local)
     sampler.start()
@@ -349,6 +507,12 @@ def run_ours(args):
     # the SM clock the last timed launch actually ran at (clock64 / globaltimer in CTA 0)
     kmhz, _ = b2g.kernel_clock()
     clocks["kernel_sm_mhz"] = round(kmhz, 1)
+    headline_launch = b2g.last_launch()
+    # the denominator of %-of-peak is the probe of the MMA the timed kernel issues: the pair
+    # MMA (cta_group::2) for the 2-CTA tiles, the one-SM MMA otherwise
+    pair_kernel = headline_launch["tile"] in (b2g.TILE_256x256_2SM, b2g.TILE_256x512_2SM,
+                                              b2g.TILE_256x128_2SM)
+    probe_fpc = probe_fpc2 if pair_kernel else probe_fpc1
 
     # correctness of the timed output against cuBLAS (device max-rel, reference metric)
     dA, dB, dD = sets[(args.steps - 1) % nbuf]
@@ -404,9 +568,18 @@ def run_ours(args):
         ag = max_over_ranks(a0.elapsed_time(a1) / reps, dev)
         recv = (world - 1) * rows * N * 2
         allgather = {"ms": ag, "bytes_received_per_gpu": recv, "gbs_per_gpu": recv / (ag * 1e-3) / 1e9}
-        allgather["fused"] = fused_allgather(full, rows, N, acc, sets[0], stream, sptr, dev,
-                                             rank, world, args, ms / args.steps + ag, barrier)
+        allgather["fused"] = fused_allgather(full, rows, N, acc, sets[0][0], sets[0][1], stream,
+                                             sptr, dev, rank, world, ms / args.steps + ag,
+                                             barrier, args.tile, args.stages, args.group)
         del full
+
+    # configs[4] strong scaling next to the (unchanged) headline; every rank takes part
+    sharded = None
+    if args.workload != "sharded" and not args.no_sharded:
+        del sets
+        torch.cuda.empty_cache()
+        sharded = sharded_leg(args, world, rank, dev, stream, sptr, barrier)
+    nccl = nccl_log_summary() if world > 1 and rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -464,7 +637,11 @@ def run_ours(args):
             "algorithmic_bytes_per_launch": 2 * (rows * K + N * K + rows * N),
         },
         "pct_probe_peak": round(100 * achieved / probe_peak, 2) if probe_peak else None,
-        "probe": {"flop_per_clk_sm": round(probe_fpc, 1), "sms": sms, "sm_mhz": sm_mhz,
+        "probe": {"flop_per_clk_sm": round(probe_fpc, 1),
+                  "cta_group": 2 if pair_kernel else 1,
+                  "flop_per_clk_sm_cta_group_1": round(probe_fpc1, 1),
+                  "flop_per_clk_sm_cta_group_2": round(probe_fpc2, 1),
+                  "timed_launch": headline_launch, "sms": sms, "sm_mhz": sm_mhz,
                   "peak_tflops": round(probe_peak, 1) if probe_peak else None},
         "cublas_tflops": round(flop_job * args.steps / (ms_cublas * 1e-3) / 1e12, 3),
         "maxrel_vs_cublas": maxrel,
@@ -478,6 +655,10 @@ def run_ours(args):
         out["cpu_baseline"] = cpu
     if allgather:
         out["allgather"] = allgather
+    if sharded:
+        out["sharded"] = sharded
+    if nccl:
+        out["nccl_comm"] = nccl
     print(json.dumps(out), flush=True)
 
 

@@ -110,12 +110,19 @@ int b2g_gemm(const void* A, const void* B, void* D, const void* bias, int M, int
  *            than half of the SMs, FP32 accumulation only), 1 = never, S >= 2 = split the
  *            K range of every tile into S even parts (S <= ceil(K / 64); acc must be
  *            B2G_ACC_F32, else B2G_ERR_UNSUPPORTED).
- * Each split writes its FP32 partial tile to a workspace; the split that finishes last sums
- * the partials in split order 0..S-1 (deterministic) and applies the epilogue. The workspace
- * belongs to the library, one per (device, stream), allocated with cudaMalloc on first use
- * and grown when a larger one is needed (after synchronising that stream). Growing is
- * refused with B2G_ERR_UNSUPPORTED while the stream is being captured, so run a call of
- * each split shape once before capturing it into a CUDA graph. */
+ * The partial sums of a tile's splits are added in split order 0..S-1 (deterministic, the
+ * same bits on every call and through every entry point) before the epilogue. On the 1-CTA
+ * tiles (128 x 64, 128 x 128, 128 x 256) with S <= 8, when the receive buffers fit in shared
+ * memory (S <= 8 on 128 x 64 and 128 x 128, S = 2 on 128 x 256), the S splits of a tile run
+ * as one thread-block cluster and each split stores its FP32 partials straight into the
+ * shared memory of the CTA that sums them (distributed shared memory): no global workspace.
+ * Otherwise (2-CTA tiles, larger S) each split writes its partial tile to a workspace and
+ * the split that finishes last sums them. That workspace belongs to the library, one per
+ * (device, stream), allocated with cudaMalloc on first use and grown when a larger one is
+ * needed (after synchronising that stream). Growing is refused with B2G_ERR_UNSUPPORTED
+ * while the stream is being captured, so run a call of each split shape once before
+ * capturing it into a CUDA graph. B2G_SPLITK_CLUSTER=0 in the environment keeps every split
+ * on the workspace path. */
 int b2g_gemm_splitk(const void* A, const void* B, void* D, const void* bias, int M, int N,
                     int K, long long lda, long long ldb, long long ldd, int b_layout, int acc,
                     int epilogue, float alpha, int tile, int stages, int group, int splits,
@@ -135,7 +142,11 @@ int b2g_gemm_splitk(const void* A, const void* B, void* D, const void* bias, int
  * library's module is loaded on the device and never need clearing later.
  * Limits: calls that can overlap on the same device (other streams, other host threads)
  * share the one array and race, so serialise them; make the first call on each device before
- * any stream capture, since it looks up the array's address (cudaGetSymbolAddress). */
+ * any stream capture, since it looks up the array's address (cudaGetSymbolAddress). The
+ * address is kept for the life of the process: after a cudaDeviceReset (or any reset of the
+ * device's primary context) the module is loaded again, maybe elsewhere, so no call of this
+ * entry point, nor of b2g_gemm_splitk (whose workspace is cached the same way), may follow a
+ * device reset in the same process. */
 int b2g_gemm_splitk_noalloc(const void* A, const void* B, void* D, const void* bias, int M,
                             int N, int K, long long lda, long long ldb, long long ldd,
                             int b_layout, int acc, int epilogue, float alpha, int tile,
@@ -234,6 +245,12 @@ int b2g_config_info(int tile, int stages, int* threads, int* regs, int* smem_byt
  * launched a GEMM yet. */
 int b2g_last_launch(int* grid, int* threads, int* tile, int* stages, int* units, int* splits);
 
+/* Thread-block cluster size of the same most recent launch: 1 for the 1-CTA kernels, 2 for
+ * the 2-CTA pair kernels, and S for a 1-CTA split-K launch whose S splits of each tile form
+ * one cluster and are summed through distributed shared memory. No counterpart in the
+ * reference (its kernel uses no clusters). B2G_ERR_ARG before any launch on this thread. */
+int b2g_last_launch_cluster(int* cluster_ctas);
+
 /* cuBLAS comparison column: exactly the reference's call (src/gemm_bench.cu:625-633):
  * cublasGemmEx(OP_T, OP_N, N, M, K, alpha, B, 16F, K, A, 16F, K, beta=0, D, 16F, N,
  * COMPUTE_32F, DEFAULT_TENSOR_OP) on `stream`, with tensor-op math mode
@@ -253,12 +270,16 @@ int b2g_bias_relu(void* D, const void* bias, int M, int N, long long ldd, float 
  * (src/device_query.cu:48-163, 199-224), which time register-resident mma.sync.
  *   kind     : 0 kind::f16 F16 in, F32 accumulate   1 kind::f16 F16 in, F16 accumulate
  *              2 kind::i8 S8 in, S32 accumulate      3 kind::f8f6f4 E4M3 in, F32 accumulate
- *   cta_group: 1 or 2 (2 = the MMA of a 2-CTA pair, M = 256)
- *   n        : UMMA N (8..256, multiple of 16 for cta_group 1 M=128)
- *   iters    : back-to-back MMAs per CTA (operands resident in shared memory,
+ *   cta_group: 1 = one CTA per SM issuing UMMA M = 128 (the 1-CTA GEMM kernels);
+ *              2 = 2-CTA clusters, the even CTA issuing the pair MMA (UMMA M = 256 over two
+ *              SMs, each holding half of A, half of B and its 128 accumulator lanes), as the
+ *              2-CTA GEMM kernels do
+ *   n        : UMMA N, 16..256 in steps of 16
+ *   iters    : back-to-back MMAs per CTA or pair (operands resident in shared memory,
  *              accumulator in TMEM, no memory traffic in the loop)
- * One CTA (or pair) per SM; clock64-timed on the device like the reference.
- * Outputs the best (fewest-cycle) SM's dense FLOP per clock per SM and its cycles. */
+ * One CTA per SM (cta_group 1) or one cluster per two SMs (cta_group 2); clock64-timed on
+ * the device like the reference. Outputs the best (fewest-cycle) CTA's or pair's dense FLOP
+ * per clock per SM (a pair's FLOP divided over its two SMs) and its cycles. */
 int b2g_probe_tcgen05(int kind, int cta_group, int n, int iters, double* flop_per_clk_sm,
                       long long* cycles);
 

@@ -331,8 +331,12 @@ void orc_tile_coord(int linear, int tiles_m, int tiles_n, int group, int* m_tile
 uint16_t orc_epilogue(float acc, int fused, float alpha, uint16_t bias_n, int has_bias) {
     float v = acc;
     if (fused) {
-        /* nvcc contracts the reference's `v *= alpha; v += bias` into one FMA (-fmad=true) */
-        v = has_bias ? fmaf(v, alpha, orc_f16_to_f32(bias_n)) : v * alpha;
+        /* `v *= alpha; v += bias`: two roundings. The reference's compiled fused and unfused
+         * kernels were checked to do exactly this on exact accumulators (tests/
+         * test_reference_gpu.py); this file is built with -ffp-contract=off so the C compiler
+         * does not fuse them either. */
+        v = v * alpha;
+        if (has_bias) v = v + orc_f16_to_f32(bias_n);
         v = v > 0.f ? v : 0.f;
     }
     return orc_f32_to_f16(v);

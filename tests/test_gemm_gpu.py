@@ -291,6 +291,22 @@ def test_probe_tcgen05(cuda):
     assert rates[2] > rates[0] * 1.5  # 8-bit kinds issue at least ~2x the 16-bit rate
 
 
+def test_probe_tcgen05_pair(cuda):
+    """cta_group::2: the pair MMA (UMMA M = 256 over two SMs) of the 2-CTA GEMM kernels,
+    FLOP per clock per SM comparable with the one-SM rate, for every kind."""
+    one, _ = b2g.probe_tcgen05(0, 1, 256, 2048)
+    for kind in (0, 1, 2, 3):
+        fl, cyc = b2g.probe_tcgen05(kind, 2, 256, 2048)
+        print(f"pair probe kind {kind} ({b2g.PROBE_KINDS[kind]}): {fl:.1f} FLOP/clk/SM, "
+              f"{cyc} cycles (one-SM kind 0: {one:.1f})")
+        assert cyc > 0
+        lo = 0.8 * one * (2 if kind >= 2 else 1)
+        assert lo < fl < 1.25 * one * (2 if kind >= 2 else 1), (kind, fl, one)
+    with pytest.raises(b2g.B2GError) as e:
+        b2g.probe_tcgen05(0, 3, 256, 16)
+    assert e.value.code == b2g.ERR_ARG
+
+
 def test_probe_hbm(cuda):
     torch = cuda
     n = 1 << 30

@@ -43,7 +43,7 @@ def _worker(rank, world, port, result_q):
     import torch.distributed as dist
 
     import oracle as O
-    from b2g.shard import gather_panels, max_over_ranks, panel
+    from b2g.shard import gather_panels, max_over_ranks, mean_over_ranks, panel
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -56,10 +56,11 @@ def _worker(rank, world, port, result_q):
         D_panel = torch.from_numpy(O.gemm_f64(A_panel, B))
         full = gather_panels(D_panel, M // world)
         slowest = max_over_ranks(10.0 + rank)
+        mean = mean_over_ranks(1000.0 + 10.0 * rank)
         if rank == 0:
             A = O.fill_uniform((M, K), 3, 0)
             ref = O.gemm_f64(A, B)
-            result_q.put((float(np.max(np.abs(full.numpy() - ref))), slowest))
+            result_q.put((float(np.max(np.abs(full.numpy() - ref))), slowest, mean))
     finally:
         dist.destroy_process_group()
 
@@ -76,10 +77,31 @@ def test_two_gloo_ranks_shard_and_gather():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0, f"rank exited with {p.exitcode}"
-    err, slowest = q.get()
+    err, slowest, mean = q.get()
     assert err == 0.0  # row panels of an FP64 product are exactly the full product's rows
     assert slowest == 11.0  # max over ranks
+    assert mean == 1005.0  # mean over ranks (e.g. the SM clock each rank's kernel ran at)
 
 
 def test_single_process_helpers():
     assert max_over_ranks(3.5) == 3.5
+
+
+def test_strong_scaling_summary():
+    """The `sharded` object's arithmetic: speed-up and efficiency against the same run's
+    1-GPU time, the clock-normalised speed-up, and what bounds the fused GEMM + all-gather."""
+    from b2g.shard import strong_scaling
+
+    flop = 2.0 * 32768 * 32768 * 8192
+    s = strong_scaling(flop, 1.5, 8, ms_1=12.0, mhz_n=1350.0, mhz_1=1170.0,
+                       gather_bytes_per_gpu=7 * 4096 * 32768 * 2, link_gbs=770.0,
+                       gemm_peak_tflops=1376.0)
+    assert s["speedup_vs_1gpu"] == 8.0 and s["efficiency"] == 1.0
+    assert abs(s["speedup_clock_normalised"] - 8.0 * 1170.0 / 1350.0) < 1e-12
+    assert abs(s["tflops"] - flop / 1.5e-3 / 1e12) < 1e-6
+    fb = s["fused_step_bound"]
+    assert fb["limit"] == "all-gather (NVLink)"  # 1.88 GB at 770 GB/s > 2.2 TFLOP at peak
+    assert abs(fb["gather_ms_at_link"] - 7 * 4096 * 32768 * 2 / 770e9 * 1e3) < 1e-9
+    assert fb["roofline_ms"] == fb["gather_ms_at_link"]
+    one = strong_scaling(flop, 12.0, 1)
+    assert "efficiency" not in one and "fused_step_bound" not in one

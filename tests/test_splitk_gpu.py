@@ -60,13 +60,16 @@ def test_split_result_is_deterministic_and_close_to_unsplit(cuda):
                                      (512, False)])
 def test_skinny_decode_auto_split(cuda, M, split):
     """The reference's Phase 6 shapes (N = K = 4096): b2g_gemm splits K automatically when
-    128 x 128 tiles leave most SMs idle (M <= 128 here); 2-CTA pair tiles (M = 512) are
-    never split automatically."""
+    128 x 128 tiles leave most SMs idle (M <= 128 here), each tile's splits forming one
+    cluster reduced through distributed shared memory; 2-CTA pair tiles (M = 512) are never
+    split automatically."""
     N = K = 4096
     A, B, _ = inputs(M, N, K, seed=33)
     D = run(cuda, A, B)
     launch = b2g.last_launch()
     assert (launch["splits"] > 1) == split, launch
+    if split:
+        assert launch["cluster"] == launch["splits"] and launch["grid"] == launch["units"]
     rows = sample_rows(M, 32)
     frob, maxrel = check_rows(A, B, D, rows)
     assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
@@ -115,3 +118,64 @@ def test_workspace_growth_and_streams(cuda):
     for A, B, dA, dB, dD, st in jobs:
         frob, maxrel = check_rows(A, B, to_host(dD), sample_rows(128, 16))
         assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+def _split_pair(torch, A, B, bias, splits, tile, kw, lda):
+    """The same split GEMM through b2g_gemm_splitk and b2g_gemm_splitk_noalloc (which always
+    reduces through its static workspace); returns both outputs and the first's launch."""
+    M, N = A.shape[0], B.shape[0]
+    dA, dB = to_dev(torch, A, lda), to_dev(torch, B, lda)
+    dbias = to_dev(torch, bias) if bias is not None else None
+    outs, launch = [], None
+    for fn in (b2g.gemm, b2g.gemm_noalloc):
+        dD = torch.full((M, N), float("nan"), dtype=torch.float16, device="cuda")
+        fn(dA, dB, dD, dbias, tile=tile, splits=splits, **kw)
+        b2g.sync_status()
+        if launch is None:
+            launch = b2g.last_launch()
+        outs.append(to_host(dD))
+    return outs, launch
+
+
+@pytest.mark.parametrize("tile,splits", [(b2g.TILE_128x128, 2), (b2g.TILE_128x128, 3),
+                                         (b2g.TILE_128x128, 4), (b2g.TILE_128x128, 8),
+                                         (b2g.TILE_128x64, 4), (b2g.TILE_128x64, 8),
+                                         (b2g.TILE_128x256, 2)])
+@pytest.mark.parametrize("fused", [False, True])
+def test_cluster_reduction_matches_workspace(cuda, tile, splits, fused):
+    """Split-K on 1-CTA tiles runs each tile's splits as one cluster and sums the partials
+    in the shared memory of the owning CTA (st.async into its receive slots); the
+    no-allocation entry point sums the same partials through its workspace. Same operations
+    in the same split order: identical bits. Ragged M, N and K; uneven K shares."""
+    M, N, K = 300, 520, 2000
+    A, B, bias = inputs(M, N, K, seed=35)
+    kw = dict(epilogue=b2g.EPI_BIAS_RELU, alpha=0.5) if fused else {}
+    (Dc, Dw), launch = _split_pair(cuda, A, B, bias if fused else None, splits, tile, kw, K)
+    assert launch["cluster"] == splits and launch["grid"] == launch["units"], launch
+    assert np.array_equal(Dc, Dw)
+    frob, maxrel = check_rows(A, B, Dc, list(range(M)), bias=bias if fused else None,
+                              alpha=kw.get("alpha", 1.0), epilogue=fused)
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
+
+
+@pytest.mark.parametrize("M", [1, 8, 128])
+def test_cluster_reduction_decode_is_deterministic(cuda, M):
+    """The decode shapes (N = K = 4096, automatic split): three calls give the same bits, and
+    the same bits as the workspace reduction of the no-allocation entry point."""
+    torch = cuda
+    A, B, _ = inputs(M, 4096, 4096, seed=36)
+    outs = [run(torch, A, B) for _ in range(3)]
+    assert all(np.array_equal(outs[0], o) for o in outs[1:])
+    splits = b2g.last_launch()["splits"]
+    (_, Dw), _ = _split_pair(torch, A, B, None, splits, b2g.TILE_128x128, {}, 4096)
+    assert np.array_equal(outs[0], Dw)
+
+
+def test_cluster_reduction_unaligned_output(cuda):
+    """Owners of pieces write D through the plain-store path when TMA cannot (ldd = N + 3)."""
+    M, N, K = 200, 300, 1024
+    A, B, _ = inputs(M, N, K, seed=37)
+    D = run(cuda, A, B, tile=b2g.TILE_128x128, splits=4, ldd=N + 3)
+    assert b2g.last_launch()["cluster"] == 4
+    frob, maxrel = check_rows(A, B, D, list(range(M)))
+    assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)

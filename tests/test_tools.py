@@ -1,13 +1,17 @@
-"""CPU tests of the experiment tools that port the reference's sweep.ps1 and soak.ps1:
-b2g.sweep (configuration sweep -> CSV with the reference's columns) and b2g.soak (SOAK
-windows + nvidia-smi telemetry). A fake gemm_bench prints lines in the real CLI's formats."""
+"""CPU tests of the experiment tools that port the reference's sweep.ps1, soak.ps1 and
+profile.ps1: b2g.sweep (configuration sweep -> CSV with the reference's columns), b2g.soak
+(SOAK windows + nvidia-smi telemetry) and b2g.profile (ncu passes + the dense-occupancy
+check). A fake gemm_bench prints lines in the real CLI's formats; a stand-in runner plays
+ncu."""
 import csv
 import os
 import stat
 import sys
 import textwrap
 
-from b2g import soak, sweep
+import pytest
+
+from b2g import profile, soak, sweep
 
 # header of the reference's data/sweep_results.csv, in order
 REFERENCE_SWEEP_HEADER = ["M", "N", "K", "tile", "cta", "layout", "stages", "threads", "regs",
@@ -126,3 +130,100 @@ def test_soak_end_to_end_with_a_fake_cli(tmp_path):
     assert len(soak.throughput_rows(open(thr).readlines())) == 9
     assert "throughput_first_last" in s
     assert os.path.getsize(thr) > 0
+
+
+def test_soak_names_the_gpu_by_uuid(tmp_path, monkeypatch):
+    """The soaked GPU and the sampled GPU are the same one: the CLI is pinned to the device's
+    UUID through CUDA_VISIBLE_DEVICES and nvidia-smi is asked about that UUID."""
+    seen = {}
+    monkeypatch.setattr(soak, "device_uuid", lambda i: f"GPU-fake-{i}")
+
+    def fake_sample(ident):
+        seen.setdefault("ident", ident)
+        return None
+
+    monkeypatch.setattr(soak, "sample", fake_sample)
+    real_popen = soak.subprocess.Popen
+
+    def spy_popen(args, **kw):
+        seen["cvd"] = kw.get("env", {}).get("CUDA_VISIBLE_DEVICES")
+        return real_popen(args, **kw)
+
+    monkeypatch.setattr(soak.subprocess, "Popen", spy_popen)
+    s = soak.run(1, 2.0, 64, 64, 64, -1, 0, 2, 0, "f32", "uuid", str(tmp_path / "data"), 20,
+                 _fake_exe(tmp_path), gpu=3, log=lambda *_: None)
+    assert s["returncode"] == 0
+    assert seen["cvd"] == "GPU-fake-3" and seen["ident"] == "GPU-fake-3"
+
+
+# ---------------------------------------------------------------------------------------
+# b2g.profile: port of scripts/profile.ps1
+# ---------------------------------------------------------------------------------------
+
+_FAKE_NCU_CSV = '''==PROF== Connected to process 1234
+M N K ...
+"ID","Process ID","Process Name","Host Name","Kernel Name","Context","Stream","Block Size","Grid Size","Device","CC","Section Name","Metric Name","Metric Unit","Metric Value"
+"0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","sm__cycles_elapsed.avg","cycle","153,016"
+"0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","sm__cycles_active.avg","cycle","134,428"
+"0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","gpu__time_duration.sum","ns","96,400"
+"0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","dram__bytes_read.sum","byte","69,190,000"
+"0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","dram__bytes_write.sum","byte","17,440,000"
+"0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","sm__ops_path_tensor_op_hmma_src_fp16_dst_fp32_sparsity_off.sum","","137,438,953,472"
+'''
+
+
+def test_profile_commands_keep_clocks_and_bound_the_capture():
+    args = profile.app_args(4096, 4096, 4096, skip=3)
+    assert args[args.index("--warmup") + 1] == "5" and args[args.index("--iters") + 1] == "1"
+    assert "--noref" in args  # our kernel only; --cublas keeps the cuBLAS column instead
+    assert "--noref" not in profile.app_args(64, 64, 64, cublas=True)
+    plain, sec, met = profile.commands("exe", args, "regex:gemm_sm100", 3, "out/x")
+    for c in (sec, met):
+        assert c[:3] == ["ncu", "--clock-control", "none"]
+        assert c[c.index("-c") + 1] == "1" and c[c.index("-s") + 1] == "3"
+        assert c[c.index("-k") + 1] == "regex:gemm_sm100"
+        assert c[-len(plain):] == plain
+    assert "--set" not in sec and sec.count("--section") == len(profile.SECTIONS)
+    _, full, _ = profile.commands("exe", args, "k", 3, "out/x", full=True)
+    assert full[full.index("--set") + 1] == "full"
+    _, _, nv = profile.commands("exe", args, "k", 3, "out/x", nvlink=True)
+    assert "nvltx__bytes_data_user.sum" in nv[nv.index("--metrics") + 1]
+
+
+def test_profile_parse_and_dense_occupancy():
+    m = profile.parse_metrics_csv(_FAKE_NCU_CSV)
+    assert m["sm__cycles_elapsed.avg"] == 153016.0 and m["dram__bytes_read.sum"] == 69.19e6
+    s = profile.summarize(m, 4096, 4096, 4096, fpc=8187.0, sms=148)
+    busy = 2.0 * 4096 ** 3 / (8187.0 * 148)  # the reference's hand calculation
+    assert abs(s["busy_tensor_cycles"] - busy) < 1e-6
+    assert abs(s["dense_occupancy_elapsed"] - busy / 153016.0) < 1e-12
+    assert abs(s["dense_occupancy_active"] - busy / 134428.0) < 1e-12
+    assert s["tensor_ops_vs_2mnk"] == 1.0  # the counter counts exactly 2MNK
+    assert abs(s["dram_bytes"] - 86.63e6) < 1
+    assert abs(s["tflops_under_ncu"] - 2.0 * 4096 ** 3 / 96.4e-6 / 1e12) < 1e-6
+    assert profile.parse_metrics_csv("no csv here") == {}
+
+
+def test_profile_run_with_a_stand_in_ncu(tmp_path):
+    """The whole flow with a fake runner: plain run first, then the two ncu passes, then
+    the markdown summary; a failing plain run stops before any ncu command."""
+    calls = []
+
+    class R:
+        def __init__(self, rc, out=""):
+            self.returncode, self.stdout, self.stderr = rc, out, ""
+
+    def runner(cmd, **_):
+        calls.append(cmd)
+        return R(0, _FAKE_NCU_CSV if "--metrics" in cmd else "ok")
+
+    out = profile.run(4096, 4096, 4096, "t", str(tmp_path), exe="gb", fpc=8187.0, sms=148,
+                      log=lambda *_: None, runner=runner)
+    assert calls[0][0] == "gb" and calls[1][0] == "ncu" and "--metrics" in calls[2]
+    md = open(out["markdown"]).read()
+    assert "dense_occupancy_elapsed" in md and "--clock-control none" in md
+    calls.clear()
+    with pytest.raises(RuntimeError):
+        profile.run(64, 64, 64, "u", str(tmp_path), exe="gb", log=lambda *_: None,
+                    runner=lambda cmd, **_: (calls.append(cmd), R(1))[1])
+    assert len(calls) == 1  # no ncu after a failed plain run
