@@ -92,12 +92,16 @@ def app_args(M, N, K, tile=-1, stages=0, group=0, acc="f32", splits=-1, skip=3, 
     return a + list(extra)
 
 
-def commands(exe, args, kernel, skip, rep_path, full=False, nvlink=False):
+def commands(exe, args, kernel, skip, rep_path, full=False, nvlink=False, kernel_base=None):
     """(plain run, section pass, metrics pass) command lines. Every ncu command keeps the
-    GPU clocks alone (--clock-control none) and captures one launch of one kernel."""
+    GPU clocks alone (--clock-control none) and captures one launch of one kernel.
+    kernel_base="demangled" matches `kernel` against the full name with template arguments
+    (e.g. to pick the fused all-gather instantiation `gemm_sm100_2cta<256, true>`)."""
     plain = [exe] + list(args)
-    base = ["ncu", "--clock-control", "none", "--target-processes", "all", "-k", kernel,
-            "-s", str(skip), "-c", "1"]
+    base = ["ncu", "--clock-control", "none", "--target-processes", "all"]
+    if kernel_base:
+        base += ["--kernel-name-base", kernel_base]
+    base += ["-k", kernel, "-s", str(skip), "-c", "1"]
     sections = ["--set", "full"] if full else [x for s in SECTIONS for x in ("--section", s)]
     section_cmd = base + sections + ["--force-overwrite", "-o", rep_path] + plain
     metrics = METRICS + (NVLINK_METRICS if nvlink else [])
@@ -185,13 +189,13 @@ def markdown(tag, cmds, m, s, M, N, K, fpc, sms) -> str:
 def run(M, N, K, tag, out_dir, exe=DEFAULT_EXE, tile=-1, stages=0, group=0, acc="f32",
         splits=-1, skip=3, seed=1, full=False, cublas=False, nvlink=False, kernel=None,
         metrics_only=False, fpc=None, sms=None, log=print, runner=subprocess.run,
-        b_layout="nk", extra=()):
+        b_layout="nk", extra=(), kernel_base=None):
     os.makedirs(out_dir, exist_ok=True)
     kernel = kernel or ("regex:nvjet" if cublas else "regex:gemm_sm100")
     args = app_args(M, N, K, tile, stages, group, acc, splits, skip, seed, cublas, extra,
                     b_layout)
     rep = os.path.join(out_dir, tag)
-    cmds = commands(exe, args, kernel, skip, rep, full, nvlink)
+    cmds = commands(exe, args, kernel, skip, rep, full, nvlink, kernel_base)
     plain, section_cmd, metric_cmd = cmds
     log("==> plain run: " + " ".join(plain))
     r = runner(plain, capture_output=True, text=True)
@@ -251,6 +255,8 @@ def main(argv=None):
     p.add_argument("--out-dir", default="gpurun_out")
     p.add_argument("--exe", default=DEFAULT_EXE)
     p.add_argument("--kernel", default=None, help="ncu -k filter (default regex:gemm_sm100)")
+    p.add_argument("--kernel-base", default=None, choices=("function", "demangled", "mangled"),
+                   help="ncu --kernel-name-base for the -k filter")
     p.add_argument("--full", action="store_true", help="--set full instead of the sections")
     p.add_argument("--cublas", action="store_true", help="profile the cuBLAS column's kernel")
     p.add_argument("--nvlink", action="store_true", help="add NVLink tx/rx byte counters")
@@ -267,7 +273,7 @@ def main(argv=None):
     extra = (["--gpus", str(a.gpus)] if a.gpus > 1 else []) + (["--allgather"] if a.allgather else [])
     run(a.m, a.n, a.k, a.tag, a.out_dir, a.exe, a.tile, a.stages, a.group, a.acc, a.splits,
         a.skip, a.seed, a.full, a.cublas, a.nvlink, a.kernel, a.metrics_only, fpc, sms,
-        b_layout=a.b_layout, extra=extra)
+        b_layout=a.b_layout, extra=extra, kernel_base=a.kernel_base)
     return 0
 
 

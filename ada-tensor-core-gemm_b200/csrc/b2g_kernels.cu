@@ -149,12 +149,14 @@ const void* kernel_ptr(int tile, bool peers = false) {
 // at K >= 1024 with 24-32 boxes; stores in flight per warp are not the limit).
 int epi_boxes_for(int num_kb) { return num_kb <= 4 ? 16 : 8; }
 
-size_t smem_needed(int tile, int stages, int epi_boxes = 8) {
+// `a_rows`: rows of A per stage of the 1-CTA kernels (128, or M rounded up to 8 when all of
+// M fits one tile); the 2-CTA and swapped-operand kernels always stage full boxes.
+size_t smem_needed(int tile, int stages, int epi_boxes = 8, int a_rows = kBM) {
     const uint32_t epi = (uint32_t)epi_boxes * kEpiBoxBytes;
     switch (tile) {
-        case B2G_TILE_128x128: return gemm_smem_bytes<128>(stages, epi);
-        case B2G_TILE_128x256: return gemm_smem_bytes<256>(stages, epi);
-        case B2G_TILE_128x64: return gemm_smem_bytes<64>(stages, epi);
+        case B2G_TILE_128x128: return gemm_smem_bytes<128>(stages, epi, a_rows);
+        case B2G_TILE_128x256: return gemm_smem_bytes<256>(stages, epi, a_rows);
+        case B2G_TILE_128x64: return gemm_smem_bytes<64>(stages, epi, a_rows);
         case B2G_TILE_256x512_2SM: return gemm2_smem_bytes<512>(stages, epi);
         case B2G_TILE_SWAP_AB: return gemm_swap_smem_bytes<64>(stages);
         case B2G_TILE_256x128_2SM: return gemm2_smem_bytes<128>(stages, epi);
@@ -166,13 +168,15 @@ size_t smem_needed(int tile, int stages, int epi_boxes = 8) {
 // one GEMM CTA is resident per SM. Every GEMM CTA allocates 2 x BN TMEM columns; two
 // co-resident CTAs of 2-CTA clusters could otherwise each hold the TMEM the other's peer
 // waits for.
-size_t smem_request(int tile, int stages, const DeviceInfo& di, int epi_boxes = 8) {
-    return std::max(smem_needed(tile, stages, epi_boxes), (size_t)di.smem_per_sm / 2 + 1024);
+size_t smem_request(int tile, int stages, const DeviceInfo& di, int epi_boxes = 8,
+                    int a_rows = kBM) {
+    return std::max(smem_needed(tile, stages, epi_boxes, a_rows),
+                    (size_t)di.smem_per_sm / 2 + 1024);
 }
 
-int max_stages_for(int tile, int smem_optin, int epi_boxes = 8) {
+int max_stages_for(int tile, int smem_optin, int epi_boxes = 8, int a_rows = kBM) {
     int s = kMaxStages;
-    while (s > 2 && smem_needed(tile, s, epi_boxes) > (size_t)smem_optin) --s;
+    while (s > 2 && smem_needed(tile, s, epi_boxes, a_rows) > (size_t)smem_optin) --s;
     return s;
 }
 
@@ -764,12 +768,15 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     }
     const TileGeom g = geom(tile);
     const int epi_boxes = epi_boxes_for((K + kBK - 1) / kBK);
-    const int max_st = max_stages_for(tile, di.smem_optin, epi_boxes);
+    // A box rows: all of M in one 1-CTA tile -> load (and stage) only round_up(M, 8) rows per
+    // k-block
+    const int a_rows = (g.ctas == 1 && M <= g.bm) ? std::min(g.box_a, (M + 7) / 8 * 8) : g.box_a;
+    const int max_st = max_stages_for(tile, di.smem_optin, epi_boxes, a_rows);
     if (stages == 0) stages = max_st;
-    if (smem_needed(tile, stages, epi_boxes) > (size_t)di.smem_optin)
+    if (smem_needed(tile, stages, epi_boxes, a_rows) > (size_t)di.smem_optin)
         return fail(B2G_ERR_SMEM, "smem over per-block opt-in limit: %zu > %d (tile %d, %d stages)",
-                    smem_needed(tile, stages, epi_boxes), di.smem_optin, tile, stages);
-    size_t smem = smem_request(tile, stages, di, epi_boxes);
+                    smem_needed(tile, stages, epi_boxes, a_rows), di.smem_optin, tile, stages);
+    size_t smem = smem_request(tile, stages, di, epi_boxes, a_rows);
 
     GemmParams p{};
     p.M = M;
@@ -781,11 +788,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     if (nt > 0x7fffffffLL) return fail(B2G_ERR_ARG, "too many tiles (%lld)", nt);
     p.num_tiles = (int)nt;
     p.num_kb = (K + kBK - 1) / kBK;
-    // A box rows: all of M in one 1-CTA tile -> load only round_up(M, 8) rows per k-block
-    const uint32_t a_rows = (g.ctas == 1 && p.tiles_m == 1)
-                                ? std::min<uint32_t>(g.box_a, (uint32_t)((M + 7) / 8 * 8))
-                                : g.box_a;
-    p.stage_tx = (a_rows + g.box_b) * kBK * 2;
+    p.stage_tx = (uint32_t)(a_rows + g.box_b) * kBK * 2;
+    p.a_stage_bytes = (uint32_t)a_rows * kBK * 2;
     p.group = group > 0 ? group : auto_group(g, p.tiles_m, K);
     p.stages = stages;
     const bool b_mn = b_layout == B2G_B_KN;
@@ -834,8 +838,9 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
         const uint32_t recv = csplit_recv_bytes(g.bn, splits);
         int st = stages;
         if (stages_arg == 0)
-            while (st > 2 && smem_needed(tile, st, epi_boxes) + recv > (size_t)di.smem_optin) --st;
-        const size_t need = smem_needed(tile, st, epi_boxes) + recv;
+            while (st > 2 && smem_needed(tile, st, epi_boxes, a_rows) + recv > (size_t)di.smem_optin)
+                --st;
+        const size_t need = smem_needed(tile, st, epi_boxes, a_rows) + recv;
         const size_t req = std::max(need, (size_t)di.smem_per_sm / 2 + 1024);
         if (recv <= kCsMaxRecvBytes && need <= (size_t)di.smem_optin) {
             if (int rc = ensure_kernel_attrs(tile, di, npeer > 0)) return rc;
@@ -878,7 +883,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     p.timeout_ns = wait_timeout_ns();
 
     CUtensorMap tmA, tmB;
-    if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK, a_rows, "A"))
+    if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK,
+                           (uint32_t)a_rows, "A"))
         return rc;
     // B: N x K in 128-row x 64-k boxes, or K x N (MN-major) either in one 3D box of all the
     // 64-column groups a CTA loads per stage (N % 64 == 0) or in 64-column x 64-k-row boxes

@@ -76,9 +76,13 @@ struct GemmParams {
     int csplit;
     uint32_t recv_bytes;
     // 1-CTA kernels: bytes one stage's two TMA loads deliver. When all of M fits one tile the
-    // A box is only round_up(M, 8) rows high; the stale shared-memory rows below it feed
+    // A box is only round_up(M, 8) rows high and the ring packs stages of a_stage_bytes of A
+    // then B, so a decode-shaped GEMM fits several times more B stages in flight; the MMA still
+    // reads 128 rows of A, the rows past the box coming from whatever follows in shared memory
+    // (never past the allocation: the epilogue staging follows the ring), and they feed only
     // accumulator rows >= M, which the epilogue never stores.
     uint32_t stage_tx;
+    uint32_t a_stage_bytes;  // A rows of one stage x 128 B (16 KiB for full 128-row tiles)
     // Epilogue staging: boxes of 4 KiB per epilogue warp (1..4), used in turn; the staging
     // area is epilogue warps x epi_bufs x 4 KiB, after the operand ring.
     int epi_bufs;
@@ -156,10 +160,12 @@ struct SmemCtl {
 };
 
 // Dynamic shared memory: [align slack][stages x (A, B)][epilogue staging][cluster split-K
-// receive slots, if any][SmemCtl]
+// receive slots, if any][SmemCtl]. A stage is a_rows x 128 B of A (a_rows = 128, or M rounded
+// up to 8 when all of M fits one tile) followed by BN x 128 B of B.
 template <int BN>
-constexpr size_t gemm_smem_bytes(int stages, uint32_t epi) {
-    return 1024 /* alignment slack */ + (size_t)stages * TileTraits<BN>::kStageBytes + epi +
+constexpr size_t gemm_smem_bytes(int stages, uint32_t epi, int a_rows = kBM) {
+    return 1024 /* alignment slack */ +
+           (size_t)stages * ((uint32_t)a_rows * kBK * 2 + TileTraits<BN>::kBStageBytes) + epi +
            sizeof(SmemCtl);
 }
 
@@ -699,6 +705,7 @@ __device__ __forceinline__ void csplit_epilogue(const GemmParams& p, const EpiSc
     int nchunks = nch;
     const int in_n = (e.N - n_first + 63) / 64;
     if (in_n < nchunks) nchunks = in_n;
+    if (threadIdx.x == 128) B2G_MARK(6);
     if (row0 < e.M) {
 #pragma unroll 1
         for (int c = c_first; c < nchunks; c += e.c_step) {
@@ -715,11 +722,13 @@ __device__ __forceinline__ void csplit_epilogue(const GemmParams& p, const EpiSc
             const int i = q * nch + c, owner = i % S, k = i / S;
             if (owner != s) continue;
             const uint32_t rb = rbar0 + 8u * (uint32_t)k;
+            if (threadIdx.x == 128) B2G_MARK(7);
             if (lane == 0) mbar_arrive_expect_tx(rb, (uint32_t)(S - 1) * kCsPieceBytes);
             __syncwarp();
             B2G_TIC(t_rv);
             if (!mbar_wait_warp<true>(rb, 0, w)) break;
             B2G_TOC64(14, t_rv);
+            if (threadIdx.x == 128) B2G_MARK(8);
             const uint32_t slots = recv0 + (uint32_t)(k * (S - 1)) * kCsPieceBytes;
             if (epi)
                 csplit_reduce<true, PEERS>(p, e, tmD, trow, c, s, slots, row0, n_first, stage0,
@@ -730,6 +739,7 @@ __device__ __forceinline__ void csplit_epilogue(const GemmParams& p, const EpiSc
         }
     }
     release();
+    if (threadIdx.x == 128) B2G_MARK(9);
 }
 
 // PEERS: the fused all-gather instantiation (every staged box of D also goes to p.peers).
@@ -741,16 +751,19 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     using TT = TileTraits<BN>;
     clock_mark(0);
     B2G_TIC(t_life);
+    if (threadIdx.x == 0) B2G_MARK(0);
     extern __shared__ uint8_t smem_dyn[];
     // stage buffers must be 1024-byte aligned (128-byte swizzle atoms, base offset 0)
     const uint32_t raw = smem_u32(smem_dyn);
     const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
+    // stage s: A at sA + s * stride, B at sB + s * stride
+    const uint32_t stride = p.a_stage_bytes + TT::kBStageBytes;
     const uint32_t sA = raw + pad;
-    const uint32_t sB = sA + (uint32_t)p.stages * kAStageBytes;
-    const uint32_t sEpi = raw + pad + (uint32_t)p.stages * TT::kStageBytes;
+    const uint32_t sB = sA + p.a_stage_bytes;
+    const uint32_t sEpi = raw + pad + (uint32_t)p.stages * stride;
     const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
     const uint32_t sRecv = sEpi + epi_bytes(epi_warps, p.epi_bufs);
-    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * TT::kStageBytes +
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * stride +
                                               epi_bytes(epi_warps, p.epi_bufs) + p.recv_bytes);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -790,12 +803,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     // cluster split-K: every CTA's receive barriers exist before any peer stores into them
     if (p.csplit) cluster_sync();
     tc_fence_after();
+    if (threadIdx.x == 0) B2G_MARK(1);
     const uint32_t tmem_base = ctl->tmem_base;
     volatile int* abort_flag = &ctl->abort;
     volatile int* no_abort = &ctl->never;
     // everything above overlapped the previous kernel; global memory only from here on
     grid_dep_wait();
     grid_dep_launch();
+    if (threadIdx.x == 0) B2G_MARK(2);
 
     if (warp == 0) {
         if (lane == 0) {
@@ -820,8 +835,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     B2G_TOC(0, t_empty);
                     const uint32_t fb = full0 + 8 * stage;
                     mbar_arrive_expect_tx(fb, p.stage_tx);
-                    tma_load_2d(sA + stage * kAStageBytes, &tmA, fb, kb * kBK, m0);
-                    const uint32_t sBs = sB + stage * TT::kBStageBytes;
+                    tma_load_2d(sA + stage * stride, &tmA, fb, kb * kBK, m0);
+                    const uint32_t sBs = sB + stage * stride;
                     if (p.b_kn3d) {
                         // B is K x N: the BN / 64 boxes of 64 columns x 64 k-rows in one load
                         tma_load_3d(sBs, &tmB, fb, 0, kb * kBK, n0 >> 6);
@@ -834,6 +849,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     } else {
                         tma_load_2d(sBs, &tmB, fb, kb * kBK, n0);
                     }
+                    if (issued == 0) B2G_MARK(3);
                     ++issued;
                     if (++stage == p.stages) {
                         stage = 0;
@@ -841,6 +857,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     }
                 }
             }
+            B2G_MARK(11);
             if (!ok) {
                 // unwind: wait (bounded) until the loads still in flight have landed
                 const WaitCtx wd{p.timeout_ns, no_abort, kErrWaitDrain};
@@ -866,7 +883,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             const uint64_t adesc0 = sdesc_sw128(sA, 16, 1024);
             const uint64_t bdesc0 = b_desc0(sB, p.b_mn_major);
             const uint32_t bk = b_kstep(p.b_mn_major);
-            constexpr uint32_t kAStep = kAStageBytes >> 4, kBStep = TT::kBStageBytes >> 4;
+            const uint32_t kAStep = stride >> 4, kBStep = stride >> 4;  // descriptor units
             const uint32_t idesc = p.idesc;
             int stage = 0;
             uint32_t phase = 0;
@@ -894,6 +911,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     }
                     if (lane == 0) B2G_TOC(1, t_full);
                     if (lane == 0) B2G_COUNT(6, 1);
+                    if (lane == 0 && kb == kb0 && it == 0) B2G_MARK(4);
                     const uint64_t ad = adesc0 + (uint64_t)((uint32_t)stage * kAStep);
                     const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kBStep);
                     if (elect_one()) {
@@ -912,6 +930,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 if (!ok) break;
                 if (elect_one()) mma_commit(tfull0 + 8 * buf);  // accumulator `buf` is final
                 __syncwarp();
+                if (lane == 0 && it == 0) B2G_MARK(5);
             }
             // drain: nothing may still read shared memory or write TMEM at teardown
             const WaitCtx wd{p.timeout_ns, no_abort, kErrWaitDrain};
@@ -969,6 +988,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     __syncthreads();
     // cluster split-K: no CTA leaves while a peer may still store into its receive slots
     if (p.csplit) cluster_sync();
+    if (threadIdx.x == 0) B2G_MARK(10);
     if (warp == 1) {
         __syncwarp();
         tc_fence_after();
