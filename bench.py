@@ -283,23 +283,38 @@ NCCL_LOG = "/tmp/b2g_nccl_{pid}.log"
 
 
 def nccl_log_setup():
-    """NCCL's communicator-init log goes to a per-process file (not stdout, which carries
-    the JSON line); rank 0 quotes its `Init COMPLETE` line (rank, nranks) in the output."""
-    if "NCCL_DEBUG" not in os.environ:
-        os.environ["NCCL_DEBUG"] = "INFO"
-        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", NCCL_LOG.format(pid=os.getpid()))
+    """NCCL's communicator-init log (NCCL_DEBUG=INFO, subsystem INIT) goes to a per-process
+    file, not to stdout, which carries the JSON line; rank 0 quotes its `Init COMPLETE` lines
+    (rank, nranks) in the output. Set before the first NCCL call of the process."""
+    os.environ["NCCL_DEBUG"] = "INFO"
+    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+    os.environ["NCCL_DEBUG_FILE"] = NCCL_LOG.format(pid=os.getpid())
 
 
-def nccl_log_summary():
+def nccl_log_summary(world):
+    """The communicator as NCCL and torch report it (read after the process group is gone,
+    so NCCL has flushed its log)."""
+    import torch
+    import torch.distributed as dist
+
+    out = {"ranks_torch": world, "backend": "nccl"}
+    try:
+        v = torch.cuda.nccl.version()
+        out["nccl_version_torch"] = ".".join(str(x) for x in v) if isinstance(v, tuple) else v
+    except Exception:  # noqa: BLE001
+        pass
     path = os.environ.get("NCCL_DEBUG_FILE", "")
-    if not path or not os.path.exists(path):
-        return None
-    with open(path, errors="replace") as fh:
-        lines = fh.read().splitlines()
-    done = [ln.split("NCCL INFO", 1)[-1].strip() for ln in lines if "Init COMPLETE" in ln]
-    ver = [ln.split("NCCL INFO", 1)[-1].strip() for ln in lines if "NCCL version" in ln]
-    return {"version": ver[0] if ver else None, "init_complete": done[:4]}
+    if path and os.path.exists(path):
+        with open(path, errors="replace") as fh:
+            lines = fh.read().splitlines()
+        out["init_complete"] = [ln.split("NCCL INFO", 1)[-1].strip() for ln in lines
+                                if "Init COMPLETE" in ln][:4]
+        ver = [ln.split("NCCL INFO", 1)[-1].strip() for ln in lines if "NCCL version" in ln]
+        out["version_line"] = ver[0] if ver else None
+        out["log_file"] = path
+    else:
+        out["log_file"] = None
+    return out
 
 
 def sharded_leg(args, world, rank, dev, stream, sptr, barrier):
@@ -579,7 +594,6 @@ def run_ours(args):
         del sets
         torch.cuda.empty_cache()
         sharded = sharded_leg(args, world, rank, dev, stream, sptr, barrier)
-    nccl = nccl_log_summary() if world > 1 and rank == 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -591,6 +605,7 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return
+    nccl = nccl_log_summary(world) if world > 1 else None
 
     peaks, peak_src = measured_peaks()
     per_launch_ms = ms / args.steps

@@ -137,21 +137,29 @@ def _split_pair(torch, A, B, bias, splits, tile, kw, lda):
     return outs, launch
 
 
+PAIR_TILES = (b2g.TILE_256x256_2SM, b2g.TILE_256x128_2SM)
+
+
 @pytest.mark.parametrize("tile,splits", [(b2g.TILE_128x128, 2), (b2g.TILE_128x128, 3),
                                          (b2g.TILE_128x128, 4), (b2g.TILE_128x128, 8),
                                          (b2g.TILE_128x64, 4), (b2g.TILE_128x64, 8),
-                                         (b2g.TILE_128x256, 2)])
+                                         (b2g.TILE_128x256, 2), (b2g.TILE_128x256, 4),
+                                         (b2g.TILE_256x256_2SM, 2), (b2g.TILE_256x256_2SM, 3),
+                                         (b2g.TILE_256x256_2SM, 4), (b2g.TILE_256x128_2SM, 2),
+                                         (b2g.TILE_256x128_2SM, 4)])
 @pytest.mark.parametrize("fused", [False, True])
 def test_cluster_reduction_matches_workspace(cuda, tile, splits, fused):
-    """Split-K on 1-CTA tiles runs each tile's splits as one cluster and sums the partials
-    in the shared memory of the owning CTA (st.async into its receive slots); the
-    no-allocation entry point sums the same partials through its workspace. Same operations
-    in the same split order: identical bits. Ragged M, N and K; uneven K shares."""
+    """Split-K runs each tile's splits as one cluster (S CTAs, or S pairs of the 2-CTA
+    kernel) and sums the partials in the shared memory of the owning CTA (st.async into its
+    receive slots, which overlay its drained operand ring); the no-allocation entry point sums
+    the same partials through its workspace. Same operations in the same split order:
+    identical bits. Ragged M, N and K; uneven K shares."""
     M, N, K = 300, 520, 2000
     A, B, bias = inputs(M, N, K, seed=35)
     kw = dict(epilogue=b2g.EPI_BIAS_RELU, alpha=0.5) if fused else {}
     (Dc, Dw), launch = _split_pair(cuda, A, B, bias if fused else None, splits, tile, kw, K)
-    assert launch["cluster"] == splits and launch["grid"] == launch["units"], launch
+    ctas = 2 if tile in PAIR_TILES else 1
+    assert launch["cluster"] == splits * ctas and launch["grid"] == ctas * launch["units"], launch
     assert np.array_equal(Dc, Dw)
     frob, maxrel = check_rows(A, B, Dc, list(range(M)), bias=bias if fused else None,
                               alpha=kw.get("alpha", 1.0), epilogue=fused)
