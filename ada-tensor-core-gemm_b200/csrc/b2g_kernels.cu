@@ -205,6 +205,13 @@ int max_pair_clusters(const DeviceInfo& di, size_t smem) {
     cfg.gridDim = dim3(2 * (di.sm_count / 2), 1, 1);
     cfg.blockDim = dim3(kMaxThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, (const void*)gemm_sm100_2cta<256>, &cfg) != cudaSuccess ||
         n <= 0) {
@@ -328,9 +335,6 @@ bool csplit_enabled() {
     return on;
 }
 
-// Largest receive area a cluster split-K launch may take from the shared-memory ring.
-constexpr uint32_t kCsMaxRecvBytes = 64 * 1024;
-
 // Whether clusters of `ctas` CTAs of the 1-CTA kernel `tile` (one per SM at this shared-
 // memory size) can be resident on this device at all; cached per (device, tile, ctas, smem).
 bool cluster_fits(const DeviceInfo& di, int tile, int ctas, int threads, size_t smem,
@@ -383,17 +387,17 @@ cudaError_t launch_gemm_t(int tile, const CUtensorMap& tmA, const CUtensorMap& t
             return launch_exc(gemm_sm100_1cta<64, PEERS>, grid, threads, smem, s,
                               p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
         case B2G_TILE_256x512_2SM:
-            grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
-            return launch_ex(gemm_sm100_2cta<512, PEERS>, grid, threads, smem, s, tmA, tmB, tmBt,
-                             tmD, p);
+            grid = 2 * (p.csplit ? p.num_units : std::min(p.num_units, max_pair_clusters(di, smem)));
+            return launch_exc(gemm_sm100_2cta<512, PEERS>, grid, threads, smem, s,
+                              p.csplit ? 2 * p.splits : 2, tmA, tmB, tmBt, tmD, p);
         case B2G_TILE_256x128_2SM:
-            grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
-            return launch_ex(gemm_sm100_2cta<128, PEERS>, grid, threads, smem, s, tmA, tmB, tmBt,
-                             tmD, p);
+            grid = 2 * (p.csplit ? p.num_units : std::min(p.num_units, max_pair_clusters(di, smem)));
+            return launch_exc(gemm_sm100_2cta<128, PEERS>, grid, threads, smem, s,
+                              p.csplit ? 2 * p.splits : 2, tmA, tmB, tmBt, tmD, p);
         default:
-            grid = 2 * std::min(p.num_units, max_pair_clusters(di, smem));
-            return launch_ex(gemm_sm100_2cta<256, PEERS>, grid, threads, smem, s, tmA, tmB, tmBt,
-                             tmD, p);
+            grid = 2 * (p.csplit ? p.num_units : std::min(p.num_units, max_pair_clusters(di, smem)));
+            return launch_exc(gemm_sm100_2cta<256, PEERS>, grid, threads, smem, s,
+                              p.csplit ? 2 * p.splits : 2, tmA, tmB, tmBt, tmD, p);
     }
 }
 
@@ -412,7 +416,7 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "GEMM launch (tile %d, grid %d, smem %zu): %s", tile, grid, smem,
                     cudaGetErrorString(e));
-    const int cluster = p.csplit ? p.splits : geom(tile).ctas;
+    const int cluster = (p.csplit ? p.splits : 1) * geom(tile).ctas;
     g_last_launch = LaunchRecord{grid, threads, tile, p.stages, p.num_units, p.splits, cluster};
     return B2G_OK;
 }
@@ -722,11 +726,20 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     // occupy under half of the pairs while 128 x 128 tiles fit one wave (measured on B200:
     // 1024^3 245 -> 258 TFLOP/s, 512^3 38 -> 42; the pair kernel's tail slices reload A);
     // else 2-CTA 256 x 256 pairs.
+    bool pair_split = false;
     if (tile == B2G_TILE_AUTO) {
         const long long pair_tiles = (long long)((M + 255) / 256) * ((N + 255) / 256);
         const long long small_tiles = (long long)((M + 127) / 128) * ((N + 127) / 128);
         const bool sparse_pairs = 2 * pair_tiles < di.sm_count / 2 && small_tiles <= di.sm_count;
-        tile = (N <= 128 || M <= 128 || sparse_pairs) ? B2G_TILE_128x128 : B2G_TILE_256x256_2SM;
+        // Pair tiles that would fill between a quarter and a half of the pair clusters, with
+        // long K: two K splits per tile, reduced inside a cluster of the two pairs, fill the
+        // GPU with pairs, whose L2 -> SM traffic per FLOP is half that of 128 x 128 tiles
+        // (measured on B200: 512 x 4096 x 4096 22.7 us on 128 x 128 tiles -> 20.7 us).
+        pair_split = sparse_pairs && 4 * pair_tiles > di.sm_count / 2 && K >= 2048 &&
+                     acc == B2G_ACC_F32 && requested_splits == 0 && !noalloc && npeer == 0 &&
+                     b_layout == B2G_B_NK && csplit_enabled();
+        tile = (N <= 128 || M <= 128 || (sparse_pairs && !pair_split)) ? B2G_TILE_128x128
+                                                                      : B2G_TILE_256x256_2SM;
         // Long K with at least ~4 waves of 256 x 512 pair tiles: the wide tile's quarter less
         // L2 traffic per FLOP wins (measured on B200: 8192^3 1446 -> 1503, 16384^3 1253 ->
         // 1310, 4096 x 32768 x 8192 1443 -> 1512 TFLOP/s; at K = 4096 it is ~3% slower).
@@ -812,7 +825,9 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     // split-K: tiles that fill under half of the SMs (pairs) get their K range split
     const int concurrent = g.ctas == 2 ? max_pair_clusters(di, smem) : di.sm_count;
     if (splits == 0)
-        splits = acc == B2G_ACC_F32 ? splitk_auto(p.num_tiles, concurrent, p.num_kb, g.ctas) : 1;
+        splits = pair_split ? 2
+                            : acc == B2G_ACC_F32 ? splitk_auto(p.num_tiles, concurrent, p.num_kb, g.ctas)
+                                                 : 1;
     if (splits > p.num_kb)
         return fail(B2G_ERR_ARG, "splits (%d) > k-blocks of 64 (%d)", splits, p.num_kb);
     if (wide && splits > 1)
@@ -834,22 +849,40 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     // on B200: the workspace's partial stores, release-ordered arrival and L2 re-reads cost
     // more than the split mainloop they serve at decode shapes). b2g_gemm_splitk_noalloc
     // keeps the workspace path on its static scratch; both reductions give the same bits.
-    if (splits > 1 && g.ctas == 1 && !noalloc && splits <= 8 && csplit_enabled()) {
-        const uint32_t recv = csplit_recv_bytes(g.bn, splits);
-        int st = stages;
+    // (1-CTA tiles: clusters of S <= 8 CTAs; 2-CTA 256 x 256 and 256 x 128 tiles: S <= 4
+    // pairs, 8 CTAs; the receive slots of the CTA's 128 x min(BN, 256) accumulator overlay the
+    // ring, which must hold them)
+    // Where the receive slots go (measured on B200, N = K = 4096): on 1-CTA tiles their own
+    // shared memory when that still leaves a ring of at least 4 stages -- a split then sends as
+    // soon as its own accumulator is final (M = 128: 14.7 us, vs 15.4 us with 6 stages and the
+    // slots over the ring; M = 1: 12.5 vs 13.3 us); on pair tiles, whose mainloop needs the
+    // deeper ring more, over the drained ring unless their own memory costs no stage (M = 512
+    // on 256 x 256 pairs: 20.7 us over the ring with 6 stages vs 22.2 us with 4).
+    if (splits > 1 && !noalloc && !wide && splits * g.ctas <= 8 && csplit_enabled()) {
+        const uint32_t recv = csplit_recv_bytes(std::min(g.bn, kPairBN), splits);
+        const size_t stage_b = (size_t)a_rows * kBK * 2 + (size_t)g.box_b * kBK * 2;
+        int st_own = stages;
         if (stages_arg == 0)
-            while (st > 2 && smem_needed(tile, st, epi_boxes, a_rows) + recv > (size_t)di.smem_optin)
-                --st;
-        const size_t need = smem_needed(tile, st, epi_boxes, a_rows) + recv;
-        const size_t req = std::max(need, (size_t)di.smem_per_sm / 2 + 1024);
-        if (recv <= kCsMaxRecvBytes && need <= (size_t)di.smem_optin) {
+            while (st_own > 2 && smem_needed(tile, st_own, epi_boxes, a_rows) + recv >
+                                     (size_t)di.smem_optin)
+                --st_own;
+        const bool own = smem_needed(tile, st_own, epi_boxes, a_rows) + recv <=
+                             (size_t)di.smem_optin &&
+                         (st_own == stages || (g.ctas == 1 && st_own >= 4));
+        if (own || recv <= (size_t)stages * stage_b) {
+            const size_t req = own ? std::max(smem_needed(tile, st_own, epi_boxes, a_rows) + recv,
+                                              (size_t)di.smem_per_sm / 2 + 1024)
+                                   : smem;
             if (int rc = ensure_kernel_attrs(tile, di, npeer > 0)) return rc;
-            if (cluster_fits(di, tile, splits, gemm_threads(8), req, npeer > 0)) {
+            if (cluster_fits(di, tile, splits * g.ctas, gemm_threads(8), req, npeer > 0)) {
                 p.csplit = 1;
+                p.recv_ring = own ? 0 : 1;
                 p.recv_bytes = recv;
-                stages = st;
-                p.stages = st;
-                smem = req;
+                if (own) {
+                    stages = st_own;
+                    p.stages = st_own;
+                    smem = req;
+                }
             }
         }
     }

@@ -69,11 +69,15 @@ struct GemmParams {
     float* ws_part;                // FP32 partial accumulators, splitk_slot() layout
     unsigned long long* ws_count;  // arrival counters: (launch epoch << 32) | arrivals
     unsigned int epoch;            // this launch's epoch, never 0 and never repeated
-    // 1-CTA kernels, splits > 1: csplit = 1 reduces the splits of a tile inside a cluster of
-    // `splits` CTAs through distributed shared memory (see csplit_epilogue) instead of the
-    // workspace; the grid is then one CTA per unit (not persistent) and recv_bytes of shared
-    // memory after the epilogue staging hold the receive slots.
+    // splits > 1: csplit = 1 reduces the splits of a tile inside one cluster (`splits` CTAs,
+    // or `splits` pairs of the 2-CTA kernel) through distributed shared memory (see
+    // csplit_epilogue) instead of the workspace; the grid is then one CTA (pair) per unit,
+    // not persistent. The receive slots (recv_bytes) either have their own shared memory after
+    // the epilogue staging (recv_ring = 0: a split sends as soon as its own accumulator is
+    // final) or overlay the drained operand ring (recv_ring = 1: more stages, but a split
+    // sends only once every peer's ring has drained).
     int csplit;
+    int recv_ring;
     uint32_t recv_bytes;
     // 1-CTA kernels: bytes one stage's two TMA loads deliver. When all of M fits one tile the
     // A box is only round_up(M, 8) rows high and the ring packs stages of a_stage_bytes of A
@@ -153,6 +157,7 @@ struct SmemCtl {
     uint64_t tmem_full[2];
     uint64_t tmem_empty[2];
     uint64_t recv[kCsMaxPieces];  // cluster split-K: one receive barrier per owned piece
+    uint64_t peers_free;          // cluster split-K: one arrival per peer whose ring drained
     uint64_t drain;
     uint32_t tmem_base;
     int abort;
@@ -160,8 +165,8 @@ struct SmemCtl {
 };
 
 // Dynamic shared memory: [align slack][stages x (A, B)][epilogue staging][cluster split-K
-// receive slots, if any][SmemCtl]. A stage is a_rows x 128 B of A (a_rows = 128, or M rounded
-// up to 8 when all of M fits one tile) followed by BN x 128 B of B.
+// receive slots, unless they overlay the ring][SmemCtl]. A stage is a_rows x 128 B of A
+// (a_rows = 128, or M rounded up to 8 when all of M fits one tile) followed by BN x 128 B of B.
 template <int BN>
 constexpr size_t gemm_smem_bytes(int stages, uint32_t epi, int a_rows = kBM) {
     return 1024 /* alignment slack */ +
@@ -688,6 +693,15 @@ __device__ __forceinline__ void csplit_reduce(const GemmParams& p, const EpiScal
     epi_box_push<PEERS>(p, e, box, col, row0, lane);
 }
 
+// Cluster split-K: this CTA's ring has drained (its accumulator is final, so every load into
+// the ring has landed and every MMA reading it is done): tell the CTAs that send to it -- the
+// ones holding the same rows in the other splits -- that they may write its receive slots.
+__device__ __forceinline__ void csplit_ring_free(uint32_t peers_free, int S, int s, int ctas,
+                                                 int prank) {
+    for (int o = 0; o < S; ++o)
+        if (o != s) mbar_arrive_remote(mapa_shared(peers_free, (uint32_t)(o * ctas + prank)));
+}
+
 // Cluster split-K epilogue of one warp (lane quarter q, chunks c_first, c_first + c_step, ...)
 // for this CTA's split s: first every piece another CTA owns is sent, then every owned piece
 // is received (bounded wait) and reduced; TMEM is released last. Pieces outside D (rows >= M
@@ -698,24 +712,32 @@ __device__ __forceinline__ void csplit_epilogue(const GemmParams& p, const EpiSc
                                                 int bn, int row0, int n_first, int c_first,
                                                 uint32_t stage0, int lane, uint32_t& seq,
                                                 bool epi, uint32_t recv0, uint32_t rbar0,
-                                                const WaitCtx& w, Release release) {
+                                                uint32_t peers_free, const WaitCtx& w,
+                                                Release release, int s, int ctas, int prank) {
+    // split s of the cluster; the CTA holding the same rows in split o has cluster rank
+    // o * ctas + prank (ctas = 2 for the pair kernel, prank = this CTA's place in its pair)
     const int S = p.splits;
-    const int s = (int)cluster_ctarank();
     const int nch = bn / 64;
     int nchunks = nch;
     const int in_n = (e.N - n_first + 63) / 64;
     if (in_n < nchunks) nchunks = in_n;
     if (threadIdx.x == 128) B2G_MARK(6);
+    bool peers_ready = false;
     if (row0 < e.M) {
 #pragma unroll 1
         for (int c = c_first; c < nchunks; c += e.c_step) {
             const int i = q * nch + c, owner = i % S, k = i / S;
             if (owner == s) continue;
+            // slots over the owners' rings: send once every peer's ring has drained
+            if (p.recv_ring && !peers_ready) {
+                if (!mbar_wait_warp<true>(peers_free, 0, w)) break;
+                peers_ready = true;
+            }
             const int j = s < owner ? s : s - 1;
+            const uint32_t orank = (uint32_t)(owner * ctas + prank);
             csplit_send(trow, c,
-                        mapa_shared(recv0 + (uint32_t)(k * (S - 1) + j) * kCsPieceBytes,
-                                    (uint32_t)owner),
-                        mapa_shared(rbar0 + 8u * (uint32_t)k, (uint32_t)owner), lane);
+                        mapa_shared(recv0 + (uint32_t)(k * (S - 1) + j) * kCsPieceBytes, orank),
+                        mapa_shared(rbar0 + 8u * (uint32_t)k, orank), lane);
         }
 #pragma unroll 1
         for (int c = c_first; c < nchunks; c += e.c_step) {
@@ -762,9 +784,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const uint32_t sB = sA + p.a_stage_bytes;
     const uint32_t sEpi = raw + pad + (uint32_t)p.stages * stride;
     const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
-    const uint32_t sRecv = sEpi + epi_bytes(epi_warps, p.epi_bufs);
+    // cluster split-K receive slots: over the drained ring, or after the epilogue staging
+    const uint32_t sRecv = p.recv_ring ? sA : sEpi + epi_bytes(epi_warps, p.epi_bufs);
     SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * stride +
-                                              epi_bytes(epi_warps, p.epi_bufs) + p.recv_bytes);
+                                              epi_bytes(epi_warps, p.epi_bufs) +
+                                              (p.recv_ring ? 0u : p.recv_bytes));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t full0 = smem_u32(&ctl->full[0]);
@@ -772,6 +796,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const uint32_t tfull0 = smem_u32(&ctl->tmem_full[0]);
     const uint32_t tempty0 = smem_u32(&ctl->tmem_empty[0]);
     const uint32_t rbar0 = smem_u32(&ctl->recv[0]);
+    const uint32_t peers_free = smem_u32(&ctl->peers_free);
     const uint32_t drain = smem_u32(&ctl->drain);
 
     if (threadIdx.x == 0) {
@@ -784,6 +809,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             mbar_init(tempty0 + 8 * b, (uint32_t)epi_warps);  // one arrive per epilogue warp
         }
         for (int k = 0; k < kCsMaxPieces; ++k) mbar_init(rbar0 + 8 * k, 1);  // owner's arm
+        mbar_init(peers_free, p.recv_ring ? (uint32_t)(p.splits - 1) : 1u);
         mbar_init(drain, 1);
         ctl->abort = 0;
         ctl->never = 0;
@@ -968,8 +994,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
             };
             if (p.splits > 1 && p.csplit) {
+                // tmem_full: every load of this CTA's ring has landed and every MMA reading it
+                // is done, so the peers may overwrite the ring with their partials
+                const int s = (int)cluster_ctarank();
+                if (p.recv_ring && threadIdx.x == 64) csplit_ring_free(peers_free, p.splits, s, 1, 0);
                 csplit_epilogue<PEERS>(p, es, &tmD, tbase, q, BN, tm * kBM + q * 32, tn * BN,
-                                       c_first, stage0, lane, seq, epi, sRecv, rbar0, w, release);
+                                       c_first, stage0, lane, seq, epi, sRecv, rbar0, peers_free,
+                                       w, release, s, 1, 0);
             } else if (p.splits > 1) {
                 splitk_epilogue<PEERS>(p, es, &tmD, tbase, t, u - t * p.splits, 0, 1, q, warp - 2, BN,
                                 tm * kBM + q * 32, tn * BN, c_first, stage0, lane, seq, epi,

@@ -18,6 +18,11 @@
 // half 0 and defers the half-1 MMAs of up to 3 k-blocks (holding their stages) until half 1
 // is free.
 //
+// Clusters: launched with a runtime cluster shape of 2 CTAs (one pair), or of 2 x S CTAs for
+// split-K reduced through distributed shared memory (csplit): pair s of the cluster computes
+// split s of the cluster's tile. Pair-local ranks: the CTA with cluster rank r is CTA r & 1 of
+// its pair, whose leader has rank r & ~1.
+//
 // Work list: whole tiles first, then the tiles of the last, partial wave cut into
 // `tail_split` (2 or 4) column slices (UMMA N = slice width <= 256; B read through a second
 // tensor map whose box matches the slice), so the tail wave keeps every SM pair busy
@@ -98,7 +103,7 @@ __device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& t, in
 
 // PEERS: the fused all-gather instantiation (every staged box of D also goes to p.peers).
 template <int BNP, bool PEERS = false>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
+__global__ void __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_2cta(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmBt,
@@ -114,11 +119,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
     const uint32_t sB = sA + (uint32_t)p.stages * kHalfBytes;
     const uint32_t sEpi = sA + (uint32_t)p.stages * PT::kStageBytes;
     const int epi_warps = (int)(blockDim.x >> 5) - 2;  // 4 or 8
+    // cluster split-K receive slots: over the drained ring, or after the epilogue staging
+    const uint32_t sRecv = p.recv_ring ? sA : sEpi + epi_bytes(epi_warps, p.epi_bufs);
     SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * PT::kStageBytes +
-                                              epi_bytes(epi_warps, p.epi_bufs));
+                                              epi_bytes(epi_warps, p.epi_bufs) +
+                                              (p.recv_ring ? 0u : p.recv_bytes));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_ctarank();
+    const uint32_t crank = cluster_ctarank();
+    const uint32_t rank = crank & 1u;               // this CTA's place in its pair
+    const uint32_t lead = crank & ~1u;              // cluster rank of the pair's leader
+    const uint16_t pair_mask = (uint16_t)(3u << lead);
     const bool leader = rank == 0;
     const int cluster_id = blockIdx.x >> 1, num_clusters = gridDim.x >> 1;
     const uint32_t full0 = smem_u32(&ctl->full[0]);
@@ -126,12 +137,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
     const uint32_t tfull0 = smem_u32(&ctl->tmem_full[0]);
     const uint32_t tempty0 = smem_u32(&ctl->tmem_empty[0]);
     const uint32_t drain = smem_u32(&ctl->drain);
+    const uint32_t rbar0 = smem_u32(&ctl->recv[0]);
+    const uint32_t peers_free = smem_u32(&ctl->peers_free);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < p.stages; ++s) {
             mbar_init(full0 + 8 * s, 1);   // only the leader's copy is used
             mbar_init(empty0 + 8 * s, 1);  // one multicast commit per use
         }
+        for (int k = 0; k < kCsMaxPieces; ++k) mbar_init(rbar0 + 8 * k, 1);  // owner's arm
+        mbar_init(peers_free, p.recv_ring ? (uint32_t)(p.splits - 1) : 1u);
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull0 + 8 * b, 1);
             mbar_init(tempty0 + 8 * b, 2u * epi_warps);  // epilogue warps x 2 CTAs (leader's copy)
@@ -158,8 +173,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
     const uint32_t tmem_base = ctl->tmem_base;
     volatile int* abort_flag = &ctl->abort;
     volatile int* no_abort = &ctl->never;
-    const uint32_t full0_leader = mapa_shared(full0, 0);
-    const uint32_t tempty0_leader = mapa_shared(tempty0, 0);
+    const uint32_t full0_leader = mapa_shared(full0, lead);
+    const uint32_t tempty0_leader = mapa_shared(tempty0, lead);
     // everything above overlapped the previous kernel; global memory only from here on
     if (threadIdx.x == 0) B2G_MARK(1);
     grid_dep_wait();
@@ -284,7 +299,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                         if (elect_one()) {
                             mma_kblock_pair(d_tmem + (uint32_t)kPairBN, ad, bd + kBHalf, bk, idesc,
                                             i > 0 ? 1u : 0u);
-                            mma_commit_pair(empty0 + 8 * st, 0x3);
+                            mma_commit_pair(empty0 + 8 * st, pair_mask);
                         }
                         __syncwarp();
                         if (++st == p.stages) st = 0;
@@ -324,7 +339,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                         }
                     }
                     if (commit) {
-                        if (elect_one()) mma_commit_pair(empty0 + 8 * stage, 0x3);  // both CTAs
+                        if (elect_one()) mma_commit_pair(empty0 + 8 * stage, pair_mask);  // both CTAs
                         __syncwarp();
                     }
                     if (++stage == p.stages) {
@@ -335,7 +350,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                 // a unit shorter than the deferral window ends with half-1 work pending
                 if (ok && two_halves && !half1_ready && !flush_deferred()) ok = false;
                 if (!ok) break;
-                if (elect_one()) mma_commit_pair(tfull0 + 8 * buf, 0x3);  // final in both CTAs
+                if (elect_one()) mma_commit_pair(tfull0 + 8 * buf, pair_mask);  // final in both CTAs
                 __syncwarp();
                 if (lane == 0) B2G_MARK(5);
             }
@@ -390,7 +405,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kMaxThreads, 1)
                 }
             } else {
                 const uint32_t tbase = tq + (uint32_t)(buf * kPairBN);
-                if (p.splits > 1) {
+                if (p.splits > 1 && p.csplit) {
+                    const int s = (int)(crank >> 1);
+                    if (p.recv_ring && threadIdx.x == 64)
+                        csplit_ring_free(peers_free, p.splits, s, 2, (int)rank);
+                    csplit_epilogue<PEERS>(p, es, &tmD, tbase, q, BNP < kPairBN ? BNP : kPairBN,
+                                           row0, n_first, c_first, stage0, lane, seq, epi, sRecv,
+                                           rbar0, peers_free, w, [&] { release(buf); }, s, 2,
+                                           (int)rank);
+                } else if (p.splits > 1) {
                     splitk_epilogue<PEERS>(p, es, &tmD, tbase, t, split, (int)rank, 2, q,
                                            warp - 2, BNP < kPairBN ? BNP : kPairBN, row0, n_first,
                                            c_first, stage0, lane, seq, epi,

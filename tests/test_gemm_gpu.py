@@ -359,6 +359,7 @@ def test_b_kn_layout_modes(cuda, mode):
     ((512, 512, 512), b2g.TILE_128x64, 1),
     ((1024, 1024, 4096), b2g.TILE_128x128, 2),     # long K: split instead
     ((128, 4096, 4096), b2g.TILE_128x128, 4),      # decode-shaped
+    ((512, 4096, 4096), b2g.TILE_256x256_2SM, 2),  # half-filled pairs: 2 K splits, one cluster
     ((2048, 1024, 1024), b2g.TILE_128x128, 1),     # 128 tiles: a full wave of 128x128
     ((4096, 4096, 4096), b2g.TILE_256x256_2SM, 1),  # the headline shape
     ((8192, 8192, 8192), b2g.TILE_256x512_2SM, 1),  # long K, >= 4 waves of 256 x 512

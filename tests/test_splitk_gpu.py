@@ -56,20 +56,24 @@ def test_split_result_is_deterministic_and_close_to_unsplit(cuda):
     assert d.max() <= 2.0 ** -9 * max(1.0, np.abs(O.f16_to_f32(one)).max()), d.max()
 
 
-@pytest.mark.parametrize("M,split", [(1, True), (8, True), (32, True), (128, True),
-                                     (512, False)])
-def test_skinny_decode_auto_split(cuda, M, split):
+@pytest.mark.parametrize("M,split,tile", [(1, 4, b2g.TILE_128x128), (8, 4, b2g.TILE_128x128),
+                                          (32, 4, b2g.TILE_128x128), (128, 4, b2g.TILE_128x128),
+                                          (256, 2, b2g.TILE_128x128),
+                                          (512, 2, b2g.TILE_256x256_2SM),
+                                          (1024, 1, b2g.TILE_256x256_2SM)])
+def test_skinny_decode_auto_split(cuda, M, split, tile):
     """The reference's Phase 6 shapes (N = K = 4096): b2g_gemm splits K automatically when
-    128 x 128 tiles leave most SMs idle (M <= 128 here), each tile's splits forming one
-    cluster reduced through distributed shared memory; 2-CTA pair tiles (M = 512) are never
-    split automatically."""
+    the tiles leave most SMs idle, each tile's splits forming one cluster reduced through
+    distributed shared memory: 128 x 128 tiles for M <= 256, and at M = 512 two splits of
+    256 x 256 pair tiles (clusters of two pairs); M = 1024 fills the GPU with pairs unsplit."""
     N = K = 4096
     A, B, _ = inputs(M, N, K, seed=33)
     D = run(cuda, A, B)
     launch = b2g.last_launch()
-    assert (launch["splits"] > 1) == split, launch
-    if split:
-        assert launch["cluster"] == launch["splits"] and launch["grid"] == launch["units"]
+    assert (launch["tile"], launch["splits"]) == (tile, split), launch
+    if split > 1:
+        ctas = 2 if tile == b2g.TILE_256x256_2SM else 1
+        assert launch["cluster"] == split * ctas and launch["grid"] == ctas * launch["units"]
     rows = sample_rows(M, 32)
     frob, maxrel = check_rows(A, B, D, rows)
     assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
