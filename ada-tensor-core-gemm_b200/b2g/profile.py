@@ -38,16 +38,14 @@ SECTIONS = ["SpeedOfLight", "ComputeWorkloadAnalysis", "MemoryWorkloadAnalysis",
             "MemoryWorkloadAnalysis_Tables", "Occupancy", "SchedulerStats", "WarpStateStats",
             "LaunchStats", "InstructionStats"]
 
-# The reference's metric list (scripts/profile.ps1:48-90), restated with the B200 names:
-# tcgen05 work is counted by the sm__ops_path_tensor_op_hmma_* counters (the `_sparsity_off`
-# forms carry the dense peak, as the reference argues at scripts/profile.ps1:49-58), the
-# tensor pipe by sm__pipe_tensor_cycles_active; TMA traffic, L2 and DRAM bytes, the stall
-# reasons of the reference's list, and NVLink bytes for the fused all-gather kernels.
+# The reference's metric list (scripts/profile.ps1:48-90), restated for B200. Its dense tensor
+# counters (sm__ops_path_tensor_op_hmma_*_sparsity_off, scripts/profile.ps1:49-58) count
+# mma.sync work only and read 0 for tcgen05 kernels (measured: ours and cuBLAS's alike), so
+# the tensor pipe is read from sm__pipe_tensor_cycles_active and cross-checked, clock-free, by
+# the dense occupancy from the probe's FLOP per clock per SM (which agreed with it to 0.1% on
+# the 4096^3 capture). Then TMA traffic, L2 and DRAM bytes, the stall reasons of the
+# reference's list, and NVLink bytes for the fused all-gather kernels.
 METRICS = [
-    "sm__ops_path_tensor_op_hmma_src_fp16_dst_fp32_sparsity_off.sum",
-    "sm__ops_path_tensor_op_hmma_src_fp16_dst_fp16_sparsity_off.sum",
-    "sm__ops_path_tensor_op_hmma_src_fp16_dst_fp32_sparsity_off.sum.pct_of_peak_sustained_elapsed",
-    "sm__ops_path_tensor_op_hmma_src_fp16_dst_fp16_sparsity_off.sum.pct_of_peak_sustained_elapsed",
     "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_active",
     "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed",
     "sm__inst_executed_pipe_tc.sum",
@@ -156,17 +154,16 @@ def summarize(m: dict, M: int, N: int, K: int, fpc: float | None, sms: int | Non
         ca = get("sm__cycles_active.avg")
         if ca:
             s["dense_occupancy_active"] = busy / ca
-    ops = get("sm__ops_path_tensor_op_hmma_src_fp16_dst_fp32_sparsity_off.sum") or \
-        get("sm__ops_path_tensor_op_hmma_src_fp16_dst_fp16_sparsity_off.sum")
-    if ops:
-        s["tensor_ops_counted"] = ops
-        s["tensor_ops_vs_2mnk"] = ops / flop
+    ta = get("sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed")
+    if ta is not None and "dense_occupancy_elapsed" in s:
+        s["tensor_pipe_vs_dense_occupancy"] = ta / 100.0 / s["dense_occupancy_elapsed"]
     return s
 
 
 def markdown(tag, cmds, m, s, M, N, K, fpc, sms) -> str:
     plain, section_cmd, metric_cmd = cmds
-    q = lambda c: " ".join(c)  # noqa: E731
+    cwd = os.getcwd() + os.sep
+    q = lambda c: " ".join(x.replace(cwd, "") for x in c)  # noqa: E731  (paths as run)
     lines = [f"# {tag}: {M} x {N} x {K} -- ncu summary (b2g.profile)", "",
              "Commands (one GPU; the plain run exited 0 first):", "", "```", q(plain),
              q(section_cmd), q(metric_cmd), "```", "",

@@ -168,7 +168,7 @@ M N K ...
 "0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","gpu__time_duration.sum","ns","96,400"
 "0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","dram__bytes_read.sum","byte","69,190,000"
 "0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","dram__bytes_write.sum","byte","17,440,000"
-"0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","sm__ops_path_tensor_op_hmma_src_fp16_dst_fp32_sparsity_off.sum","","137,438,953,472"
+"0","1","gemm_bench","h","b2g::gemm_sm100_2cta<256, 0>","1","7","(320, 1, 1)","(148, 1, 1)","0","10.0","Command line profiler metrics","sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed","%","74.58"
 '''
 
 
@@ -198,9 +198,10 @@ def test_profile_parse_and_dense_occupancy():
     assert abs(s["busy_tensor_cycles"] - busy) < 1e-6
     assert abs(s["dense_occupancy_elapsed"] - busy / 153016.0) < 1e-12
     assert abs(s["dense_occupancy_active"] - busy / 134428.0) < 1e-12
-    assert s["tensor_ops_vs_2mnk"] == 1.0  # the counter counts exactly 2MNK
     assert abs(s["dram_bytes"] - 86.63e6) < 1
     assert abs(s["tflops_under_ncu"] - 2.0 * 4096 ** 3 / 96.4e-6 / 1e12) < 1e-6
+    # the pipe counter against the clock-free figure (1.0: they agree)
+    assert abs(s["tensor_pipe_vs_dense_occupancy"] - 0.7458 / (busy / 153016.0)) < 1e-12
     assert profile.parse_metrics_csv("no csv here") == {}
 
 
