@@ -24,7 +24,8 @@ file and rank 0 quotes its `Init COMPLETE` line (`nccl_comm`).
 `value` is whole-job TFLOP/s with inputs resident in HBM, timed with CUDA events on the
 launching stream, max over ranks. Between timed iterations the inputs rotate over enough
 buffer sets that the working set exceeds the 126 MB L2. `e2e` is the same metric through
-the C-ABI with pinned host buffers: every step copies A and B host->device and D back.
+the C-ABI with pinned host buffers: every step copies A and B host->device and D back
+(steps pipelined over two device buffer sets on H2D, compute and D2H streams).
 --impl reference times the reference's own implementation on the same workload: its CPU
 GEMM code (the FP64 dot products of cpu_spot_check, src/gemm_bench.cu:672-696, compiled
 from its source) on all host cores, plus its sm_89 kernel JIT-run on this B200 as an extra
@@ -539,26 +540,52 @@ def run_ours(args):
     del dRef
     ms_cublas = timed("cublas", args.steps, args.warmup)
 
-    # e2e through the C-ABI with pinned host buffers: H2D of A and B, GEMM, D2H of D
+    # e2e through the C-ABI with pinned host buffers: every step copies its A and B host ->
+    # device, runs the GEMM and copies D device -> host. The steps are pipelined over two
+    # device buffer sets and three streams: step i's inputs go up on the H2D stream while
+    # step i - 1 computes and step i - 2's D comes down on the D2H stream (PCIe is full
+    # duplex), each copy ordered after the last use of its buffer by events.
     e2e_steps = args.e2e_steps or min(args.steps, 20)
-    dA, dB, dD = sets[0]
+    bufs = [sets[0], sets[1 % nbuf]]
+    hDs = [hD, torch.empty_like(hD, pin_memory=True)]
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev = {k: [torch.cuda.Event(), torch.cuda.Event()] for k in ("in", "gemm", "out")}
+    used = [False, False]
 
-    def e2e_step():
-        dA.copy_(hA, non_blocking=True)
-        dB.copy_(hB, non_blocking=True)
+    def e2e_step(i):
+        b = i % 2
+        dA, dB, dD = bufs[b]
+        if used[b]:
+            s_in.wait_event(ev["gemm"][b])  # the GEMM two steps back has read these inputs
+        with torch.cuda.stream(s_in):
+            dA.copy_(hA, non_blocking=True)
+            dB.copy_(hB, non_blocking=True)
+            ev["in"][b].record(s_in)
+        stream.wait_event(ev["in"][b])
+        if used[b]:
+            stream.wait_event(ev["out"][b])  # D of two steps back has been read out
         b2g.gemm_raw(dA.data_ptr(), dB.data_ptr(), dD.data_ptr(), None, rows, N, K, K, K, N,
                      b2g.B_NK, acc, b2g.EPI_NONE, 1.0, args.tile, args.stages, args.group, sptr)
-        hD.copy_(dD, non_blocking=True)
+        ev["gemm"][b].record(stream)
+        s_out.wait_event(ev["gemm"][b])
+        with torch.cuda.stream(s_out):
+            hDs[b].copy_(dD, non_blocking=True)
+            ev["out"][b].record(s_out)
+        used[b] = True
 
-    for _ in range(2):
-        e2e_step()
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize()
     b2g.sync_status(sptr)
     barrier()
-    torch.cuda.synchronize()
+    used[0] = used[1] = False
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
+    s_in.wait_event(e0)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    for b in range(2):
+        stream.wait_event(ev["out"][b])  # the timed region ends when the last D is on the host
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -662,7 +689,9 @@ def run_ours(args):
         "maxrel_vs_cublas": maxrel,
         "e2e": {"value": round(flop_job * e2e_steps / (ms_e2e * 1e-3) / 1e12, 3),
                 "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
-                "d2h_bytes_per_step": d2h * world, "steps": e2e_steps},
+                "d2h_bytes_per_step": d2h * world, "steps": e2e_steps,
+                "how": "every step: pinned H2D of A and B, the GEMM through the C-ABI, D2H of "
+                       "D; steps pipelined over 2 buffer sets on H2D / compute / D2H streams"},
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
