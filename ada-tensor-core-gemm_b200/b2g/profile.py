@@ -134,9 +134,13 @@ def dense_occupancy(flop: float, flop_per_clk_sm: float, sms: int, cycles_elapse
     return busy, busy / cycles_elapsed
 
 
-def summarize(m: dict, M: int, N: int, K: int, fpc: float | None, sms: int | None) -> dict:
-    flop = 2.0 * M * N * K
-    s = {"flop": flop, "compulsory_bytes": 2.0 * (M * K + N * K + M * N)}
+def summarize(m: dict, M: int, N: int, K: int, fpc: float | None, sms: int | None,
+              gpus: int = 1) -> dict:
+    """Derived figures of one captured launch; with gpus > 1 the launch is one device's
+    M / gpus-row panel (gemm_bench --gpus), so FLOP and compulsory bytes are per panel."""
+    Mp = M / gpus
+    flop = 2.0 * Mp * N * K
+    s = {"flop": flop, "compulsory_bytes": 2.0 * (Mp * K + N * K + Mp * N)}
     get = m.get
     if get("gpu__time_duration.sum"):
         t = get("gpu__time_duration.sum") * 1e-9
@@ -211,7 +215,8 @@ def run(M, N, K, tag, out_dir, exe=DEFAULT_EXE, tile=-1, stages=0, group=0, acc=
     m = parse_metrics_csv(r.stdout)
     if not m:
         raise RuntimeError("ncu metrics pass printed no metric rows:\n" + r.stdout[-2000:])
-    s = summarize(m, M, N, K, fpc, sms)
+    gpus = int(extra[list(extra).index("--gpus") + 1]) if "--gpus" in extra else 1
+    s = summarize(m, M, N, K, fpc, sms, gpus)
     md = markdown(tag, cmds, m, s, M, N, K, fpc, sms)
     with open(rep + ".md", "w") as fh:
         fh.write(md)
