@@ -1107,8 +1107,10 @@ B2G_EXPORT int b2g_instr_read(unsigned long long* out, int n_ctas) {
     return cudaMemcpyToSymbol(g_b2g_instr, zeros, sizeof(zeros)) == cudaSuccess ? B2G_OK
                                                                                 : B2G_ERR_CUDA;
 }
-B2G_EXPORT int b2g_instr_timeline(unsigned long long* out16) {
-    return cudaMemcpyFromSymbol(out16, g_b2g_tl, sizeof(unsigned long long) * 16) == cudaSuccess
+// Copy out the marks of the first n_ctas (<= 1024) CTAs of the most recent launch: 16 per CTA.
+B2G_EXPORT int b2g_instr_timeline(unsigned long long* out, int n_ctas) {
+    return cudaMemcpyFromSymbol(out, g_b2g_tl, sizeof(unsigned long long) * 16 * (size_t)n_ctas) ==
+                   cudaSuccess
                ? B2G_OK
                : B2G_ERR_CUDA;
 }

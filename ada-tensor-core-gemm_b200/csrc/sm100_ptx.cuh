@@ -151,14 +151,14 @@ __device__ unsigned long long g_b2g_instr[1024][kInstrSlots];
 #define B2G_COUNT(slot, n) atomicAdd(&g_b2g_instr[blockIdx.x][slot], (unsigned long long)(n))
 #define B2G_TOC64(slot, v) \
     if (threadIdx.x == 64) B2G_TOC(slot, v)
-// Timeline of CTA 0 (globaltimer ns): mark i is written by whichever thread reaches it.
-// 1-CTA kernel: 0 entry, 1 barriers and TMEM ready (cluster synced), 2 after
-// griddepcontrol.wait, 3 first TMA load issued, 4 first stage full at the MMA warp,
+// Timeline of every CTA (globaltimer ns, [CTA][mark]): mark i is written by whichever thread
+// of the CTA reaches it. 1-CTA kernel: 0 entry, 1 barriers and TMEM ready (cluster synced),
+// 2 after griddepcontrol.wait, 3 first TMA load issued, 4 first stage full at the MMA warp,
 // 5 accumulator committed, 6-9 cluster split-K epilogue of thread 128 (start, sends issued,
 // receive wait done, end), 10 after the teardown barriers, 11 producer issued its last load.
-__device__ unsigned long long g_b2g_tl[16];
+__device__ unsigned long long g_b2g_tl[1024][16];
 #define B2G_MARK(i) \
-    if (blockIdx.x == 0) g_b2g_tl[i] = globaltimer_ns()
+    if (blockIdx.x < 1024) g_b2g_tl[blockIdx.x][i] = globaltimer_ns()
 #else
 #define B2G_MARK(i)
 #define B2G_TOC64(slot, v)
