@@ -833,6 +833,14 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     const uint32_t tmem_base = ctl->tmem_base;
     volatile int* abort_flag = &ctl->abort;
     volatile int* no_abort = &ctl->never;
+    // the producer's first unit (tile and k-block range) is worked out while the previous
+    // kernel may still be running, so its first load follows the wait directly
+    int tm0 = 0, tn0 = 0, kb00 = 0, kb10 = 0;
+    if (warp == 0 && lane == 0 && (int)blockIdx.x < p.num_units) {
+        const int t = (int)blockIdx.x / p.splits;
+        tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm0, tn0);
+        split_range(p, (int)blockIdx.x - t * p.splits, kb00, kb10);
+    }
     // everything above overlapped the previous kernel; global memory only from here on
     grid_dep_wait();
     grid_dep_launch();
@@ -847,10 +855,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             long long issued = 0;
             bool ok = true;
             for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
-                const int t = u / p.splits;
-                int tm, tn, kb0, kb1;
-                tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
-                split_range(p, u - t * p.splits, kb0, kb1);
+                int tm = tm0, tn = tn0, kb0 = kb00, kb1 = kb10;
+                if (u != (int)blockIdx.x) {
+                    const int t = u / p.splits;
+                    tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
+                    split_range(p, u - t * p.splits, kb0, kb1);
+                }
                 const int m0 = tm * kBM, n0 = tn * BN;
                 for (int kb = kb0; kb < kb1; ++kb) {
                     B2G_TIC(t_empty);
@@ -1012,7 +1022,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             }
             if (warp == 2 && lane == 0) B2G_TOC(4, t_epi);
         }
-        if (lane == 0) bulk_wait<0>();  // this warp's TMA stores have completed
+        // this warp's TMA stores have read their staging boxes (their global writes complete
+        // on their own; the kernel's completion makes them visible)
+        if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
     }
 

@@ -427,7 +427,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             if (warp == 2 && lane == 0) B2G_TOC(4, t_epi);
             if (warp == 2 && lane == 0) B2G_MARK(7);
         }
-        if (lane == 0) bulk_wait<0>();  // this warp's TMA stores have completed
+        // this warp's TMA stores have read their staging boxes (their global writes complete
+        // on their own; the kernel's completion makes them visible)
+        if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
         if (warp == 2 && lane == 0) B2G_MARK(8);
     }
