@@ -124,15 +124,23 @@ TileGeom geom(int tile) {
     }
 }
 
-// `peers`: the fused all-gather instantiation (the swapped-operand kernel has none).
-const void* kernel_ptr(int tile, bool peers = false) {
+// `peers`: the fused all-gather instantiation (the swapped-operand kernel has none);
+// `plain`: the 1-CTA kernels' plain-path instantiation (no split-K, FP32 accumulation, plain
+// store, no peers; see gemm_sm100_1cta).
+const void* kernel_ptr(int tile, bool peers = false, bool plain = false) {
     switch (tile) {
         case B2G_TILE_128x128:
-            return peers ? (const void*)gemm_sm100_1cta<128, true> : (const void*)gemm_sm100_1cta<128>;
+            return peers ? (const void*)gemm_sm100_1cta<128, true>
+                         : plain ? (const void*)gemm_sm100_1cta<128, false, true>
+                                 : (const void*)gemm_sm100_1cta<128>;
         case B2G_TILE_128x256:
-            return peers ? (const void*)gemm_sm100_1cta<256, true> : (const void*)gemm_sm100_1cta<256>;
+            return peers ? (const void*)gemm_sm100_1cta<256, true>
+                         : plain ? (const void*)gemm_sm100_1cta<256, false, true>
+                                 : (const void*)gemm_sm100_1cta<256>;
         case B2G_TILE_128x64:
-            return peers ? (const void*)gemm_sm100_1cta<64, true> : (const void*)gemm_sm100_1cta<64>;
+            return peers ? (const void*)gemm_sm100_1cta<64, true>
+                         : plain ? (const void*)gemm_sm100_1cta<64, false, true>
+                                 : (const void*)gemm_sm100_1cta<64>;
         case B2G_TILE_256x512_2SM:
             return peers ? (const void*)gemm_sm100_2cta<512, true> : (const void*)gemm_sm100_2cta<512>;
         case B2G_TILE_SWAP_AB: return (const void*)gemm_sm100_swap<64>;
@@ -180,19 +188,25 @@ int max_stages_for(int tile, int smem_optin, int epi_boxes = 8, int a_rows = kBM
     return s;
 }
 
-int ensure_kernel_attrs(int tile, const DeviceInfo& di, bool peers = false) {
-    static bool done[2][7][kMaxDevices] = {};
+int ensure_kernel_attrs(int tile, const DeviceInfo& di, bool peers = false, bool plain = false) {
+    static bool done[3][7][kMaxDevices] = {};
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
-    if (di.device < kMaxDevices && done[peers][tile][di.device]) return B2G_OK;
-    cudaError_t e = cudaFuncSetAttribute(kernel_ptr(tile, peers),
+    const int v = peers ? 1 : plain ? 2 : 0;
+    if (di.device < kMaxDevices && done[v][tile][di.device]) return B2G_OK;
+    cudaError_t e = cudaFuncSetAttribute(kernel_ptr(tile, peers, plain),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          di.smem_optin);
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "cudaFuncSetAttribute(tile %d, max dynamic smem %d): %s", tile,
                     di.smem_optin, cudaGetErrorString(e));
-    if (di.device < kMaxDevices) done[peers][tile][di.device] = true;
+    if (di.device < kMaxDevices) done[v][tile][di.device] = true;
     return B2G_OK;
+}
+
+// Whether a 1-CTA launch with these parameters takes the plain-path instantiation.
+bool plain_path(const GemmParams& p) {
+    return p.splits == 1 && !p.csplit && !p.acc_f16 && !p.epilogue && p.peers.n == 0;
 }
 
 // Clusters of two that can be resident at once (GPCs with an odd SM count leave one idle).
@@ -373,17 +387,27 @@ cudaError_t launch_gemm_t(int tile, const CUtensorMap& tmA, const CUtensorMap& t
                           const CUtensorMap& tmBt, const CUtensorMap& tmD, const GemmParams& p,
                           const DeviceInfo& di, size_t smem, cudaStream_t s, int threads,
                           int& grid) {
+    const bool plain = !PEERS && plain_path(p);
     switch (tile) {
         case B2G_TILE_128x128:
             grid = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
+            if (plain)
+                return launch_exc(gemm_sm100_1cta<128, false, true>, grid, threads, smem, s, 1,
+                                  tmA, tmB, tmD, p);
             return launch_exc(gemm_sm100_1cta<128, PEERS>, grid, threads, smem, s,
                               p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
         case B2G_TILE_128x256:
             grid = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
+            if (plain)
+                return launch_exc(gemm_sm100_1cta<256, false, true>, grid, threads, smem, s, 1,
+                                  tmA, tmB, tmD, p);
             return launch_exc(gemm_sm100_1cta<256, PEERS>, grid, threads, smem, s,
                               p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
         case B2G_TILE_128x64:
             grid = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
+            if (plain)
+                return launch_exc(gemm_sm100_1cta<64, false, true>, grid, threads, smem, s, 1,
+                                  tmA, tmB, tmD, p);
             return launch_exc(gemm_sm100_1cta<64, PEERS>, grid, threads, smem, s,
                               p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
         case B2G_TILE_256x512_2SM:
@@ -406,6 +430,8 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
                 const DeviceInfo& di, size_t smem, cudaStream_t s, int epi_warps) {
     const bool peers = p.peers.n > 0;
     if (int rc = ensure_kernel_attrs(tile, di, peers)) return rc;
+    if (geom(tile).ctas == 1 && tile != B2G_TILE_SWAP_AB && !peers && plain_path(p))
+        if (int rc = ensure_kernel_attrs(tile, di, false, true)) return rc;
     int grid = 0;
     const int threads = gemm_threads(epi_warps);
     cudaError_t e = peers ? launch_gemm_t<true>(tile, tmA, tmB, tmBt, tmD, p, di, smem, s,
@@ -1107,9 +1133,11 @@ B2G_EXPORT int b2g_instr_read(unsigned long long* out, int n_ctas) {
     return cudaMemcpyToSymbol(g_b2g_instr, zeros, sizeof(zeros)) == cudaSuccess ? B2G_OK
                                                                                 : B2G_ERR_CUDA;
 }
-// Copy out the marks of the first n_ctas (<= 1024) CTAs of the most recent launch: 16 per CTA.
+// Copy out the marks of the first n_ctas (<= 1024) CTAs of the most recent launch:
+// 2 x kTlMarks per CTA (global timer, then clock64).
 B2G_EXPORT int b2g_instr_timeline(unsigned long long* out, int n_ctas) {
-    return cudaMemcpyFromSymbol(out, g_b2g_tl, sizeof(unsigned long long) * 16 * (size_t)n_ctas) ==
+    return cudaMemcpyFromSymbol(out, g_b2g_tl,
+                                sizeof(unsigned long long) * 2 * kTlMarks * (size_t)n_ctas) ==
                    cudaSuccess
                ? B2G_OK
                : B2G_ERR_CUDA;

@@ -363,7 +363,9 @@ __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiSc
                 for (int h = 0; h < 2; ++h) {
                     tmem_ld_32x32b_x32(trow + (uint32_t)(cc * 64 + h * 32), r);
                     tmem_ld_wait();
+                    if (threadIdx.x == 64 && c == c_first && i == 0 && h == 0) B2G_MARK(16);
                     epi_box_put32<ACC16, EPI>(e, box, n_first + cc * 64, h, r, lane);
+                    if (threadIdx.x == 64 && c == c_first && i == 0 && h == 0) B2G_MARK(17);
                 }
             }
             fence_proxy_async_smem();
@@ -374,6 +376,7 @@ __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiSc
                                       n_first + (c + i * e.c_step) * 64, row0, e.store_pol);
                 bulk_commit();
             }
+            if (threadIdx.x == 64 && c == c_first) B2G_MARK(18);
             for (int i = 0; i < cn; ++i)  // the TMA stores and these read the boxes together
                 epi_box_push<PEERS>(p, e, stage0 + (uint32_t)i * kEpiBoxBytes,
                                     n_first + (c + i * e.c_step) * 64, row0, lane);
@@ -392,12 +395,15 @@ __device__ __forceinline__ void epilogue_rows_t(const GemmParams& p, const EpiSc
         for (int h = 0; h < 2; ++h) {
             tmem_ld_32x32b_x32(trow + (uint32_t)(c * 64 + h * 32), r);
             tmem_ld_wait();
+            if (threadIdx.x == 64 && c == c_first && h == 0) B2G_MARK(16);
             epi_box_put32<ACC16, EPI>(e, box, col, h, r, lane);
+            if (threadIdx.x == 64 && c == c_first && h == 0) B2G_MARK(17);
         }
         if (e.d_tma)
             epi_box_store(e, tmD, box, col, row0, lane, seq);
         else
             epi_box_store_rows(p, e, box, col, row0, lane);
+        if (threadIdx.x == 64 && c == c_first) B2G_MARK(18);
         epi_box_push<PEERS>(p, e, box, col, row0, lane);
     }
 }
@@ -765,12 +771,28 @@ __device__ __forceinline__ void csplit_epilogue(const GemmParams& p, const EpiSc
 }
 
 // PEERS: the fused all-gather instantiation (every staged box of D also goes to p.peers).
-template <int BN, bool PEERS = false>
+// PLAIN: the instantiation for the common case -- no split-K, FP32 accumulation, plain store,
+// no peers -- in which those modes are compile-time constants, so the code a launch runs is
+// only the plain path (fewer instruction-cache misses on its way, no integer divisions for
+// split ranges); the host launches it whenever p allows.
+template <int BN, bool PEERS = false, bool PLAIN = false>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_1cta(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
+    static_assert(!(PEERS && PLAIN), "the plain path has no peers");
     using TT = TileTraits<BN>;
+    const int splits = PLAIN ? 1 : p.splits;
+    const bool csplit = PLAIN ? false : p.csplit != 0;
+    // k-blocks [kb0, kb1) of split s of a tile
+    const auto krange = [&](int s, int& kb0, int& kb1) {
+        if (PLAIN) {
+            kb0 = 0;
+            kb1 = p.num_kb;
+        } else {
+            split_range(p, s, kb0, kb1);
+        }
+    };
     clock_mark(0);
     B2G_TIC(t_life);
     if (threadIdx.x == 0) B2G_MARK(0);
@@ -808,8 +830,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             mbar_init(tfull0 + 8 * b, 1);
             mbar_init(tempty0 + 8 * b, (uint32_t)epi_warps);  // one arrive per epilogue warp
         }
-        for (int k = 0; k < kCsMaxPieces; ++k) mbar_init(rbar0 + 8 * k, 1);  // owner's arm
-        mbar_init(peers_free, p.recv_ring ? (uint32_t)(p.splits - 1) : 1u);
+        if (csplit) {
+            for (int k = 0; k < kCsMaxPieces; ++k) mbar_init(rbar0 + 8 * k, 1);  // owner's arm
+            mbar_init(peers_free, p.recv_ring ? (uint32_t)(splits - 1) : 1u);
+        }
         mbar_init(drain, 1);
         ctl->abort = 0;
         ctl->never = 0;
@@ -827,7 +851,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     tc_fence_before();
     __syncthreads();
     // cluster split-K: every CTA's receive barriers exist before any peer stores into them
-    if (p.csplit) cluster_sync();
+    if (csplit) cluster_sync();
     tc_fence_after();
     if (threadIdx.x == 0) B2G_MARK(1);
     const uint32_t tmem_base = ctl->tmem_base;
@@ -837,9 +861,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     // kernel may still be running, so its first load follows the wait directly
     int tm0 = 0, tn0 = 0, kb00 = 0, kb10 = 0;
     if (warp == 0 && lane == 0 && (int)blockIdx.x < p.num_units) {
-        const int t = (int)blockIdx.x / p.splits;
+        const int t = (int)blockIdx.x / splits;
         tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm0, tn0);
-        split_range(p, (int)blockIdx.x - t * p.splits, kb00, kb10);
+        krange((int)blockIdx.x - t * splits, kb00, kb10);
     }
     // everything above overlapped the previous kernel; global memory only from here on
     grid_dep_wait();
@@ -857,9 +881,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
                 int tm = tm0, tn = tn0, kb0 = kb00, kb1 = kb10;
                 if (u != (int)blockIdx.x) {
-                    const int t = u / p.splits;
+                    const int t = u / splits;
                     tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
-                    split_range(p, u - t * p.splits, kb0, kb1);
+                    krange(u - t * splits, kb0, kb1);
                 }
                 const int m0 = tm * kBM, n0 = tn * BN;
                 for (int kb = kb0; kb < kb1; ++kb) {
@@ -869,6 +893,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                         break;
                     }
                     B2G_TOC(0, t_empty);
+                    if (issued == 0) B2G_MARK(15);
                     const uint32_t fb = full0 + 8 * stage;
                     mbar_arrive_expect_tx(fb, p.stage_tx);
                     tma_load_2d(sA + stage * stride, &tmA, fb, kb * kBK, m0);
@@ -929,7 +954,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 const int buf = it & 1;
                 const uint32_t use = (uint32_t)(it >> 1) & 1u;
                 int kb0, kb1;
-                split_range(p, u % p.splits, kb0, kb1);
+                krange(u % splits, kb0, kb1);
                 B2G_TIC(t_te);
                 if (!mbar_wait_warp(tempty0 + 8 * buf, use ^ 1u, w)) {
                     ok = false;
@@ -982,7 +1007,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const int c_first = (warp - 2) >> 2;  // first 64-column chunk of this warp
         const EpiScalars es = epi_scalars(p, epi_warps);
         const uint32_t stage0 = sEpi + (uint32_t)((warp - 2) * es.bufs) * kEpiBoxBytes;
-        const bool acc16 = p.acc_f16 != 0, epi = p.epilogue != 0;
+        const bool acc16 = PLAIN ? false : p.acc_f16 != 0, epi = PLAIN ? false : p.epilogue != 0;
         uint32_t seq = 0;
         int it = 0;
         for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {
@@ -993,8 +1018,9 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             if (!__all_sync(0xffffffffu, ok)) break;
             if (warp == 2 && lane == 0) B2G_TOC(3, t_tf);
             B2G_TIC(t_epi);
+            if (threadIdx.x == 64 && it == 0) B2G_MARK(12);
             tc_fence_after();
-            const int t = u / p.splits;
+            const int t = u / splits;
             int tm, tn;
             tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
             const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
@@ -1003,16 +1029,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(tempty0 + 8 * buf);
             };
-            if (p.splits > 1 && p.csplit) {
+            if (splits > 1 && csplit) {
                 // tmem_full: every load of this CTA's ring has landed and every MMA reading it
                 // is done, so the peers may overwrite the ring with their partials
                 const int s = (int)cluster_ctarank();
-                if (p.recv_ring && threadIdx.x == 64) csplit_ring_free(peers_free, p.splits, s, 1, 0);
+                if (p.recv_ring && threadIdx.x == 64) csplit_ring_free(peers_free, splits, s, 1, 0);
                 csplit_epilogue<PEERS>(p, es, &tmD, tbase, q, BN, tm * kBM + q * 32, tn * BN,
                                        c_first, stage0, lane, seq, epi, sRecv, rbar0, peers_free,
                                        w, release, s, 1, 0);
-            } else if (p.splits > 1) {
-                splitk_epilogue<PEERS>(p, es, &tmD, tbase, t, u - t * p.splits, 0, 1, q, warp - 2, BN,
+            } else if (splits > 1) {
+                splitk_epilogue<PEERS>(p, es, &tmD, tbase, t, u - t * splits, 0, 1, q, warp - 2, BN,
                                 tm * kBM + q * 32, tn * BN, c_first, stage0, lane, seq, epi,
                                 release);
             } else {
@@ -1021,16 +1047,18 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 release();
             }
             if (warp == 2 && lane == 0) B2G_TOC(4, t_epi);
+            if (threadIdx.x == 64) B2G_MARK(13);
         }
         // this warp's TMA stores have read their staging boxes (their global writes complete
         // on their own; the kernel's completion makes them visible)
         if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
+        if (threadIdx.x == 64) B2G_MARK(14);
     }
 
     __syncthreads();
     // cluster split-K: no CTA leaves while a peer may still store into its receive slots
-    if (p.csplit) cluster_sync();
+    if (csplit) cluster_sync();
     if (threadIdx.x == 0) B2G_MARK(10);
     if (warp == 1) {
         __syncwarp();

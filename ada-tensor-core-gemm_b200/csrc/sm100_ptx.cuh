@@ -155,10 +155,17 @@ __device__ unsigned long long g_b2g_instr[1024][kInstrSlots];
 // of the CTA reaches it. 1-CTA kernel: 0 entry, 1 barriers and TMEM ready (cluster synced),
 // 2 after griddepcontrol.wait, 3 first TMA load issued, 4 first stage full at the MMA warp,
 // 5 accumulator committed, 6-9 cluster split-K epilogue of thread 128 (start, sends issued,
-// receive wait done, end), 10 after the teardown barriers, 11 producer issued its last load.
-__device__ unsigned long long g_b2g_tl[1024][16];
-#define B2G_MARK(i) \
-    if (blockIdx.x < 1024) g_b2g_tl[blockIdx.x][i] = globaltimer_ns()
+// receive wait done, end), 10 after the teardown barriers, 11 producer issued its last load,
+// 12-14 epilogue thread 64: first accumulator ready, last unit's epilogue done, stores read.
+// 15 producer's first empty wait done; 16-18 epilogue thread 64, first chunk: TMEM load
+// done, first half staged, store issued. Slots 24 + i hold clock64() at mark i.
+constexpr int kTlMarks = 24;
+__device__ unsigned long long g_b2g_tl[1024][2 * kTlMarks];
+#define B2G_MARK(i)                                                    \
+    if (blockIdx.x < 1024) {                                           \
+        g_b2g_tl[blockIdx.x][kTlMarks + (i)] = (unsigned long long)clock64(); \
+        g_b2g_tl[blockIdx.x][i] = globaltimer_ns();                    \
+    }
 #else
 #define B2G_MARK(i)
 #define B2G_TOC64(slot, v)
