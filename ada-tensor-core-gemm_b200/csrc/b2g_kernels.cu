@@ -142,12 +142,18 @@ const void* kernel_ptr(int tile, bool peers = false, bool plain = false) {
                          : plain ? (const void*)gemm_sm100_1cta<64, false, true>
                                  : (const void*)gemm_sm100_1cta<64>;
         case B2G_TILE_256x512_2SM:
-            return peers ? (const void*)gemm_sm100_2cta<512, true> : (const void*)gemm_sm100_2cta<512>;
+            return peers ? (const void*)gemm_sm100_2cta<512, true>
+                         : plain ? (const void*)gemm_sm100_2cta<512, false, true>
+                                 : (const void*)gemm_sm100_2cta<512>;
         case B2G_TILE_SWAP_AB: return (const void*)gemm_sm100_swap<64>;
         case B2G_TILE_256x128_2SM:
-            return peers ? (const void*)gemm_sm100_2cta<128, true> : (const void*)gemm_sm100_2cta<128>;
+            return peers ? (const void*)gemm_sm100_2cta<128, true>
+                         : plain ? (const void*)gemm_sm100_2cta<128, false, true>
+                                 : (const void*)gemm_sm100_2cta<128>;
         default:
-            return peers ? (const void*)gemm_sm100_2cta<256, true> : (const void*)gemm_sm100_2cta<256>;
+            return peers ? (const void*)gemm_sm100_2cta<256, true>
+                         : plain ? (const void*)gemm_sm100_2cta<256, false, true>
+                                 : (const void*)gemm_sm100_2cta<256>;
     }
 }
 
@@ -204,9 +210,11 @@ int ensure_kernel_attrs(int tile, const DeviceInfo& di, bool peers = false, bool
     return B2G_OK;
 }
 
-// Whether a 1-CTA launch with these parameters takes the plain-path instantiation.
-bool plain_path(const GemmParams& p) {
-    return p.splits == 1 && !p.csplit && !p.acc_f16 && !p.epilogue && p.peers.n == 0;
+// Whether a launch with these parameters takes the plain-path instantiation of its kernel
+// (the 1-CTA kernels read B in either layout alike; the pair kernel's plain path is N x K only).
+bool plain_path(const GemmParams& p, int ctas) {
+    return p.splits == 1 && !p.csplit && !p.acc_f16 && !p.epilogue && p.peers.n == 0 &&
+           (ctas == 1 || !p.b_mn_major);
 }
 
 // Clusters of two that can be resident at once (GPCs with an odd SM count leave one idle).
@@ -387,7 +395,7 @@ cudaError_t launch_gemm_t(int tile, const CUtensorMap& tmA, const CUtensorMap& t
                           const CUtensorMap& tmBt, const CUtensorMap& tmD, const GemmParams& p,
                           const DeviceInfo& di, size_t smem, cudaStream_t s, int threads,
                           int& grid) {
-    const bool plain = !PEERS && plain_path(p);
+    const bool plain = !PEERS && plain_path(p, geom(tile).ctas);
     switch (tile) {
         case B2G_TILE_128x128:
             grid = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
@@ -412,14 +420,23 @@ cudaError_t launch_gemm_t(int tile, const CUtensorMap& tmA, const CUtensorMap& t
                               p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
         case B2G_TILE_256x512_2SM:
             grid = 2 * (p.csplit ? p.num_units : std::min(p.num_units, max_pair_clusters(di, smem)));
+            if (plain)
+                return launch_exc(gemm_sm100_2cta<512, false, true>, grid, threads, smem, s, 2,
+                                  tmA, tmB, tmBt, tmD, p);
             return launch_exc(gemm_sm100_2cta<512, PEERS>, grid, threads, smem, s,
                               p.csplit ? 2 * p.splits : 2, tmA, tmB, tmBt, tmD, p);
         case B2G_TILE_256x128_2SM:
             grid = 2 * (p.csplit ? p.num_units : std::min(p.num_units, max_pair_clusters(di, smem)));
+            if (plain)
+                return launch_exc(gemm_sm100_2cta<128, false, true>, grid, threads, smem, s, 2,
+                                  tmA, tmB, tmBt, tmD, p);
             return launch_exc(gemm_sm100_2cta<128, PEERS>, grid, threads, smem, s,
                               p.csplit ? 2 * p.splits : 2, tmA, tmB, tmBt, tmD, p);
         default:
             grid = 2 * (p.csplit ? p.num_units : std::min(p.num_units, max_pair_clusters(di, smem)));
+            if (plain)
+                return launch_exc(gemm_sm100_2cta<256, false, true>, grid, threads, smem, s, 2,
+                                  tmA, tmB, tmBt, tmD, p);
             return launch_exc(gemm_sm100_2cta<256, PEERS>, grid, threads, smem, s,
                               p.csplit ? 2 * p.splits : 2, tmA, tmB, tmBt, tmD, p);
     }
@@ -430,7 +447,7 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
                 const DeviceInfo& di, size_t smem, cudaStream_t s, int epi_warps) {
     const bool peers = p.peers.n > 0;
     if (int rc = ensure_kernel_attrs(tile, di, peers)) return rc;
-    if (geom(tile).ctas == 1 && tile != B2G_TILE_SWAP_AB && !peers && plain_path(p))
+    if (tile != B2G_TILE_SWAP_AB && !peers && plain_path(p, geom(tile).ctas))
         if (int rc = ensure_kernel_attrs(tile, di, false, true)) return rc;
     int grid = 0;
     const int threads = gemm_threads(epi_warps);

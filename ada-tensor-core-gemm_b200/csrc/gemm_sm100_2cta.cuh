@@ -78,13 +78,13 @@ __device__ __forceinline__ void mma_kblock_pair(uint32_t d_tmem, uint64_t ad, ui
 // Work unit u -> tile index t, output tile (tm, tn), first output column and width of the
 // unit, whether it is a tail slice, and its split-K index (split-K and tail slices are never
 // combined: with splits > 1, unit u is split u % splits of tile u / splits).
-template <int BNP>
+template <int BNP, bool PLAIN = false>
 __device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& t, int& tm, int& tn,
                                           int& n_first, int& width, bool& tail, int& split) {
     t = u;
     int sub = 0;
     split = 0;
-    if (p.splits > 1) {
+    if (!PLAIN && p.splits > 1) {
         t = u / p.splits;
         split = u - t * p.splits;
         tail = false;
@@ -102,12 +102,28 @@ __device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& t, in
 }
 
 // PEERS: the fused all-gather instantiation (every staged box of D also goes to p.peers).
-template <int BNP, bool PEERS = false>
+// PLAIN: the instantiation for the common case -- no split-K, FP32 accumulation, plain store,
+// B stored N x K, no peers -- with those modes as compile-time constants (see gemm_sm100_1cta).
+template <int BNP, bool PEERS = false, bool PLAIN = false>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_2cta(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmBt,
                     const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
+    static_assert(!(PEERS && PLAIN), "the plain path has no peers");
+    const int splits = PLAIN ? 1 : p.splits;
+    const bool csplit = PLAIN ? false : p.csplit != 0;
+    const bool b_mn = PLAIN ? false : p.b_mn_major != 0;
+    const bool b_kn3d = PLAIN ? false : p.b_kn3d != 0;
+    // k-blocks [kb0, kb1) of split s of a tile
+    const auto krange = [&](int s, int& kb0, int& kb1) {
+        if (PLAIN) {
+            kb0 = 0;
+            kb1 = p.num_kb;
+        } else {
+            split_range(p, s, kb0, kb1);
+        }
+    };
     clock_mark(0);
     B2G_TIC(t_life);
     if (threadIdx.x == 0) B2G_MARK(0);
@@ -145,8 +161,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             mbar_init(full0 + 8 * s, 1);   // only the leader's copy is used
             mbar_init(empty0 + 8 * s, 1);  // one multicast commit per use
         }
-        for (int k = 0; k < kCsMaxPieces; ++k) mbar_init(rbar0 + 8 * k, 1);  // owner's arm
-        mbar_init(peers_free, p.recv_ring ? (uint32_t)(p.splits - 1) : 1u);
+        if (csplit) {
+            for (int k = 0; k < kCsMaxPieces; ++k) mbar_init(rbar0 + 8 * k, 1);  // owner's arm
+            mbar_init(peers_free, p.recv_ring ? (uint32_t)(splits - 1) : 1u);
+        }
         for (int b = 0; b < 2; ++b) {
             mbar_init(tfull0 + 8 * b, 1);
             mbar_init(tempty0 + 8 * b, 2u * epi_warps);  // epilogue warps x 2 CTAs (leader's copy)
@@ -191,8 +209,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             for (int u = cluster_id; u < p.num_units && ok; u += num_clusters) {
                 int t, tm, tn, n_first, width, split, kb0, kb1;
                 bool tail;
-                pair_unit<BNP>(p, u, t, tm, tn, n_first, width, tail, split);
-                split_range(p, split, kb0, kb1);
+                pair_unit<BNP, PLAIN>(p, u, t, tm, tn, n_first, width, tail, split);
+                krange(split, kb0, kb1);
                 const int m0 = tm * kPairBM + (int)rank * 128;
                 // B of the unit in 256-column halves; this CTA loads hw rows of each
                 const int nh = width > kPairBN ? 2 : 1;
@@ -216,10 +234,10 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     for (int h = 0; h < nh; ++h) {
                         const int n0 = n_first + h * kPairBN + (int)rank * hw;
                         const uint32_t dst = sB + stage * PT::kBStageBytes + (uint32_t)h * kHalfBytes;
-                        if (p.b_kn3d) {
+                        if (b_kn3d) {
                             // B is K x N: the hw / 64 boxes of 64 columns x 64 k-rows at once
                             tma_load_3d_pair(dst, mapB, fb, 0, kb * kBK, n0 >> 6);
-                        } else if (p.b_mn_major) {
+                        } else if (b_mn) {
                             // B is K x N: hw / 64 boxes of 64 columns x 64 k-rows
                             for (int j = 0; j < (hw >> 6); ++j)
                                 tma_load_2d_pair(dst + (uint32_t)j * kMnBoxBytes, mapB, fb,
@@ -252,8 +270,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             // operand address is below 256 KiB, so the 14-bit field never carries.
             const WaitCtx w{p.timeout_ns, abort_flag, kErrWaitMma};
             const uint64_t adesc0 = sdesc_sw128(sA, 16, 1024);
-            const uint64_t bdesc0 = b_desc0(sB, p.b_mn_major);
-            const uint32_t bk = b_kstep(p.b_mn_major);
+            const uint64_t bdesc0 = b_desc0(sB, b_mn);
+            const uint32_t bk = b_kstep(b_mn);
             constexpr uint32_t kAStep = kHalfBytes >> 4;         // descriptor units per stage
             constexpr uint32_t kBStep = PT::kBStageBytes >> 4;
             constexpr uint32_t kBHalf = kHalfBytes >> 4;         // second 256-column half of B
@@ -264,8 +282,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             for (int u = cluster_id; u < p.num_units && ok; u += num_clusters, ++it) {
                 int t, tm, tn, n_first, width, split, kb0, kb1;
                 bool tail;
-                pair_unit<BNP>(p, u, t, tm, tn, n_first, width, tail, split);
-                split_range(p, split, kb0, kb1);
+                pair_unit<BNP, PLAIN>(p, u, t, tm, tn, n_first, width, tail, split);
+                krange(split, kb0, kb1);
                 const uint32_t idesc = tail ? p.idesc_tail : p.idesc;
                 const bool two_halves = PT::kWide && width > kPairBN;
                 // 256-wide: double-buffered accumulators (buffer it & 1, reused every 2nd unit);
@@ -367,7 +385,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const int c_first = (warp - 2) >> 2;
         const EpiScalars es = epi_scalars(p, epi_warps);
         const uint32_t stage0 = sEpi + (uint32_t)((warp - 2) * es.bufs) * kEpiBoxBytes;
-        const bool acc16 = p.acc_f16 != 0, epi = p.epilogue != 0;
+        const bool acc16 = PLAIN ? false : p.acc_f16 != 0, epi = PLAIN ? false : p.epilogue != 0;
         uint32_t seq = 0;
         int it = 0;
         for (int u = cluster_id; u < p.num_units; u += num_clusters, ++it) {
@@ -381,7 +399,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             tc_fence_after();
             int t, tm, tn, n_first, width, split;
             bool tail;
-            pair_unit<BNP>(p, u, t, tm, tn, n_first, width, tail, split);
+            pair_unit<BNP, PLAIN>(p, u, t, tm, tn, n_first, width, tail, split);
             const int row0 = tm * kPairBM + (int)rank * 128 + q * 32;
             const uint32_t tq = tmem_base + ((uint32_t)(q * 32) << 16);
             // accumulator buffer / half `b` has been read: the leader may reuse it
@@ -405,15 +423,15 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 }
             } else {
                 const uint32_t tbase = tq + (uint32_t)(buf * kPairBN);
-                if (p.splits > 1 && p.csplit) {
+                if (splits > 1 && csplit) {
                     const int s = (int)(crank >> 1);
                     if (p.recv_ring && threadIdx.x == 64)
-                        csplit_ring_free(peers_free, p.splits, s, 2, (int)rank);
+                        csplit_ring_free(peers_free, splits, s, 2, (int)rank);
                     csplit_epilogue<PEERS>(p, es, &tmD, tbase, q, BNP < kPairBN ? BNP : kPairBN,
                                            row0, n_first, c_first, stage0, lane, seq, epi, sRecv,
                                            rbar0, peers_free, w, [&] { release(buf); }, s, 2,
                                            (int)rank);
-                } else if (p.splits > 1) {
+                } else if (splits > 1) {
                     splitk_epilogue<PEERS>(p, es, &tmD, tbase, t, split, (int)rank, 2, q,
                                            warp - 2, BNP < kPairBN ? BNP : kPairBN, row0, n_first,
                                            c_first, stage0, lane, seq, epi,
