@@ -124,38 +124,36 @@ TileGeom geom(int tile) {
     }
 }
 
-// `peers`: the fused all-gather instantiation (the swapped-operand kernel has none);
-// `plain`: the 1-CTA kernels' plain-path instantiation (no split-K, FP32 accumulation, plain
-// store, no peers; see gemm_sm100_1cta).
-const void* kernel_ptr(int tile, bool peers = false, bool plain = false) {
+// Instantiation of a GEMM kernel: the general one, the fused all-gather one (peers), the
+// plain path (no split-K, FP32 accumulation, plain store, no peers; the pair kernel's also
+// N x K B only) or split-K reduced in a cluster (FP32 accumulation, no peers); see
+// gemm_sm100_1cta. The swapped-operand kernel has one instantiation.
+enum KernelVariant { kVarGeneral = 0, kVarPeers = 1, kVarPlain = 2, kVarCsplit = 3 };
+
+#define B2G_VARIANTS_1CTA(BN)                                                        \
+    (v == kVarPeers    ? (const void*)gemm_sm100_1cta<BN, true>                      \
+     : v == kVarPlain  ? (const void*)gemm_sm100_1cta<BN, false, true>               \
+     : v == kVarCsplit ? (const void*)gemm_sm100_1cta<BN, false, false, true>        \
+                       : (const void*)gemm_sm100_1cta<BN>)
+#define B2G_VARIANTS_2CTA(BNP)                                                       \
+    (v == kVarPeers    ? (const void*)gemm_sm100_2cta<BNP, true>                     \
+     : v == kVarPlain  ? (const void*)gemm_sm100_2cta<BNP, false, true>              \
+     : v == kVarCsplit ? (const void*)gemm_sm100_2cta<BNP, false, false, true>       \
+                       : (const void*)gemm_sm100_2cta<BNP>)
+
+const void* kernel_ptr(int tile, int v = kVarGeneral) {
     switch (tile) {
-        case B2G_TILE_128x128:
-            return peers ? (const void*)gemm_sm100_1cta<128, true>
-                         : plain ? (const void*)gemm_sm100_1cta<128, false, true>
-                                 : (const void*)gemm_sm100_1cta<128>;
-        case B2G_TILE_128x256:
-            return peers ? (const void*)gemm_sm100_1cta<256, true>
-                         : plain ? (const void*)gemm_sm100_1cta<256, false, true>
-                                 : (const void*)gemm_sm100_1cta<256>;
-        case B2G_TILE_128x64:
-            return peers ? (const void*)gemm_sm100_1cta<64, true>
-                         : plain ? (const void*)gemm_sm100_1cta<64, false, true>
-                                 : (const void*)gemm_sm100_1cta<64>;
-        case B2G_TILE_256x512_2SM:
-            return peers ? (const void*)gemm_sm100_2cta<512, true>
-                         : plain ? (const void*)gemm_sm100_2cta<512, false, true>
-                                 : (const void*)gemm_sm100_2cta<512>;
+        case B2G_TILE_128x128: return B2G_VARIANTS_1CTA(128);
+        case B2G_TILE_128x256: return B2G_VARIANTS_1CTA(256);
+        case B2G_TILE_128x64: return B2G_VARIANTS_1CTA(64);
+        case B2G_TILE_256x512_2SM: return B2G_VARIANTS_2CTA(512);
         case B2G_TILE_SWAP_AB: return (const void*)gemm_sm100_swap<64>;
-        case B2G_TILE_256x128_2SM:
-            return peers ? (const void*)gemm_sm100_2cta<128, true>
-                         : plain ? (const void*)gemm_sm100_2cta<128, false, true>
-                                 : (const void*)gemm_sm100_2cta<128>;
-        default:
-            return peers ? (const void*)gemm_sm100_2cta<256, true>
-                         : plain ? (const void*)gemm_sm100_2cta<256, false, true>
-                                 : (const void*)gemm_sm100_2cta<256>;
+        case B2G_TILE_256x128_2SM: return B2G_VARIANTS_2CTA(128);
+        default: return B2G_VARIANTS_2CTA(256);
     }
 }
+#undef B2G_VARIANTS_1CTA
+#undef B2G_VARIANTS_2CTA
 
 // Epilogue staging boxes (4 KiB each) of a launch, shared out among its epilogue warps: 16
 // for K <= 256 (two per warp, so the 8 epilogue warps store chunks in fenced pairs: 16384^2 x
@@ -194,13 +192,12 @@ int max_stages_for(int tile, int smem_optin, int epi_boxes = 8, int a_rows = kBM
     return s;
 }
 
-int ensure_kernel_attrs(int tile, const DeviceInfo& di, bool peers = false, bool plain = false) {
-    static bool done[3][7][kMaxDevices] = {};
+int ensure_kernel_attrs(int tile, const DeviceInfo& di, int v = kVarGeneral) {
+    static bool done[4][7][kMaxDevices] = {};
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
-    const int v = peers ? 1 : plain ? 2 : 0;
     if (di.device < kMaxDevices && done[v][tile][di.device]) return B2G_OK;
-    cudaError_t e = cudaFuncSetAttribute(kernel_ptr(tile, peers, plain),
+    cudaError_t e = cudaFuncSetAttribute(kernel_ptr(tile, v),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          di.smem_optin);
     if (e != cudaSuccess)
@@ -210,11 +207,14 @@ int ensure_kernel_attrs(int tile, const DeviceInfo& di, bool peers = false, bool
     return B2G_OK;
 }
 
-// Whether a launch with these parameters takes the plain-path instantiation of its kernel
-// (the 1-CTA kernels read B in either layout alike; the pair kernel's plain path is N x K only).
-bool plain_path(const GemmParams& p, int ctas) {
-    return p.splits == 1 && !p.csplit && !p.acc_f16 && !p.epilogue && p.peers.n == 0 &&
-           (ctas == 1 || !p.b_mn_major);
+// The instantiation a launch with these parameters takes (tile kernels with `ctas` CTAs per
+// tile; the 1-CTA kernels' plain path reads B in either layout, the pair kernel's N x K only).
+int kernel_variant(const GemmParams& p, int ctas) {
+    if (p.peers.n > 0) return kVarPeers;
+    if (p.splits == 1 && !p.csplit && !p.acc_f16 && !p.epilogue && (ctas == 1 || !p.b_mn_major))
+        return kVarPlain;
+    if (p.splits > 1 && p.csplit) return kVarCsplit;
+    return kVarGeneral;
 }
 
 // Clusters of two that can be resident at once (GPCs with an odd SM count leave one idle).
@@ -223,6 +223,7 @@ int max_pair_clusters(const DeviceInfo& di, size_t smem) {
     static std::mutex mu;
     std::lock_guard<std::mutex> lock(mu);
     if (di.device < kMaxDevices && cache[di.device] > 0) return cache[di.device];
+    ensure_kernel_attrs(B2G_TILE_256x256_2SM, di);  // the occupancy query needs its smem limit
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * (di.sm_count / 2), 1, 1);
     cfg.blockDim = dim3(kMaxThreads, 1, 1);
@@ -381,7 +382,8 @@ bool cluster_fits(const DeviceInfo& di, int tile, int ctas, int threads, size_t 
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    const bool ok = cudaOccupancyMaxActiveClusters(&n, kernel_ptr(tile, peers), &cfg) ==
+    const bool ok = cudaOccupancyMaxActiveClusters(
+                        &n, kernel_ptr(tile, peers ? kVarPeers : kVarCsplit), &cfg) ==
                         cudaSuccess &&
                     n > 0;
     if (!ok) cudaGetLastError();
@@ -390,71 +392,67 @@ bool cluster_fits(const DeviceInfo& di, int tile, int ctas, int threads, size_t 
     return ok;
 }
 
-template <bool PEERS>
+// One launch of instantiation V (KernelVariant) of a tile kernel.
+template <int V>
 cudaError_t launch_gemm_t(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
                           const CUtensorMap& tmBt, const CUtensorMap& tmD, const GemmParams& p,
                           const DeviceInfo& di, size_t smem, cudaStream_t s, int threads,
                           int& grid) {
-    const bool plain = !PEERS && plain_path(p, geom(tile).ctas);
+    constexpr bool PEERS = V == kVarPeers, PLAIN = V == kVarPlain, CS = V == kVarCsplit;
+    const int grid1 = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
+    const int cl1 = p.csplit ? p.splits : 1;
+    const int grid2 =
+        2 * (p.csplit ? p.num_units : std::min(p.num_units, max_pair_clusters(di, smem)));
+    const int cl2 = p.csplit ? 2 * p.splits : 2;
     switch (tile) {
         case B2G_TILE_128x128:
-            grid = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
-            if (plain)
-                return launch_exc(gemm_sm100_1cta<128, false, true>, grid, threads, smem, s, 1,
-                                  tmA, tmB, tmD, p);
-            return launch_exc(gemm_sm100_1cta<128, PEERS>, grid, threads, smem, s,
-                              p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
+            grid = grid1;
+            return launch_exc(gemm_sm100_1cta<128, PEERS, PLAIN, CS>, grid, threads, smem, s, cl1,
+                              tmA, tmB, tmD, p);
         case B2G_TILE_128x256:
-            grid = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
-            if (plain)
-                return launch_exc(gemm_sm100_1cta<256, false, true>, grid, threads, smem, s, 1,
-                                  tmA, tmB, tmD, p);
-            return launch_exc(gemm_sm100_1cta<256, PEERS>, grid, threads, smem, s,
-                              p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
+            grid = grid1;
+            return launch_exc(gemm_sm100_1cta<256, PEERS, PLAIN, CS>, grid, threads, smem, s, cl1,
+                              tmA, tmB, tmD, p);
         case B2G_TILE_128x64:
-            grid = p.csplit ? p.num_units : std::min(p.num_units, di.sm_count);
-            if (plain)
-                return launch_exc(gemm_sm100_1cta<64, false, true>, grid, threads, smem, s, 1,
-                                  tmA, tmB, tmD, p);
-            return launch_exc(gemm_sm100_1cta<64, PEERS>, grid, threads, smem, s,
-                              p.csplit ? p.splits : 1, tmA, tmB, tmD, p);
+            grid = grid1;
+            return launch_exc(gemm_sm100_1cta<64, PEERS, PLAIN, CS>, grid, threads, smem, s, cl1,
+                              tmA, tmB, tmD, p);
         case B2G_TILE_256x512_2SM:
-            grid = 2 * (p.csplit ? p.num_units : std::min(p.num_units, max_pair_clusters(di, smem)));
-            if (plain)
-                return launch_exc(gemm_sm100_2cta<512, false, true>, grid, threads, smem, s, 2,
-                                  tmA, tmB, tmBt, tmD, p);
-            return launch_exc(gemm_sm100_2cta<512, PEERS>, grid, threads, smem, s,
-                              p.csplit ? 2 * p.splits : 2, tmA, tmB, tmBt, tmD, p);
+            grid = grid2;
+            return launch_exc(gemm_sm100_2cta<512, PEERS, PLAIN, CS>, grid, threads, smem, s, cl2,
+                              tmA, tmB, tmBt, tmD, p);
         case B2G_TILE_256x128_2SM:
-            grid = 2 * (p.csplit ? p.num_units : std::min(p.num_units, max_pair_clusters(di, smem)));
-            if (plain)
-                return launch_exc(gemm_sm100_2cta<128, false, true>, grid, threads, smem, s, 2,
-                                  tmA, tmB, tmBt, tmD, p);
-            return launch_exc(gemm_sm100_2cta<128, PEERS>, grid, threads, smem, s,
-                              p.csplit ? 2 * p.splits : 2, tmA, tmB, tmBt, tmD, p);
+            grid = grid2;
+            return launch_exc(gemm_sm100_2cta<128, PEERS, PLAIN, CS>, grid, threads, smem, s, cl2,
+                              tmA, tmB, tmBt, tmD, p);
         default:
-            grid = 2 * (p.csplit ? p.num_units : std::min(p.num_units, max_pair_clusters(di, smem)));
-            if (plain)
-                return launch_exc(gemm_sm100_2cta<256, false, true>, grid, threads, smem, s, 2,
-                                  tmA, tmB, tmBt, tmD, p);
-            return launch_exc(gemm_sm100_2cta<256, PEERS>, grid, threads, smem, s,
-                              p.csplit ? 2 * p.splits : 2, tmA, tmB, tmBt, tmD, p);
+            grid = grid2;
+            return launch_exc(gemm_sm100_2cta<256, PEERS, PLAIN, CS>, grid, threads, smem, s, cl2,
+                              tmA, tmB, tmBt, tmD, p);
     }
 }
 
 int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
                 const CUtensorMap& tmBt, const CUtensorMap& tmD, const GemmParams& p,
                 const DeviceInfo& di, size_t smem, cudaStream_t s, int epi_warps) {
-    const bool peers = p.peers.n > 0;
-    if (int rc = ensure_kernel_attrs(tile, di, peers)) return rc;
-    if (tile != B2G_TILE_SWAP_AB && !peers && plain_path(p, geom(tile).ctas))
-        if (int rc = ensure_kernel_attrs(tile, di, false, true)) return rc;
+    const int v = kernel_variant(p, geom(tile).ctas);
+    if (int rc = ensure_kernel_attrs(tile, di, v)) return rc;
     int grid = 0;
     const int threads = gemm_threads(epi_warps);
-    cudaError_t e = peers ? launch_gemm_t<true>(tile, tmA, tmB, tmBt, tmD, p, di, smem, s,
-                                                threads, grid)
-                          : launch_gemm_t<false>(tile, tmA, tmB, tmBt, tmD, p, di, smem, s,
-                                                 threads, grid);
+    cudaError_t e;
+    switch (v) {
+        case kVarPeers:
+            e = launch_gemm_t<kVarPeers>(tile, tmA, tmB, tmBt, tmD, p, di, smem, s, threads, grid);
+            break;
+        case kVarPlain:
+            e = launch_gemm_t<kVarPlain>(tile, tmA, tmB, tmBt, tmD, p, di, smem, s, threads, grid);
+            break;
+        case kVarCsplit:
+            e = launch_gemm_t<kVarCsplit>(tile, tmA, tmB, tmBt, tmD, p, di, smem, s, threads, grid);
+            break;
+        default:
+            e = launch_gemm_t<kVarGeneral>(tile, tmA, tmB, tmBt, tmD, p, di, smem, s, threads, grid);
+    }
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "GEMM launch (tile %d, grid %d, smem %zu): %s", tile, grid, smem,
@@ -916,7 +914,8 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
             const size_t req = own ? std::max(smem_needed(tile, st_own, epi_boxes, a_rows) + recv,
                                               (size_t)di.smem_per_sm / 2 + 1024)
                                    : smem;
-            if (int rc = ensure_kernel_attrs(tile, di, npeer > 0)) return rc;
+            if (int rc = ensure_kernel_attrs(tile, di, npeer > 0 ? kVarPeers : kVarCsplit))
+                return rc;
             if (cluster_fits(di, tile, splits * g.ctas, gemm_threads(8), req, npeer > 0)) {
                 p.csplit = 1;
                 p.recv_ring = own ? 0 : 1;

@@ -96,10 +96,17 @@ struct GemmParams {
     PeerCopies peers;
 };
 
-// k-blocks [kb0, kb1) of split s: an even share of the tile's num_kb k-blocks.
+// k-blocks [kb0, kb1) of split s: an even share of the tile's num_kb k-blocks (32-bit
+// arithmetic whenever splits x num_kb fits, as it does for any K below 2^22).
 __device__ __forceinline__ void split_range(const GemmParams& p, int s, int& kb0, int& kb1) {
-    kb0 = (int)((long long)s * p.num_kb / p.splits);
-    kb1 = (int)((long long)(s + 1) * p.num_kb / p.splits);
+    if (p.num_kb <= 0xffff && p.splits <= 0xffff) {
+        const uint32_t n = (uint32_t)p.num_kb, d = (uint32_t)p.splits;
+        kb0 = (int)((uint32_t)s * n / d);
+        kb1 = (int)((uint32_t)(s + 1) * n / d);
+    } else {
+        kb0 = (int)((long long)s * p.num_kb / p.splits);
+        kb1 = (int)((long long)(s + 1) * p.num_kb / p.splits);
+    }
 }
 
 constexpr int kBM = 128;      // rows of A per CTA (UMMA M for cta_group::1)
@@ -774,16 +781,17 @@ __device__ __forceinline__ void csplit_epilogue(const GemmParams& p, const EpiSc
 // PLAIN: the instantiation for the common case -- no split-K, FP32 accumulation, plain store,
 // no peers -- in which those modes are compile-time constants, so the code a launch runs is
 // only the plain path (fewer instruction-cache misses on its way, no integer divisions for
-// split ranges); the host launches it whenever p allows.
-template <int BN, bool PEERS = false, bool PLAIN = false>
+// split ranges); the host launches it whenever p allows. CSPLIT: likewise for split-K reduced
+// in a cluster (FP32 accumulation, no peers), the decode-shaped launches.
+template <int BN, bool PEERS = false, bool PLAIN = false, bool CSPLIT = false>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_1cta(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
-    static_assert(!(PEERS && PLAIN), "the plain path has no peers");
+    static_assert(!(PEERS && (PLAIN || CSPLIT)) && !(PLAIN && CSPLIT), "one variant at a time");
     using TT = TileTraits<BN>;
     const int splits = PLAIN ? 1 : p.splits;
-    const bool csplit = PLAIN ? false : p.csplit != 0;
+    const bool csplit = PLAIN ? false : CSPLIT ? true : p.csplit != 0;
     // k-blocks [kb0, kb1) of split s of a tile
     const auto krange = [&](int s, int& kb0, int& kb1) {
         if (PLAIN) {
@@ -1007,7 +1015,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const int c_first = (warp - 2) >> 2;  // first 64-column chunk of this warp
         const EpiScalars es = epi_scalars(p, epi_warps);
         const uint32_t stage0 = sEpi + (uint32_t)((warp - 2) * es.bufs) * kEpiBoxBytes;
-        const bool acc16 = PLAIN ? false : p.acc_f16 != 0, epi = PLAIN ? false : p.epilogue != 0;
+        const bool acc16 = (PLAIN || CSPLIT) ? false : p.acc_f16 != 0;
+        const bool epi = PLAIN ? false : p.epilogue != 0;
         uint32_t seq = 0;
         int it = 0;
         for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {

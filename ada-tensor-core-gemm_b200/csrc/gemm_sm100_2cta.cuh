@@ -103,16 +103,17 @@ __device__ __forceinline__ void pair_unit(const GemmParams& p, int u, int& t, in
 
 // PEERS: the fused all-gather instantiation (every staged box of D also goes to p.peers).
 // PLAIN: the instantiation for the common case -- no split-K, FP32 accumulation, plain store,
-// B stored N x K, no peers -- with those modes as compile-time constants (see gemm_sm100_1cta).
-template <int BNP, bool PEERS = false, bool PLAIN = false>
+// B stored N x K, no peers -- with those modes as compile-time constants; CSPLIT: split-K
+// reduced in a cluster, FP32 accumulation, no peers (see gemm_sm100_1cta).
+template <int BNP, bool PEERS = false, bool PLAIN = false, bool CSPLIT = false>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_2cta(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmBt,
                     const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
-    static_assert(!(PEERS && PLAIN), "the plain path has no peers");
+    static_assert(!(PEERS && (PLAIN || CSPLIT)) && !(PLAIN && CSPLIT), "one variant at a time");
     const int splits = PLAIN ? 1 : p.splits;
-    const bool csplit = PLAIN ? false : p.csplit != 0;
+    const bool csplit = PLAIN ? false : CSPLIT ? true : p.csplit != 0;
     const bool b_mn = PLAIN ? false : p.b_mn_major != 0;
     const bool b_kn3d = PLAIN ? false : p.b_kn3d != 0;
     // k-blocks [kb0, kb1) of split s of a tile
@@ -385,7 +386,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const int c_first = (warp - 2) >> 2;
         const EpiScalars es = epi_scalars(p, epi_warps);
         const uint32_t stage0 = sEpi + (uint32_t)((warp - 2) * es.bufs) * kEpiBoxBytes;
-        const bool acc16 = PLAIN ? false : p.acc_f16 != 0, epi = PLAIN ? false : p.epilogue != 0;
+        const bool acc16 = (PLAIN || CSPLIT) ? false : p.acc_f16 != 0;
+        const bool epi = PLAIN ? false : p.epilogue != 0;
         uint32_t seq = 0;
         int it = 0;
         for (int u = cluster_id; u < p.num_units; u += num_clusters, ++it) {
