@@ -296,15 +296,19 @@ bool pdl_enabled() {
 // Epilogue warps of a launch: 8 when K <= 1024 (at most 16 k-blocks per tile: the next
 // tile's mainloop is too short to hide a 4-warp epilogue, and D's writes dominate), else 4.
 // B2G_EPI_WARPS=4 or 8 in the environment forces one (read once per process).
-int epi_warps_for(int num_kb, int splits, bool wide) {
+int epi_warps_for(int num_kb, int splits, bool wide, bool one_unit_per_cta) {
     static const int forced = [] {
         const char* e = std::getenv("B2G_EPI_WARPS");
         return e ? std::atoi(e) : 0;
     }();
     if (forced == 4 || forced == 8) return forced;
     // split-K: the reduction wants 8 as well; 256 x 512 tiles: the MMA warp waits for the
-    // epilogue of half 1 at the start of every tile
-    return (num_kb <= 16 || splits > 1 || wide) ? 8 : 4;
+    // epilogue of half 1 at the start of every tile. A CTA with a single tile has no next
+    // mainloop for its epilogue to keep up with: 4 (measured on B200, device time: 512^3
+    // 5.05 -> 4.80 us, 1024^3 8.10 -> 7.81 us)
+    if (splits > 1 || wide) return 8;
+    if (one_unit_per_cta) return 4;
+    return num_kb <= 16 ? 8 : 4;
 }
 
 // The most recent GEMM launch of this host thread (b2g_last_launch, b2g_last_launch_cluster).
@@ -993,7 +997,9 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
     if (p.d_tma)
         if (int rc = make_tmap(&tmD, D, (uint64_t)N, (uint64_t)M, (uint64_t)ldd, 64, 32, "D"))
             return rc;
-    const int epi_warps = epi_warps_for(p.num_kb, p.splits, wide);
+    const int ctas_at_once = g.ctas == 2 ? 2 * max_pair_clusters(di, smem) : di.sm_count;
+    const int epi_warps = epi_warps_for(p.num_kb, p.splits, wide,
+                                        (long long)p.num_units * g.ctas <= ctas_at_once);
     p.epi_bufs = std::max(1, std::min(kMaxEpiBufs, epi_boxes / epi_warps));
     return launch_gemm(tile, tmA, tmB, tmBt, tmD, p, di, smem, s, epi_warps);
 }

@@ -79,12 +79,14 @@ def test_pair_tail_slices(cuda, shape):
                                   b2g.TILE_256x128_2SM])
 @pytest.mark.parametrize("K,warps", [(1024, 8), (1088, 4), (64, 8)])
 @pytest.mark.parametrize("mode", ["plain", "fused", "f16acc"])
-def test_epilogue_warps_by_k(cuda, tile, K, warps, mode):
+@pytest.mark.parametrize("MN", [(640, 704), (2560, 2304)])
+def test_epilogue_warps_by_k(cuda, tile, K, warps, mode, MN):
     """Without split-K, K <= 1024 launches 8 epilogue warps (two per TMEM lane quarter,
     alternate 64-column chunks, one staging box each) and longer K launches 4 (two boxes
-    each); both give the same result in every epilogue mode, including the 64-column tail
-    slices of the 2-CTA kernel."""
-    M, N = 640, 704
+    each), unless every CTA (pair) has a single tile, which takes 4 (no next mainloop to keep
+    up with); all give the same result in every epilogue mode, including the tail slices of
+    the 2-CTA kernel (640 x 704: one tile per CTA; 2560 x 2304: more tiles than CTAs)."""
+    M, N = MN
     A, B, bias = inputs(M, N, K, seed=21, lo=-0.5, hi=0.5)
     kw = {}
     if mode == "fused":
@@ -93,8 +95,11 @@ def test_epilogue_warps_by_k(cuda, tile, K, warps, mode):
         kw = dict(acc=b2g.ACC_F16)
     D = run(cuda, A, B, bias if mode == "fused" else None, tile=tile, splits=1, **kw)
     launch = b2g.last_launch()
+    ctas = 2 if tile in (b2g.TILE_256x256_2SM, b2g.TILE_256x512_2SM, b2g.TILE_256x128_2SM) else 1
     if tile == b2g.TILE_256x512_2SM:
         warps = 8  # always: the next tile's half-1 MMAs wait for this epilogue
+    elif launch["units"] * ctas <= launch["grid"]:
+        warps = 4  # one tile per CTA (pair)
     assert launch["threads"] == 64 + 32 * warps, launch
     assert launch["tile"] == tile
     rows = sample_rows(M, 96)
