@@ -42,7 +42,12 @@ EXPORTS = (
     "b2g_kernel_clock", "b2g_last_launch", "b2g_gemm_splitk", "b2g_gemm_splitk_noalloc",
     "b2g_gemm_multi", "b2g_allgather_rows", "b2g_gemm_multi_allgather", "b2g_gemm_peers",
     "b2g_ipc_handle", "b2g_ipc_open", "b2g_ipc_close", "b2g_last_launch_cluster",
+    "b2g_last_launch_variant",
 )
+
+
+# b2g_last_launch_variant values (B2G_VARIANT_*)
+VARIANT_NAMES = {0: "general", 1: "peers", 2: "plain", 3: "csplit"}
 
 
 class B2GError(RuntimeError):
@@ -111,6 +116,8 @@ def lib():
         L.b2g_last_launch.argtypes = [ip, ip, ip, ip, ip, ip]
         L.b2g_last_launch_cluster.restype = i
         L.b2g_last_launch_cluster.argtypes = [ip]
+        L.b2g_last_launch_variant.restype = i
+        L.b2g_last_launch_variant.argtypes = [ip]
         L.b2g_gemm_multi.restype = i
         L.b2g_gemm_multi.argtypes = [i, ip, vp, vp, vp, vp, i, i, i, ll, ll, ll, i, i, i, f, i,
                                      i, i, vp, i]
@@ -350,8 +357,9 @@ def config_info(tile: int = TILE_AUTO, stages: int = 0) -> dict:
 
 
 def last_launch() -> dict:
-    """Grid, threads, tile, stages, work units and split-K factor of this thread's most recent
-    GEMM launch."""
+    """Grid, threads, tile, stages, work units, split-K factor, cluster size and kernel
+    variant ("plain", "csplit", "peers" or "general") of this thread's most recent GEMM
+    launch."""
     vals = [C.c_int() for _ in range(6)]
     _check(lib().b2g_last_launch(*[C.byref(v) for v in vals]))
     keys = ("grid", "threads", "tile", "stages", "units", "splits")
@@ -359,6 +367,9 @@ def last_launch() -> dict:
     cl = C.c_int()
     _check(lib().b2g_last_launch_cluster(C.byref(cl)))
     out["cluster"] = cl.value  # CTAs per thread-block cluster (split-K clusters: the splits)
+    var = C.c_int()
+    _check(lib().b2g_last_launch_variant(C.byref(var)))
+    out["variant"] = VARIANT_NAMES.get(var.value, var.value)  # compiled form of the kernel
     return out
 
 

@@ -314,6 +314,7 @@ int epi_warps_for(int num_kb, int splits, bool wide, bool one_unit_per_cta) {
 // The most recent GEMM launch of this host thread (b2g_last_launch, b2g_last_launch_cluster).
 struct LaunchRecord {
     int grid, threads, tile, stages, units, splits, cluster;
+    int variant;  // KernelVariant of the tile kernels; the swapped-operand kernel: general
 };
 thread_local LaunchRecord g_last_launch = {};
 
@@ -462,7 +463,7 @@ int launch_gemm(int tile, const CUtensorMap& tmA, const CUtensorMap& tmB,
         return fail(B2G_ERR_CUDA, "GEMM launch (tile %d, grid %d, smem %zu): %s", tile, grid, smem,
                     cudaGetErrorString(e));
     const int cluster = (p.csplit ? p.splits : 1) * geom(tile).ctas;
-    g_last_launch = LaunchRecord{grid, threads, tile, p.stages, p.num_units, p.splits, cluster};
+    g_last_launch = LaunchRecord{grid, threads, tile, p.stages, p.num_units, p.splits, cluster, v};
     return B2G_OK;
 }
 
@@ -528,7 +529,8 @@ int launch_swap(const void* A, const void* B, int M, int N, int K, long long lda
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "swap GEMM launch (MT %d, grid %d): %s", MT, grid,
                     cudaGetErrorString(e));
-    g_last_launch = LaunchRecord{grid, threads, B2G_TILE_SWAP_AB, p.stages, p.num_units, 1, 1};
+    g_last_launch =
+        LaunchRecord{grid, threads, B2G_TILE_SWAP_AB, p.stages, p.num_units, 1, 1, kVarGeneral};
     return B2G_OK;
 }
 
@@ -1119,6 +1121,14 @@ B2G_EXPORT int b2g_last_launch_cluster(int* cluster_ctas) {
     const LaunchRecord r = g_last_launch;
     if (r.grid == 0) return fail(B2G_ERR_ARG, "no GEMM kernel launched on this host thread yet");
     if (cluster_ctas) *cluster_ctas = r.cluster;
+    return B2G_OK;
+}
+
+B2G_EXPORT int b2g_last_launch_variant(int* variant) {
+    clear_error();
+    const LaunchRecord r = g_last_launch;
+    if (r.grid == 0) return fail(B2G_ERR_ARG, "no GEMM kernel launched on this host thread yet");
+    if (variant) *variant = r.variant;
     return B2G_OK;
 }
 

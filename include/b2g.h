@@ -251,6 +251,20 @@ int b2g_last_launch(int* grid, int* threads, int* tile, int* stages, int* units,
  * reference (its kernel uses no clusters). B2G_ERR_ARG before any launch on this thread. */
 int b2g_last_launch_cluster(int* cluster_ctas);
 
+/* Which compiled form of the tile kernel the same most recent launch ran:
+ * B2G_VARIANT_GENERAL (every mode a runtime branch: FP16 accumulation, fused epilogue,
+ * workspace split-K, K x N B on the pair kernel; also the swapped-operand kernel),
+ * B2G_VARIANT_PEERS (the fused all-gather of b2g_gemm_peers), B2G_VARIANT_PLAIN (no split-K,
+ * FP32 accumulation, plain store, no peers, compiled as constants) or B2G_VARIANT_CSPLIT
+ * (split-K summed in a cluster, FP32 accumulation, no peers). The choice follows from the
+ * arguments; the results do not depend on it. No counterpart in the reference (one kernel).
+ * B2G_ERR_ARG before any launch on this thread. */
+#define B2G_VARIANT_GENERAL 0
+#define B2G_VARIANT_PEERS 1
+#define B2G_VARIANT_PLAIN 2
+#define B2G_VARIANT_CSPLIT 3
+int b2g_last_launch_variant(int* variant);
+
 /* cuBLAS comparison column: exactly the reference's call (src/gemm_bench.cu:625-633):
  * cublasGemmEx(OP_T, OP_N, N, M, K, alpha, B, 16F, K, A, 16F, K, beta=0, D, 16F, N,
  * COMPUTE_32F, DEFAULT_TENSOR_OP) on `stream`, with tensor-op math mode

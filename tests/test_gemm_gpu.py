@@ -383,6 +383,34 @@ def test_auto_tile_choice(cuda, shape, tile, splits):
     assert frob <= FROB_F32 and maxrel <= ELEM_F32, (frob, maxrel)
 
 
+@pytest.mark.parametrize("shape,kw,variant", [
+    ((512, 512, 512), {}, "plain"),                                   # 1-CTA, no split
+    ((2048, 2048, 2048), {}, "plain"),                                # pair tiles
+    ((2048, 1536, 1024), dict(tile=b2g.TILE_256x512_2SM), "plain"),  # wide pair tiles
+    ((512, 512, 512), dict(acc=b2g.ACC_F16), "general"),
+    ((512, 512, 512), dict(epilogue=b2g.EPI_BIAS_RELU, alpha=0.5), "general"),
+    ((128, 4096, 4096), {}, "csplit"),                                # decode: split in a cluster
+    ((512, 4096, 4096), {}, "csplit"),                                # pairs split in a cluster
+    ((1024, 1024, 1024), dict(b_layout=b2g.B_KN, tile=b2g.TILE_256x256_2SM), "general"),
+    ((1024, 1024, 1024), dict(b_layout=b2g.B_KN, tile=b2g.TILE_128x128), "plain"),
+])
+def test_kernel_variant_by_mode(cuda, shape, kw, variant):
+    """Each tile kernel is compiled as a plain-path form (no split-K, FP32 accumulation, plain
+    store, no peers; the pair kernel's also N x K B only), a cluster split-K form and a general
+    one; the launch record names the form that ran, and each gives correct results."""
+    M, N, K = shape
+    A, B, bias = inputs(M, N, K, seed=81, lo=-0.5, hi=0.5)
+    b_layout = kw.get("b_layout", b2g.B_NK)
+    Bx = np.ascontiguousarray(B.T) if b_layout == b2g.B_KN else B
+    epi = kw.get("epilogue", b2g.EPI_NONE) != b2g.EPI_NONE
+    D = run(cuda, A, Bx, bias if epi else None, **kw)
+    launch = b2g.last_launch()
+    assert launch["variant"] == variant, launch
+    frob, _ = check_rows(A, Bx, D, sample_rows(M, 32), bias=bias if epi else None,
+                         alpha=kw.get("alpha", 1.0), epilogue=epi, b_layout=b_layout)
+    assert frob <= (FROB_F16 if kw.get("acc") == b2g.ACC_F16 else FROB_F32), frob
+
+
 @pytest.mark.parametrize("shape", [(2304, 4352, 320), (1024, 1536, 1000), (4096, 3000, 512),
                                    (520, 700, 128)])
 @pytest.mark.parametrize("b_layout", [b2g.B_NK, b2g.B_KN])
