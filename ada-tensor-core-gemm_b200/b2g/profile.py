@@ -254,7 +254,7 @@ def main(argv=None):
     p.add_argument("--seed", type=int, default=1)
     p.add_argument("--skip", type=int, default=3, help="warm-up launches of the kernel skipped")
     p.add_argument("--tag", default="run")
-    p.add_argument("--out-dir", default="gpurun_out")
+    p.add_argument("--out-dir", default="ncu_out")
     p.add_argument("--exe", default=DEFAULT_EXE)
     p.add_argument("--kernel", default=None, help="ncu -k filter (default regex:gemm_sm100)")
     p.add_argument("--kernel-base", default=None, choices=("function", "demangled", "mangled"),
