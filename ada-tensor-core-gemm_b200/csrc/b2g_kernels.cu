@@ -787,11 +787,17 @@ int gemm_impl(const void* A, const void* B, void* D, const void* bias, int M, in
                      b_layout == B2G_B_NK && csplit_enabled();
         tile = (N <= 128 || M <= 128 || (sparse_pairs && !pair_split)) ? B2G_TILE_128x128
                                                                       : B2G_TILE_256x256_2SM;
-        // Long K with at least ~4 waves of 256 x 512 pair tiles: the wide tile's quarter less
-        // L2 traffic per FLOP wins (measured on B200: 8192^3 1446 -> 1503, 16384^3 1253 ->
-        // 1310, 4096 x 32768 x 8192 1443 -> 1512 TFLOP/s; at K = 4096 it is ~3% slower).
+        // 256 x 512 pair tiles when every pair gets enough of them to amortise the half-1
+        // hand-over at each tile start: K >= 4096, >= 3.5 waves of wide tiles and >= 320
+        // k-blocks of wide tiles per pair; then the wide tile's quarter less L2 traffic per
+        // FLOP wins (measured on B200, device time: 8192^3 1446 -> 1503, 16384^3 1253 -> 1310,
+        // 4096 x 32768 x 8192 1443 -> 1512 TFLOP/s; 6144^3 374.8 -> 354.7 us, 8192 x 8192 x 4096
+        // 442.7 -> 427.0 us; 6144 x 6144 x 4096, 249 k-blocks per pair, 221.7 -> 253.2 us and
+        // 5120^3, 2.7 waves, 203.8 -> 219.4 us stay on 256 x 256 tiles).
         const long long wide_tiles = (long long)((M + 255) / 256) * ((N + 511) / 512);
-        if (tile == B2G_TILE_256x256_2SM && K >= 8192 && wide_tiles >= 2LL * di.sm_count)
+        const long long pairs = di.sm_count / 2;
+        if (tile == B2G_TILE_256x256_2SM && K >= 4096 && 2 * wide_tiles >= 7 * pairs &&
+            wide_tiles * ((K + 63) / 64) >= 320 * pairs)
             tile = B2G_TILE_256x512_2SM;
         // Tiny M with N wide enough that 128-column blocks alone give ~one CTA per SM (no
         // split-K needed): the swapped-operand kernel skips the 128-row tile's padding
