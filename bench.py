@@ -71,6 +71,8 @@ SWEEPS = {
     "decode": [(m, 4096, 4096) for m in (1, 8, 32, 128, 512, 2048, 4096)],
 }
 SWEEPS["all"] = SWEEPS["config4"] + SWEEPS["decode"]
+# extra shapes in the default bench line, each with its configs[3] / decode sweep seed
+BENCH_SHAPES = [((8192, 8192, 8192), 105), ((128, 4096, 4096), 103)]
 
 NVML_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                 0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
@@ -93,6 +95,8 @@ def parse():
                    help="target CPU time of the bounded cpu_baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--allgather", action="store_true")
+    p.add_argument("--no-shapes", action="store_true",
+                   help="leave out the 8192^3 and decode comparisons with cuBLAS")
     p.add_argument("--no-sharded", action="store_true",
                    help="skip the configs[4] strong-scaling object (`sharded`) of the bench line")
     p.add_argument("--sweep", choices=tuple(SWEEPS), default=None,
@@ -622,6 +626,21 @@ def run_ours(args):
         torch.cuda.empty_cache()
         sharded = sharded_leg(args, world, rank, dev, stream, sptr, barrier)
 
+    # the north star's other square (8192^3) and a decode shape, each against the reference's
+    # cuBLAS call in the same run (1 GPU only: the scaling runs keep their per-N time)
+    shapes = None
+    if world == 1 and not args.no_shapes:
+        side = torch.cuda.Stream(device=dev)  # graphs are captured on a non-default stream
+        shapes = []
+        with torch.cuda.stream(side):
+            for (M, N, K), seed in BENCH_SHAPES:
+                row, _, _ = shape_vs_cublas(M, N, K, seed, 50, 10, side)
+                shapes.append({k: row[k] for k in (
+                    "M", "N", "K", "seed", "ms", "tflops", "cublas_tflops", "ours_over_cublas",
+                    "maxrel_vs_cublas", "roofline", "hbm_gbs_algorithmic", "launch",
+                    "kernel_sm_mhz")})
+        torch.cuda.synchronize()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(hA.numpy().view(np.uint16), hB.numpy().view(np.uint16), N, K,
@@ -694,6 +713,7 @@ def run_ours(args):
                        "D; steps pipelined over 2 buffer sets on H2D / compute / D2H streams"},
         "gpu_launches": args.steps,
         "clocks": clocks,
+        "shapes_vs_cublas": shapes,
     }
     if cpu:
         out["cpu_baseline"] = cpu
@@ -881,102 +901,117 @@ def _time_graph(launch, n, stream, replays=5):
     return ms
 
 
-def sweep_ours(args):
-    """Per shape: our kernel and cuBLAS (device time of graph-replayed launches; the host-loop
-    times through the C-ABI beside it), roofline fraction against
-    min(measured tensor peak, AI x measured HBM bandwidth), HBM GB/s, max-rel vs cuBLAS, and
-    a blocked FP32 CPU GEMM on a bounded row sample (the cpu_baseline leg)."""
+def shape_vs_cublas(M, N, K, seed, steps, warmup, stream, tile=-1, stages=0, group=0):
+    """One GEMM shape, ours and the reference's cuBLAS call on the same inputs: device time per
+    launch from CUDA-graph replay (input sets rotated, together > 2 x L2), the host-loop time
+    through each C-ABI beside it, max-rel vs cuBLAS, roofline fraction against
+    min(measured tensor peak, AI x measured HBM bandwidth) and the algorithmic HBM GB/s.
+    Returns (row, hA, hB); `stream` must be a non-default stream (graphs are captured on it)."""
     import numpy as np
     import torch
 
     import b2g
 
+    sptr = stream.cuda_stream
+    peaks, _ = measured_peaks()
+    bw = peaks["hbm_gbs"]
+    ptc = peaks["bf16_tflops"]
+    ld = _ld8(K)
+    hA = np.zeros((M, ld), np.uint16)
+    hB = np.zeros((N, ld), np.uint16)
+    hA[:, :K] = b2g.fill_uniform(M * K, seed, 0, -1.0, 1.0).reshape(M, K)
+    hB[:, :K] = b2g.fill_uniform(N * K, seed, 1, -1.0, 1.0).reshape(N, K)
+    # rotating input sets whose total exceeds twice the L2 (at least 2 sets)
+    set_bytes = 2 * (M * ld + N * ld + M * N)
+    nbuf = max(2, min(4096, math.ceil(2 * L2_BYTES / set_bytes)))
+    dA0 = torch.from_numpy(hA.view(np.float16)).cuda()
+    dB0 = torch.from_numpy(hB.view(np.float16)).cuda()
+    sets = [(dA0.clone(), dB0.clone(), torch.empty((M, N), dtype=torch.float16,
+                                                   device="cuda")) for _ in range(nbuf)]
+    del dA0, dB0
+    flop = 2.0 * M * N * K
+    # every set at least once per timed run (a set comes round again only after sets
+    # totalling > 2 x L2 have been read), and about a second of GPU time at most
+    steps = max(5, min(steps, int(2e15 / max(flop, 1) / 1000) + 5), min(nbuf, 4096))
+    warm = max(3, min(warmup, steps))
+
+    def ours(i):
+        dA, dB, dD = sets[i % nbuf]
+        b2g.gemm_raw(dA.data_ptr(), dB.data_ptr(), dD.data_ptr(), None, M, N, K, ld, ld, N,
+                     b2g.B_NK, b2g.ACC_F32, b2g.EPI_NONE, 1.0, tile, stages, group, sptr)
+
+    # device time (graph replay) is the figure; the host loop through the C-ABI is kept
+    # beside it, since at decode sizes its host work per call can bound the loop
+    ms_loop = _time_launches(ours, steps, warm, stream)
+    ms = _time_graph(ours, min(steps, 1024), stream)
+    b2g.sync_status(sptr)
+    launch = b2g.last_launch()
+    kmhz, _ = b2g.kernel_clock()
+    # the reference's cuBLAS call takes lda = ldb = K: unpadded copies when K % 8 != 0
+    csets = sets if ld == K else [(a[:, :K].contiguous(), b[:, :K].contiguous(), d)
+                                  for a, b, d in sets]
+
+    def cub(i):
+        dA, dB, dD = csets[i % nbuf]
+        b2g.cublas_gemm(dA, dB, dD, sptr)
+
+    dRef = torch.empty((M, N), dtype=torch.float16, device="cuda")
+    b2g.cublas_gemm(csets[0][0], csets[0][1], dRef, sptr)
+    ours(0)
+    err = torch.zeros(1, dtype=torch.float32, device="cuda")
+    b2g.max_rel_diff(sets[0][2], dRef, err, sptr)
+    maxrel = float(err.item())
+    del dRef
+    cublas_ms_loop = _time_launches(cub, steps, warm, stream)
+    cublas_ms = _time_graph(cub, min(steps, 1024), stream)
+    del csets
+    alg_bytes = 2.0 * (M * K + N * K + M * N)
+    ai = flop / alg_bytes
+    roof = min(ptc, ai * bw / 1e3)  # TFLOP/s
+    tf = flop / (ms * 1e-3) / 1e12
+    ctf = flop / (cublas_ms * 1e-3) / 1e12 if cublas_ms else None
+    row = {
+        "M": M, "N": N, "K": K, "seed": seed, "ms": round(ms, 5), "tflops": round(tf, 2),
+        "cublas_tflops": round(ctf, 2) if ctf else None,
+        "ours_over_cublas": round(tf / ctf, 4) if ctf else None,
+        "timing": "device time per launch: CUDA-graph replay of the launches (both arms)",
+        "ms_api_loop": round(ms_loop, 5),
+        "cublas_ms_api_loop": round(cublas_ms_loop, 5),
+        "maxrel_vs_cublas": maxrel,
+        "roofline": {"bound": "tensor" if ai * bw / 1e3 >= ptc else "hbm",
+                     "ai_flop_per_byte": round(ai, 1), "peak_tflops": round(roof, 1),
+                     "frac": round(tf / roof, 4)},
+        "hbm_gbs_algorithmic": round(alg_bytes / (ms * 1e-3) / 1e9, 1),
+        "launch": launch, "kernel_sm_mhz": round(kmhz),
+        "l2": f"{nbuf} rotating input sets, {nbuf * set_bytes / 2**20:.0f} MiB > 2 x L2",
+    }
+    del sets
+    torch.cuda.empty_cache()
+    return row, hA, hB
+
+
+def sweep_ours(args):
+    """Per shape: our kernel and cuBLAS (shape_vs_cublas) and a blocked FP32 CPU GEMM on a
+    bounded row sample (the cpu_baseline leg)."""
+    import torch
+
     torch.cuda.set_device(0)
     stream = torch.cuda.Stream()  # CUDA graphs are captured on a non-default stream
     torch.cuda.set_stream(stream)
-    sptr = stream.cuda_stream
     peaks, peak_src = measured_peaks()
     bw = peaks["hbm_gbs"]
     ptc = peaks["bf16_tflops"]
     rows_out = []
     for idx, (M, N, K) in enumerate(SWEEPS[args.sweep]):
-        seed = 100 + idx
-        ld = _ld8(K)
-        hA = np.zeros((M, ld), np.uint16)
-        hB = np.zeros((N, ld), np.uint16)
-        hA[:, :K] = b2g.fill_uniform(M * K, seed, 0, -1.0, 1.0).reshape(M, K)
-        hB[:, :K] = b2g.fill_uniform(N * K, seed, 1, -1.0, 1.0).reshape(N, K)
-        # rotating input sets whose total exceeds twice the L2 (at least 2 sets)
-        set_bytes = 2 * (M * ld + N * ld + M * N)
-        nbuf = max(2, min(4096, math.ceil(2 * L2_BYTES / set_bytes)))
-        dA0 = torch.from_numpy(hA.view(np.float16)).cuda()
-        dB0 = torch.from_numpy(hB.view(np.float16)).cuda()
-        sets = [(dA0.clone(), dB0.clone(), torch.empty((M, N), dtype=torch.float16,
-                                                       device="cuda")) for _ in range(nbuf)]
-        del dA0, dB0
-        flop = 2.0 * M * N * K
-        # every set at least once per timed run (a set comes round again only after sets
-        # totalling > 2 x L2 have been read), and about a second of GPU time at most
-        steps = max(5, min(args.steps, int(2e15 / max(flop, 1) / 1000) + 5), min(nbuf, 4096))
-        warm = max(3, min(args.warmup, steps))
-
-        def ours(i):
-            dA, dB, dD = sets[i % nbuf]
-            b2g.gemm_raw(dA.data_ptr(), dB.data_ptr(), dD.data_ptr(), None, M, N, K, ld, ld, N,
-                         b2g.B_NK, b2g.ACC_F32, b2g.EPI_NONE, 1.0, args.tile, args.stages,
-                         args.group, sptr)
-
-        # device time (graph replay) is the figure; the host loop through the C-ABI is kept
-        # beside it, since at decode sizes its host work per call can bound the loop
-        ms_loop = _time_launches(ours, steps, warm, stream)
-        ms = _time_graph(ours, min(steps, 1024), stream)
-        b2g.sync_status(sptr)
-        launch = b2g.last_launch()
-        kmhz, _ = b2g.kernel_clock()
-        # the reference's cuBLAS call takes lda = ldb = K: unpadded copies when K % 8 != 0
-        csets = sets if ld == K else [(a[:, :K].contiguous(), b[:, :K].contiguous(), d)
-                                      for a, b, d in sets]
-
-        def cub(i):
-            dA, dB, dD = csets[i % nbuf]
-            b2g.cublas_gemm(dA, dB, dD, sptr)
-
-        dRef = torch.empty((M, N), dtype=torch.float16, device="cuda")
-        b2g.cublas_gemm(csets[0][0], csets[0][1], dRef, sptr)
-        ours(0)
-        err = torch.zeros(1, dtype=torch.float32, device="cuda")
-        b2g.max_rel_diff(sets[0][2], dRef, err, sptr)
-        maxrel = float(err.item())
-        del dRef
-        cublas_ms_loop = _time_launches(cub, steps, warm, stream)
-        cublas_ms = _time_graph(cub, min(steps, 1024), stream)
-        del csets
-        alg_bytes = 2.0 * (M * K + N * K + M * N)
-        ai = flop / alg_bytes
-        roof = min(ptc, ai * bw / 1e3)  # TFLOP/s
-        tf = flop / (ms * 1e-3) / 1e12
-        row = {
-            "M": M, "N": N, "K": K, "seed": seed, "ms": round(ms, 5), "tflops": round(tf, 2),
-            "cublas_tflops": round(flop / (cublas_ms * 1e-3) / 1e12, 2) if cublas_ms else None,
-            "timing": "device time per launch: CUDA-graph replay of the launches (both arms)",
-            "ms_api_loop": round(ms_loop, 5),
-            "cublas_ms_api_loop": round(cublas_ms_loop, 5),
-            "maxrel_vs_cublas": maxrel,
-            "roofline": {"bound": "tensor" if ai * bw / 1e3 >= ptc else "hbm",
-                         "ai_flop_per_byte": round(ai, 1), "peak_tflops": round(roof, 1),
-                         "frac": round(tf / roof, 4)},
-            "hbm_gbs_algorithmic": round(alg_bytes / (ms * 1e-3) / 1e9, 1),
-            "launch": launch, "kernel_sm_mhz": round(kmhz),
-            "l2": f"{nbuf} rotating input sets, {nbuf * set_bytes / 2**20:.0f} MiB > 2 x L2",
-        }
+        row, hA, hB = shape_vs_cublas(M, N, K, 100 + idx, args.steps, args.warmup, stream,
+                                      args.tile, args.stages, args.group)
         if not args.no_cpu_baseline:
             row["cpu_baseline"] = cpu_baseline(hA[:, :K].copy(), hB[:, :K].copy(), N, K,
                                                min(args.cpu_seconds, 2.0),
                                                {"M": M})
         print(json.dumps(row), flush=True)
         rows_out.append(row)
-        del sets
-        torch.cuda.empty_cache()
+        del hA, hB
     print(f"\n| M | N | K | ours TFLOP/s | cuBLAS | ours/cuBLAS | bound | frac of roofline "
           f"({peak_src} {ptc:.0f} TF/s, {bw:.0f} GB/s) | HBM GB/s | us ours / cuBLAS (host "
           f"loop) | CPU FP32 TFLOP/s |")
