@@ -47,7 +47,7 @@ EXPORTS = (
 
 
 # b2g_last_launch_variant values (B2G_VARIANT_*)
-VARIANT_NAMES = {0: "general", 1: "peers", 2: "plain", 3: "csplit"}
+VARIANT_NAMES = {0: "general", 1: "peers", 2: "plain", 3: "csplit", 4: "narrow"}
 
 
 class B2GError(RuntimeError):
@@ -358,7 +358,7 @@ def config_info(tile: int = TILE_AUTO, stages: int = 0) -> dict:
 
 def last_launch() -> dict:
     """Grid, threads, tile, stages, work units, split-K factor, cluster size and kernel
-    variant ("plain", "csplit", "peers" or "general") of this thread's most recent GEMM
+    variant ("plain", "csplit", "peers", "narrow" or "general") of this thread's most recent GEMM
     launch."""
     vals = [C.c_int() for _ in range(6)]
     _check(lib().b2g_last_launch(*[C.byref(v) for v in vals]))

@@ -92,6 +92,28 @@ int make_tmap_kn3d(CUtensorMap* tm, const void* ptr, uint64_t N, uint64_t K, uin
 
 // One 3D load per stage for B stored K x N (default; B2G_KN3D=0 in the environment, read
 // once per process, keeps the per-64-column 2D loads).
+// 3D map over a row-major rows x K matrix (K % 64 == 0) whose box brings `kbs` consecutive
+// k-blocks of `box_rows` rows in one load: dims (64, rows, K / 64), strides (ld x 2, 128 B);
+// the k-blocks land back to back, box_rows x 128 B each. Rows past `rows` and k-blocks past
+// K are zero-filled.
+int make_tmap_kblocks(CUtensorMap* tm, const void* ptr, uint64_t rows, uint64_t K, uint64_t ld,
+                      uint32_t box_rows, uint32_t kbs, const char* what) {
+    auto enc = encode_fn();
+    if (!enc) return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const cuuint64_t dims[3] = {64, rows, K / 64};
+    const cuuint64_t strides[2] = {ld * 2, 128};
+    const cuuint32_t box[3] = {64, box_rows, kbs};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(ptr), dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(B2G_ERR_CUDA, "cuTensorMapEncodeTiled(%s in k-block boxes, %llu x %llu, box %u x %u): %d",
+                    what, (unsigned long long)rows, (unsigned long long)K, box_rows, kbs, (int)r);
+    return B2G_OK;
+}
+
 bool kn3d_enabled() {
     static const bool on = [] {
         const char* e = std::getenv("B2G_KN3D");
@@ -128,7 +150,7 @@ TileGeom geom(int tile) {
 // plain path (no split-K, FP32 accumulation, plain store, no peers; the pair kernel's also
 // N x K B only) or split-K reduced in a cluster (FP32 accumulation, no peers); see
 // gemm_sm100_1cta. The swapped-operand kernel has one instantiation.
-enum KernelVariant { kVarGeneral = 0, kVarPeers = 1, kVarPlain = 2, kVarCsplit = 3 };
+enum KernelVariant { kVarGeneral = 0, kVarPeers = 1, kVarPlain = 2, kVarCsplit = 3, kVarNarrow = 4 };
 
 #define B2G_VARIANTS_1CTA(BN)                                                        \
     (v == kVarPeers    ? (const void*)gemm_sm100_1cta<BN, true>                      \
@@ -476,61 +498,116 @@ int swap_mt_for(int M, int N, int sm_count) {
     const int n_tiles = (N + 127) / 128;
     const int target = std::max(1, sm_count / std::max(1, n_tiles));
     const int rows = (M + target - 1) / target;
-    return rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+    const int mt = rows <= 16 ? 16 : rows <= 32 ? 32 : 64;
+    // launch_swap takes the narrow form when the 128-row blocks would leave more than half of
+    // the SMs idle; it spreads N over the SMs itself, so it wants M in as few blocks as
+    // possible (each M block re-reads all of B)
+    if (2LL * ((M + mt - 1) / mt) * n_tiles < sm_count) return M <= 16 ? 16 : M <= 32 ? 32 : 64;
+    return mt;
 }
 
 template <int MT>
 int launch_swap(const void* A, const void* B, int M, int N, int K, long long lda, long long ldb,
                 GemmParams& p, int stages, const DeviceInfo& di, cudaStream_t s) {
     using ST = SwapTraits<MT>;
-    static bool done[kMaxDevices] = {};
+    // The narrow form when 128-row blocks of B would leave more than half of the SMs idle:
+    // ~N / (SMs per M-block) rows of B per CTA (8..64), so every SM streams its share of B
+    // over the whole K range (measured on B200, N = K = 4096, device time, against the
+    // 128-row form: M = 1 16.6 -> 12.0 us, M = 32 17.0 -> 13.4 us; the automatic choice there,
+    // 128 x 128 tiles with cluster split-K, takes 11.6-11.7 us).
+    const int tiles_m = (M + MT - 1) / MT;
+    const bool narrow = 2LL * tiles_m * ((N + 127) / 128) < di.sm_count;
+    int rb = 128, kbs = 1;
+    uint32_t slot_b = ST::kBStageBytes, slot_a = ST::kAStageBytes;
+    // A box rows: all of M in one block -> only round_up(M, 8) rows are loaded; the MMA reads
+    // MT rows, the rows past the box feeding only D^T columns >= M, which are never stored
+    int a_rows = MT;
+    // K % 64 == 0: one 3D load per operand and stage, with rows in multiples of 8 so every
+    // k-block's slot starts on a 1 KiB swizzle atom (else one 2D load per k-block and operand)
+    const bool three_d = narrow && K % 64 == 0;
+    if (narrow) {
+        const int per_m = std::max(1, di.sm_count / tiles_m);
+        const int step = three_d ? 8 : 4;
+        rb = (N + per_m - 1) / per_m;
+        rb = std::min(64, std::max(8, (rb + step - 1) / step * step));
+        slot_b = (uint32_t)((rb * kBK * 2 + 1023) / 1024 * 1024);
+        if (tiles_m == 1) a_rows = std::min(MT, (M + 7) / 8 * 8);
+        if (three_d) slot_a = (uint32_t)a_rows * kBK * 2;
+        // stages of ~32 KiB (a box's third dimension is at most 256 k-blocks)
+        kbs = std::min(256, std::max(1, (int)(32768u / (slot_b + slot_a))));
+    }
+    const auto smem_for = [&](int st) {
+        return narrow ? gemm_swapn_smem_bytes<MT>(st, kbs, slot_b, slot_a)
+                      : gemm_swap_smem_bytes<MT>(st);
+    };
+    static bool done[2][kMaxDevices] = {};
     static std::mutex mu;
-    const void* kern = (const void*)gemm_sm100_swap<MT>;
+    const void* kern = narrow ? (const void*)gemm_sm100_swap<MT, true>
+                              : (const void*)gemm_sm100_swap<MT, false>;
     {
         std::lock_guard<std::mutex> lock(mu);
-        if (!(di.device < kMaxDevices && done[di.device])) {
+        if (!(di.device < kMaxDevices && done[narrow][di.device])) {
             cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  di.smem_optin);
             if (e != cudaSuccess)
                 return fail(B2G_ERR_CUDA, "cudaFuncSetAttribute(swap kernel): %s",
                             cudaGetErrorString(e));
-            if (di.device < kMaxDevices) done[di.device] = true;
+            if (di.device < kMaxDevices) done[narrow][di.device] = true;
         }
     }
     if (stages == 0) {
         stages = kMaxStages;
-        while (stages > 2 && gemm_swap_smem_bytes<MT>(stages) > (size_t)di.smem_optin) --stages;
+        while (stages > 2 && smem_for(stages) > (size_t)di.smem_optin) --stages;
     }
-    if (gemm_swap_smem_bytes<MT>(stages) > (size_t)di.smem_optin)
+    if (smem_for(stages) > (size_t)di.smem_optin)
         return fail(B2G_ERR_SMEM, "smem over per-block opt-in limit (swap kernel, %d stages)",
                     stages);
-    const size_t smem =
-        std::max(gemm_swap_smem_bytes<MT>(stages), (size_t)di.smem_per_sm / 2 + 1024);
+    const size_t smem = std::max(smem_for(stages), (size_t)di.smem_per_sm / 2 + 1024);
     p.stages = stages;
-    p.tiles_m = (M + MT - 1) / MT;
-    p.tiles_n = (N + 127) / 128;
+    p.tiles_m = tiles_m;
+    p.tiles_n = (N + rb - 1) / rb;
     const long long nt = (long long)p.tiles_m * p.tiles_n;
     if (nt > 0x7fffffffLL) return fail(B2G_ERR_ARG, "too many tiles (%lld)", nt);
     p.num_tiles = p.num_units = p.dp_tiles = (int)nt;
     p.tail_split = 1;
     p.splits = 1;
     p.idesc = p.idesc_tail = idesc_f16(128, MT, p.acc_f16 == 0, false);
-    p.stage_tx = ST::kStageBytes;
+    // bytes one k-block's two boxes deliver
+    p.stage_tx = (uint32_t)(rb + a_rows) * kBK * 2;
+    p.swap_rb = rb;
+    p.swap_kbs = kbs;
+    p.swap_3d = three_d ? 1 : 0;
+    p.swap_slot_b = slot_b;
+    p.swap_slot_a = slot_a;
     if (p.group <= 0) p.group = 1;
     CUtensorMap tmA, tmB;
-    if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK, MT, "A"))
-        return rc;
-    if (int rc = make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK, 128, "B"))
-        return rc;
+    if (three_d) {
+        if (int rc = make_tmap_kblocks(&tmA, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda,
+                                       (uint32_t)a_rows, (uint32_t)kbs, "A"))
+            return rc;
+        if (int rc = make_tmap_kblocks(&tmB, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb,
+                                       (uint32_t)rb, (uint32_t)kbs, "B"))
+            return rc;
+    } else {
+        if (int rc = make_tmap(&tmA, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, kBK,
+                               (uint32_t)a_rows, "A"))
+            return rc;
+        if (int rc = make_tmap(&tmB, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, kBK,
+                               (uint32_t)rb, "B"))
+            return rc;
+    }
     const int grid = std::min(p.num_units, di.sm_count);
     const int threads = gemm_threads(4);
-    cudaError_t e = launch_ex(gemm_sm100_swap<MT>, grid, threads, smem, s, tmA, tmB, p);
+    cudaError_t e = narrow ? launch_ex(gemm_sm100_swap<MT, true>, grid, threads, smem, s, tmA,
+                                       tmB, p)
+                           : launch_ex(gemm_sm100_swap<MT, false>, grid, threads, smem, s, tmA,
+                                       tmB, p);
     if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess)
         return fail(B2G_ERR_CUDA, "swap GEMM launch (MT %d, grid %d): %s", MT, grid,
                     cudaGetErrorString(e));
-    g_last_launch =
-        LaunchRecord{grid, threads, B2G_TILE_SWAP_AB, p.stages, p.num_units, 1, 1, kVarGeneral};
+    g_last_launch = LaunchRecord{grid, threads, B2G_TILE_SWAP_AB, p.stages, p.num_units, 1, 1,
+                                 narrow ? kVarNarrow : kVarGeneral};
     return B2G_OK;
 }
 

@@ -94,6 +94,15 @@ struct GemmParams {
     // same rows and columns of npeer other copies of D (same ldd; peer devices' memory over
     // NVLink). The host guarantees N % 8 == 0, ldd % 8 == 0 and 16-byte aligned copies.
     PeerCopies peers;
+    // Swapped-operand kernel, narrow form (decode shapes that give the 128-row form too few
+    // CTAs): each CTA streams swap_rb (< 128) rows of B over the whole K range, swap_kbs
+    // k-blocks per ring stage, each k-block's rows in a slot of swap_slot_b bytes (1 KiB
+    // multiple). The UMMA still reads 128 rows: the rows past swap_rb come from whatever
+    // follows in shared memory and feed only accumulator lanes the epilogue never stores.
+    // swap_3d: K % 64 == 0 and rows in multiples of 8, so one 3D load per operand brings a
+    // stage's swap_kbs k-blocks (box 64 x rows x k-blocks; slots of rows x 128 B, back to back).
+    int swap_rb, swap_kbs, swap_3d;
+    uint32_t swap_slot_b, swap_slot_a;
 };
 
 // k-blocks [kb0, kb1) of split s: an even share of the tile's num_kb k-blocks (32-bit

@@ -14,6 +14,14 @@
 // row m0 + j of D, so each thread holds a column of the output block: it converts its MT
 // values (alpha, bias[n], ReLU, FP16) and stores them row by row -- for every m the 32 lanes
 // of a warp write 32 consecutive columns (64 contiguous bytes). No staging, no TMA store.
+//
+// With N = 4096 the 128-row blocks give only 32 CTAs. The narrow form (NARROW) takes ~N / SMs
+// rows of B per CTA instead (32 at N = 4096: 128 CTAs), several k-blocks per ring stage, and
+// streams every CTA's rows over the whole K range: all SMs read B at once and no split-K
+// reduction follows the mainloop. Each UMMA still reads 128 rows of its B slot, three
+// quarters of them unused at N = 4096, which keeps it behind the 128 x 128 tiles with
+// cluster split-K at decode shapes (M = 1: 12.0 vs 11.6 us); b2g_gemm therefore never picks
+// it on its own.
 #pragma once
 
 #include "gemm_sm100.cuh"
@@ -34,14 +42,25 @@ constexpr size_t gemm_swap_smem_bytes(int stages) {
     return 1024 + (size_t)stages * SwapTraits<MT>::kStageBytes + sizeof(SmemCtl);
 }
 
+// Narrow form: [align slack][SmemCtl, 1 KiB multiple][stages x kbs B slots][stages x kbs A
+// slots][room]. The UMMA of a B slot reads 128 rows (16 KiB) from the slot's start and that
+// of an A slot MT rows, so the allocation extends 16 KiB - slot_b + MT x 128 - slot_a past the
+// slots; the barriers lie before them, out of reach of those reads.
+constexpr uint32_t kSwapCtlBytes = (sizeof(SmemCtl) + 1023) / 1024 * 1024;
+template <int MT>
+constexpr size_t gemm_swapn_smem_bytes(int stages, int kbs, uint32_t slot_b, uint32_t slot_a) {
+    return 1024 + kSwapCtlBytes + (size_t)stages * kbs * (slot_b + slot_a) + (16384u - slot_b) +
+           (SwapTraits<MT>::kAStageBytes - slot_a);
+}
+
 // MT accumulator columns of TMEM lane (row) `lane` of this warp's quarter -> D[m0 + j][n].
-// The TMEM loads are warp-collective: every lane runs the loop, lanes with n >= N only skip
-// their stores.
+// The TMEM loads are warp-collective: every lane runs the loop, lanes with n >= N (or, in the
+// narrow form, lanes past the CTA's rows of B: `valid` false) only skip their stores.
 template <int MT, bool ACC16, bool EPI>
 __device__ __forceinline__ void swap_epilogue_t(const GemmParams& p, uint32_t trow, int m0,
-                                                int n) {
+                                                int n, bool valid) {
     const int M = p.M;
-    const bool in_n = n < p.N;  // not warp-uniform: only the stores are skipped
+    const bool in_n = valid && n < p.N;  // not warp-uniform: only the stores are skipped
     float badd = 0.f;
     if constexpr (EPI) badd = (p.bias != nullptr && in_n) ? __half2float(p.bias[n]) : 0.f;
     const float alpha = p.alpha;
@@ -66,7 +85,15 @@ __device__ __forceinline__ void swap_epilogue_t(const GemmParams& p, uint32_t tr
     }
 }
 
-template <int MT>
+// NARROW: the form for decode shapes whose 128-row blocks of B would leave most SMs idle.
+// Each CTA takes p.swap_rb (< 128) rows of B -- ~N / SMs, so the whole B streams through
+// every SM at once with no split-K and no cross-CTA reduction -- and a ring stage holds
+// p.swap_kbs k-blocks (small boxes, enough bytes in flight). The UMMA is the same 128 x MT x
+// 16: it reads 128 rows from the start of each B slot, the rows past swap_rb being whatever
+// follows in shared memory; they only feed accumulator lanes >= swap_rb, which no epilogue
+// lane stores. Per output element the k order is the 128-row form's, so results match it bit
+// for bit.
+template <int MT, bool NARROW = false>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     gemm_sm100_swap(const __grid_constant__ CUtensorMap tmA,
                     const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
@@ -75,10 +102,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
     extern __shared__ uint8_t smem_dyn[];
     const uint32_t raw = smem_u32(smem_dyn);
     const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
-    const uint32_t sB = raw + pad;                                // UMMA A operand: B rows
-    const uint32_t sA = sB + (uint32_t)p.stages * ST::kBStageBytes;  // UMMA B operand: A rows
-    SmemCtl* ctl =
-        reinterpret_cast<SmemCtl*>(smem_dyn + pad + (size_t)p.stages * ST::kStageBytes);
+    // k-block j of ring stage s lives in B slot and A slot s * kbs + j
+    const int kbs = NARROW ? p.swap_kbs : 1;
+    const int rb = NARROW ? p.swap_rb : 128;
+    const uint32_t slot_b = NARROW ? p.swap_slot_b : ST::kBStageBytes;
+    const uint32_t slot_a = NARROW ? p.swap_slot_a : ST::kAStageBytes;
+    const uint32_t nslots = (uint32_t)(p.stages * kbs);
+    const uint32_t sB = raw + pad + (NARROW ? kSwapCtlBytes : 0u);  // UMMA A operand: B rows
+    const uint32_t sA = sB + nslots * slot_b;                     // UMMA B operand: A rows
+    SmemCtl* ctl = reinterpret_cast<SmemCtl*>(
+        smem_dyn + pad + (NARROW ? 0 : (size_t)nslots * (slot_b + slot_a)));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t full0 = smem_u32(&ctl->full[0]);
@@ -129,16 +162,31 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
                 int tm, tn;
                 tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
-                const int m0 = tm * MT, n0 = tn * 128;
-                for (int kb = 0; kb < p.num_kb; ++kb) {
+                const int m0 = tm * MT, n0 = tn * rb;
+                for (int kb = 0; kb < p.num_kb; kb += kbs) {
                     if (!mbar_wait(empty0 + 8 * stage, phase ^ 1u, w)) {
                         ok = false;
                         break;
                     }
                     const uint32_t fb = full0 + 8 * stage;
-                    mbar_arrive_expect_tx(fb, p.stage_tx);
-                    tma_load_2d(sB + stage * ST::kBStageBytes, &tmB, fb, kb * kBK, n0);
-                    tma_load_2d(sA + stage * ST::kAStageBytes, &tmA, fb, kb * kBK, m0);
+                    // stage_tx: bytes of one k-block's two boxes
+                    if (NARROW && p.swap_3d) {
+                        // the whole stage in one box per operand (k-blocks past K zero-filled
+                        // but counted: a box always lands whole)
+                        const uint32_t slot = (uint32_t)(stage * kbs);
+                        mbar_arrive_expect_tx(fb, (uint32_t)kbs * p.stage_tx);
+                        tma_load_3d(sB + slot * slot_b, &tmB, fb, 0, n0, kb);
+                        tma_load_3d(sA + slot * slot_a, &tmA, fb, 0, m0, kb);
+                    } else {
+                        // the last stage may be short
+                        const int nk = NARROW ? min(kbs, p.num_kb - kb) : 1;
+                        mbar_arrive_expect_tx(fb, (uint32_t)nk * p.stage_tx);
+                        for (int j = 0; j < nk; ++j) {
+                            const uint32_t slot = (uint32_t)(stage * kbs + j);
+                            tma_load_2d(sB + slot * slot_b, &tmB, fb, (kb + j) * kBK, n0);
+                            tma_load_2d(sA + slot * slot_a, &tmA, fb, (kb + j) * kBK, m0);
+                        }
+                    }
                     ++issued;
                     if (++stage == p.stages) {
                         stage = 0;
@@ -166,7 +214,6 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const WaitCtx w{p.timeout_ns, abort_flag, kErrWaitMma};
         const uint64_t adesc0 = sdesc_sw128(sB, 16, 1024);  // 128 rows of B
         const uint64_t bdesc0 = sdesc_sw128(sA, 16, 1024);  // MT rows of A
-        constexpr uint32_t kAStep = ST::kBStageBytes >> 4, kBStep = ST::kAStageBytes >> 4;
         const uint32_t idesc = p.idesc;
         int stage = 0;
         uint32_t phase = 0;
@@ -181,18 +228,22 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             }
             tc_fence_after();
             const uint32_t d_tmem = tmem_base + (uint32_t)(buf * MT);
-            for (int kb = 0; kb < p.num_kb; ++kb) {
+            for (int kb = 0; kb < p.num_kb; kb += kbs) {
                 if (!mbar_wait_warp(full0 + 8 * stage, phase, w)) {
                     ok = false;
                     break;
                 }
-                const uint64_t ad = adesc0 + (uint64_t)((uint32_t)stage * kAStep);
-                const uint64_t bd = bdesc0 + (uint64_t)((uint32_t)stage * kBStep);
+                const int nk = NARROW ? min(kbs, p.num_kb - kb) : 1;
                 if (elect_one()) {
-                    mma_f16_ss<1>(d_tmem, ad, bd, idesc, kb > 0 ? 1u : 0u);
-                    mma_f16_ss<1>(d_tmem, ad + 2, bd + 2, idesc, 1u);
-                    mma_f16_ss<1>(d_tmem, ad + 4, bd + 4, idesc, 1u);
-                    mma_f16_ss<1>(d_tmem, ad + 6, bd + 6, idesc, 1u);
+                    for (int j = 0; j < nk; ++j) {
+                        const uint32_t slot = (uint32_t)(stage * kbs + j);
+                        const uint64_t ad = adesc0 + (uint64_t)((slot * slot_b) >> 4);
+                        const uint64_t bd = bdesc0 + (uint64_t)((slot * slot_a) >> 4);
+                        mma_f16_ss<1>(d_tmem, ad, bd, idesc, kb + j > 0 ? 1u : 0u);
+                        mma_f16_ss<1>(d_tmem, ad + 2, bd + 2, idesc, 1u);
+                        mma_f16_ss<1>(d_tmem, ad + 4, bd + 4, idesc, 1u);
+                        mma_f16_ss<1>(d_tmem, ad + 6, bd + 6, idesc, 1u);
+                    }
                     mma_commit(empty0 + 8 * stage);
                 }
                 __syncwarp();
@@ -225,17 +276,21 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             int tm, tn;
             tile_coord(t, p.tiles_m, p.tiles_n, p.group, tm, tn);
             const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * MT);
-            const int m0 = tm * MT, n = tn * 128 + q * 32 + lane;
-            if (acc16) {
-                if (epi)
-                    swap_epilogue_t<MT, true, true>(p, trow, m0, n);
-                else
-                    swap_epilogue_t<MT, true, false>(p, trow, m0, n);
-            } else {
-                if (epi)
-                    swap_epilogue_t<MT, false, true>(p, trow, m0, n);
-                else
-                    swap_epilogue_t<MT, false, false>(p, trow, m0, n);
+            const int m0 = tm * MT, n = tn * rb + q * 32 + lane;
+            // narrow form: quarters wholly past the CTA's rows of B have nothing to store
+            if (!NARROW || q * 32 < rb) {
+                const bool valid = !NARROW || q * 32 + lane < rb;
+                if (acc16) {
+                    if (epi)
+                        swap_epilogue_t<MT, true, true>(p, trow, m0, n, valid);
+                    else
+                        swap_epilogue_t<MT, true, false>(p, trow, m0, n, valid);
+                } else {
+                    if (epi)
+                        swap_epilogue_t<MT, false, true>(p, trow, m0, n, valid);
+                    else
+                        swap_epilogue_t<MT, false, false>(p, trow, m0, n, valid);
+                }
             }
             tc_fence_before();
             __syncwarp();

@@ -256,13 +256,16 @@ int b2g_last_launch_cluster(int* cluster_ctas);
  * workspace split-K, K x N B on the pair kernel; also the swapped-operand kernel),
  * B2G_VARIANT_PEERS (the fused all-gather of b2g_gemm_peers), B2G_VARIANT_PLAIN (no split-K,
  * FP32 accumulation, plain store, no peers, compiled as constants) or B2G_VARIANT_CSPLIT
- * (split-K summed in a cluster, FP32 accumulation, no peers). The choice follows from the
+ * (split-K summed in a cluster, FP32 accumulation, no peers), or B2G_VARIANT_NARROW (the
+ * swapped-operand kernel's narrow form: ~N / SMs rows of B per CTA over the whole K range,
+ * chosen when its 128-row blocks would leave more than half of the SMs idle). The choice follows from the
  * arguments; the results do not depend on it. No counterpart in the reference (one kernel).
  * B2G_ERR_ARG before any launch on this thread. */
 #define B2G_VARIANT_GENERAL 0
 #define B2G_VARIANT_PEERS 1
 #define B2G_VARIANT_PLAIN 2
 #define B2G_VARIANT_CSPLIT 3
+#define B2G_VARIANT_NARROW 4
 int b2g_last_launch_variant(int* variant);
 
 /* cuBLAS comparison column: exactly the reference's call (src/gemm_bench.cu:625-633):
