@@ -72,7 +72,8 @@ SWEEPS = {
 }
 SWEEPS["all"] = SWEEPS["config4"] + SWEEPS["decode"]
 # extra shapes in the default bench line, each with its configs[3] / decode sweep seed
-BENCH_SHAPES = [((8192, 8192, 8192), 105), ((128, 4096, 4096), 103)]
+# (the decode shape first: the 8192^3 GEMM runs the GPU at its power cap and lowers the clock)
+BENCH_SHAPES = [((128, 4096, 4096), 103), ((8192, 8192, 8192), 105)]
 
 NVML_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
                 0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
@@ -874,11 +875,8 @@ def _time_launches(launch, steps, warmup, stream):
     return e0.elapsed_time(e1) / steps
 
 
-def _time_graph(launch, n, stream, replays=5):
-    """Device time per launch: n launches (input set i % sets, as in _time_launches) captured
-    in one CUDA graph, replayed back to back. Unlike a host loop of C-ABI calls, whose ~6-12 us
-    of host work per call can exceed a small GEMM's device time, this times only the GPU.
-    Both arms of the sweep (ours and cuBLAS) are timed the same way."""
+def _capture(launch, n, stream):
+    """n launches (input set i % sets, as in _time_launches) captured in one CUDA graph."""
     import torch
 
     for i in range(3):
@@ -890,13 +888,28 @@ def _time_graph(launch, n, stream, replays=5):
             launch(i)
     g.replay()
     torch.cuda.synchronize()
+    return g
+
+
+def _replay_ms(g, n, stream, replays=5):
+    """Device ms per launch of `replays` back-to-back replays of a graph of n launches."""
+    import torch
+
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(replays):
         g.replay()
     e1.record(stream)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / (replays * n)
+    return e0.elapsed_time(e1) / (replays * n)
+
+
+def _time_graph(launch, n, stream, replays=5):
+    """Device time per launch: n launches captured in one CUDA graph, replayed back to back.
+    Unlike a host loop of C-ABI calls, whose ~6-12 us of host work per call can exceed a small
+    GEMM's device time, this times only the GPU."""
+    g = _capture(launch, n, stream)
+    ms = _replay_ms(g, n, stream, replays)
     del g
     return ms
 
@@ -943,7 +956,8 @@ def shape_vs_cublas(M, N, K, seed, steps, warmup, stream, tile=-1, stages=0, gro
     # device time (graph replay) is the figure; the host loop through the C-ABI is kept
     # beside it, since at decode sizes its host work per call can bound the loop
     ms_loop = _time_launches(ours, steps, warm, stream)
-    ms = _time_graph(ours, min(steps, 1024), stream)
+    n_graph = min(steps, 1024)
+    g_ours = _capture(ours, n_graph, stream)
     b2g.sync_status(sptr)
     launch = b2g.last_launch()
     kmhz, _ = b2g.kernel_clock()
@@ -963,8 +977,15 @@ def shape_vs_cublas(M, N, K, seed, steps, warmup, stream, tile=-1, stages=0, gro
     maxrel = float(err.item())
     del dRef
     cublas_ms_loop = _time_launches(cub, steps, warm, stream)
-    cublas_ms = _time_graph(cub, min(steps, 1024), stream)
-    del csets
+    g_cub = _capture(cub, n_graph, stream)
+    # the two arms' replays alternate, three rounds, best of each: the SM clock drifts under
+    # the 1 kW cap (e.g. after a power-heavy shape), and alternation gives both arms the same
+    ms, cublas_ms = float("inf"), float("inf")
+    for _ in range(3):
+        ms = min(ms, _replay_ms(g_ours, n_graph, stream))
+        cublas_ms = min(cublas_ms, _replay_ms(g_cub, n_graph, stream))
+    b2g.sync_status(sptr)
+    del g_ours, g_cub, csets
     alg_bytes = 2.0 * (M * K + N * K + M * N)
     ai = flop / alg_bytes
     roof = min(ptc, ai * bw / 1e3)  # TFLOP/s
@@ -974,7 +995,8 @@ def shape_vs_cublas(M, N, K, seed, steps, warmup, stream, tile=-1, stages=0, gro
         "M": M, "N": N, "K": K, "seed": seed, "ms": round(ms, 5), "tflops": round(tf, 2),
         "cublas_tflops": round(ctf, 2) if ctf else None,
         "ours_over_cublas": round(tf / ctf, 4) if ctf else None,
-        "timing": "device time per launch: CUDA-graph replay of the launches (both arms)",
+        "timing": "device time per launch: CUDA-graph replay of the launches, the two arms' "
+                  "replays alternating, best of 3 each",
         "ms_api_loop": round(ms_loop, 5),
         "cublas_ms_api_loop": round(cublas_ms_loop, 5),
         "maxrel_vs_cublas": maxrel,
