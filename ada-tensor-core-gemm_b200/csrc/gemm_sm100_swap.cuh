@@ -18,10 +18,8 @@
 // With N = 4096 the 128-row blocks give only 32 CTAs. The narrow form (NARROW) takes ~N / SMs
 // rows of B per CTA instead (32 at N = 4096: 128 CTAs), several k-blocks per ring stage, and
 // streams every CTA's rows over the whole K range: all SMs read B at once and no split-K
-// reduction follows the mainloop. Each UMMA still reads 128 rows of its B slot, three
-// quarters of them unused at N = 4096, which keeps it behind the 128 x 128 tiles with
-// cluster split-K at decode shapes (M = 1: 12.0 vs 11.6 us); b2g_gemm therefore never picks
-// it on its own.
+// reduction follows the mainloop. Measured at decode shapes it stays behind the 128 x 128
+// tiles with cluster split-K (M = 1: 12.0 vs 11.6 us), so b2g_gemm never picks it on its own.
 #pragma once
 
 #include "gemm_sm100.cuh"
