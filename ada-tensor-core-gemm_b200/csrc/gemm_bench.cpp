@@ -172,6 +172,7 @@ void usage(const char* argv0) {
            "       3 = 128x64x64   1 CTA, UMMA 128x64, TMEM 2x64 cols\n"
            "       4 = 256x512x64  2-CTA pair, two UMMA 256x256 halves, TMEM 512 cols\n"
            "       5 = swapAB      small M: UMMA 128 x MT (MT = 16..64 rows of A), B rows on M\n"
+           "                       (narrow form, ~N/SMs rows of B per CTA, when N is small)\n"
            "       6 = 256x128x64  2-CTA pair, UMMA 256x128\n"
            "  --splits S split-K factor (0 automatic, 1 none, S >= 2 forced; default: automatic)\n"
            "  --gpus N   M-row panels over devices 0..N-1 (b2g_gemm_multi), B on every device;\n"
